@@ -1,0 +1,178 @@
+// Internal declarations shared by the shlo_cuda translation units.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <atomic>
+#include <cstdint>
+#include <cstring>
+#include <map>
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/shlo_cuda.h"
+
+namespace shlo {
+
+constexpr int kMaxRank = SHLO_MAX_RANK;
+
+// ---- dtypes (mlx-c codes, StablehloMlx/Mlx.lean:30-37) ----
+enum DType : uint8_t {
+  kBool = 0, kU8 = 1, kU16 = 2, kU32 = 3, kU64 = 4,
+  kI8 = 5, kI16 = 6, kI32 = 7, kI64 = 8, kF16 = 9, kF32 = 10, kNumDTypes = 11
+};
+bool dtype_valid(int dt);
+size_t dtype_size(int dt);
+const char *dtype_name(int dt);
+bool dtype_is_float(int dt);
+bool dtype_is_signed_int(int dt);
+bool dtype_is_unsigned_int(int dt);
+int promote_types(int a, int b);
+
+// ---- errors ----
+// Record an error message for this host thread and return 1.
+int fail(const char *fmt, ...);
+// Check a CUDA call; on error record it and return 1.
+int cuda_check(cudaError_t e, const char *what);
+#define SHLO_CUDA(call)                                \
+  do {                                                 \
+    if (::shlo::cuda_check((call), #call)) return 1;   \
+  } while (0)
+#define SHLO_TRY(call)                                 \
+  do {                                                 \
+    if ((call) != 0) return 1;                         \
+  } while (0)
+
+// ---- per-device state ----
+struct Device {
+  int id = 0;
+  int sm_count = 0;
+  cudaStream_t stream = nullptr;  // all compute
+  cudaStream_t copy = nullptr;    // host<->device copies of shlo_of_bytes
+  cudaEvent_t copy_done = nullptr;
+  std::mutex mu;                  // allocator
+  std::multimap<size_t, void *> free_blocks;
+  size_t pooled_bytes = 0;
+  bool capturing = false;         // a graph capture is in progress on `stream`
+  std::vector<void *> *capture_allocs = nullptr;  // blocks owned by the graph being captured
+};
+// The device current on this host thread, initialised on first use.
+int current_device(Device **out);
+int device_by_id(int id, Device **out);
+int current_flavor();
+
+// ---- storage ----
+struct Buffer {
+  std::atomic<int> rc{1};
+  Device *dev = nullptr;
+  void *ptr = nullptr;
+  size_t bytes = 0;
+  bool graph_owned = false;  // belongs to a captured graph; never pooled while the graph lives
+  // Derived layouts (e.g. the packed operand of mul_mat), keyed by how they
+  // were derived. Storage is immutable once written, so they stay valid for
+  // the buffer's lifetime.
+  std::mutex derived_mu;
+  std::map<std::string, Buffer *> derived;
+};
+int buffer_alloc(Device *dev, size_t bytes, Buffer **out);
+void buffer_retain(Buffer *b);
+void buffer_release(Buffer *b);
+
+}  // namespace shlo
+
+// The array handle (opaque in the C ABI).
+struct shlo_arr_s {
+  std::atomic<int> rc{1};
+  uint8_t dtype = shlo::kF32;
+  int ndim = 0;
+  int64_t shape[shlo::kMaxRank] = {0};
+  int64_t strides[shlo::kMaxRank] = {0};  // in elements
+  int64_t offset = 0;                     // in elements
+  shlo::Buffer *buf = nullptr;            // nullptr for the empty array
+  // Host copy of small arrays made by shlo_of_bytes (row-major): the kernel
+  // parameter words are read from here without a device round trip.
+  std::vector<uint8_t> host;
+  bool has_host = false;
+};
+
+namespace shlo {
+
+using Arr = shlo_arr_s;
+
+int64_t numel(const Arr *a);
+bool is_row_contiguous(const Arr *a);
+void set_row_major(Arr *a);
+// A new array of `shape` with fresh row-major storage on device `dev`.
+int new_array(Device *dev, uint8_t dtype, const int64_t *shape, int ndim, Arr **out);
+// A new handle sharing `src`'s storage (the caller sets shape/strides/offset).
+Arr *new_view(const Arr *src);
+int arr_device(const Arr *a, Device **out);
+// A row-contiguous version of `a` (a new reference to `a` itself when it already is).
+int make_contiguous(Arr *a, Arr **out);
+// Element pointer of the array's first element.
+inline char *data_ptr(const Arr *a) {
+  return a->buf ? static_cast<char *>(a->buf->ptr) + a->offset * (int64_t)dtype_size(a->dtype) : nullptr;
+}
+// Read `n` 32-bit words of a small array (host copy, or a synchronous readback).
+int read_words(Arr *a, uint32_t *words, int n);
+
+// ---- strided iteration descriptors passed by value to kernels ----
+struct StridedDesc {
+  int ndim;
+  int64_t shape[kMaxRank];
+  int64_t strides[kMaxRank];  // per operand, set by the op
+};
+
+// Copy `src` (any strides) into the contiguous buffer `dst` (same dtype).
+int launch_copy_strided(Device *dev, const Arr *src, void *dst);
+// Broadcast `a` to `shape` (stride-0 view) -- no copy.
+int broadcast_view(Arr *a, const int64_t *shape, int ndim, Arr **out);
+// numpy broadcast of two shapes.
+int broadcast_shapes(const int64_t *a, int na, const int64_t *b, int nb, int64_t *out, int *nout);
+int cast_array(Arr *a, uint8_t dtype, Arr **out);
+
+// Kernel launch size helper: a grid-stride launch over n elements.
+inline unsigned grid_for(int64_t n, int threads, Device *dev, int per_sm = 8) {
+  int64_t blocks = (n + threads - 1) / threads;
+  int64_t cap = (int64_t)dev->sm_count * per_sm;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return (unsigned)blocks;
+}
+
+inline float bitsf_host(uint32_t u) {
+  float f;
+  memcpy(&f, &u, 4);
+  return f;
+}
+
+// Launch-error check after a kernel launch.
+int launch_check(const char *what);
+
+// ---- ggml kernels (ggml_kernels.cu) ----
+int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out);
+int k_soft_max(Device *dev, Arr *x, const uint32_t *p, Arr **out);
+int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out);
+int k_silu(Device *dev, Arr *x, const uint32_t *p, Arr **out);
+int k_gelu_erf(Device *dev, Arr *x, const uint32_t *p, Arr **out);
+int k_erff_map(Device *dev, const uint32_t *p, Arr **out);
+int k_divide(Device *dev, Arr *a, Arr *b, const uint32_t *p, Arr **out);
+int k_sqrt(Device *dev, Arr *a, const uint32_t *p, Arr **out);
+int k_f64_ew(Device *dev, Arr *a, Arr *b, const uint32_t *p, Arr **out);
+int k_f64_of_f32(Device *dev, Arr *a, const uint32_t *p, Arr **out);
+int k_f32_of_f64(Device *dev, Arr *a, const uint32_t *p, Arr **out);
+
+// ---- built-ins (elementwise.cu) ----
+int op_unary(uint32_t op, Arr *a, Arr **out);
+int op_binary(uint32_t op, Arr *a, Arr *b, Arr **out);
+int op_where(Arr *c, Arr *a, Arr *b, Arr **out);
+int op_astype(Arr *a, uint8_t dt, Arr **out);
+int op_max_axis(Arr *a, int axis, Arr **out);
+int op_count_nonzero(Arr *a, uint64_t *count);
+int op_take(Arr *a, Arr *idx, int axis, Arr **out);
+int op_concat(Arr *const *xs, int n, int axis, Arr **out);
+
+}  // namespace shlo

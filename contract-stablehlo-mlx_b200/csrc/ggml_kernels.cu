@@ -1,0 +1,998 @@
+// The exact kernels: ggml-cpu's arm64 arithmetic, bit for bit, on sm_100a.
+//
+// Each kernel reproduces the reference's Lean kernel spec
+// (StablehloMlx/Kernels/Shaders.lean) with the parameter words of
+// StablehloMlx/Kernels/Run.lean:62-104. Built with -fmad=false: every fused
+// multiply-add below is an explicit __fmaf_rn where ggml uses vfmaq_f32, and
+// every other product and sum is rounded on its own.
+#include <cmath>
+
+#include "common.cuh"
+#include "erff_cr.cuh"
+
+namespace shlo {
+
+__device__ __forceinline__ uint32_t fbits(float f) { return __float_as_uint(f); }
+__device__ __forceinline__ float bitsf(uint32_t u) { return __uint_as_float(u); }
+
+// ggml_v_expf, one lane (StablehloMlx/Kernels/Math.lean:28-49): ggml-cpu's NEON
+// exp ("adapted from arm limited optimized routine"), with vfmaq_f32(a, b, c)
+// = fma(b, c, a) and vfmsq_f32(a, b, c) = fma(-b, c, a).
+__device__ __forceinline__ float ggml_v_expf(float x) {
+  const float r = bitsf(0x4B400000u);
+  float z = __fmaf_rn(x, bitsf(0x3FB8AA3Bu), r);
+  float n = __fsub_rn(z, r);
+  float b = __fmaf_rn(-n, bitsf(0x35BFBE8Eu), __fmaf_rn(-n, bitsf(0x3F317200u), x));
+  uint32_t e = fbits(z) << 23;
+  float k = bitsf(e + 0x3F800000u);
+  float u = __fmul_rn(b, b);
+  float p1 = __fmaf_rn(bitsf(0x3E2AAF33u), b, bitsf(0x3EFFFEDBu));
+  float p2 = __fmaf_rn(bitsf(0x3C072010u), b, bitsf(0x3D2B9F17u));
+  float p3 = __fmaf_rn(p2, u, p1);
+  float j = __fmaf_rn(p3, u, __fmul_rn(bitsf(0x3F7FFFF6u), b));
+  float an = fabsf(n);
+  uint32_t d = (n <= 0.0f) ? 0x82000000u : 0u;
+  float s1 = bitsf(d + 0x7F000000u);
+  if (an > bitsf(0x43400000u)) return __fmul_rn(s1, s1);
+  if (an > bitsf(0x42FC0000u)) {
+    float s2 = bitsf(e - d);
+    return __fmul_rn(__fmaf_rn(s2, j, s2), s1);
+  }
+  return __fmaf_rn(k, j, k);
+}
+
+static int check_elems(Arr *a, int64_t need, const char *what) {
+  if (numel(a) < need)
+    return fail("%s: input of %lld elements, the parameters need %lld", what, (long long)numel(a), (long long)need);
+  return 0;
+}
+
+static int require_dtype(Arr *a, int dt, const char *what) {
+  if (a->dtype != dt) return fail("%s: input is %s, %s expected", what, dtype_name(a->dtype), dtype_name(dt));
+  return 0;
+}
+
+// =============================================================== mul_mat ====
+// y[r*M + m] = ggml_vec_dot_f32(w row (r/N)*wbs + m*K, x row r), K long
+// (StablehloMlx/Kernels/Shaders.lean:55-91; Run.lean:64-65). ggml's order:
+// sixteen accumulators a[j], j = k mod 16, each a k-ascending chain of fused
+// multiply-adds starting at +0; the GGML_F32x4_REDUCE tree
+// ((a0+a8)+(a4+a12)) + ((a1+a9)+(a5+a13)) + ((a2+a10)+(a6+a14)) + ((a3+a11)+(a7+a15))
+// grouped as (v0+v1)+(v2+v3); then the tail of K mod 16 elements.
+//
+// The tree is a perfect binary tree whose leaves, left to right, are the
+// classes in bit-reversed order (0, 8, 4, 12, 1, 9, ...). The fast path packs
+// each operand k-major with its K reordered so that leaf s's class fills the
+// s-th contiguous segment of the packed K axis. Each class chain is then an
+// ordinary k-ascending register-tiled GEMM over one segment; at each segment
+// boundary the running accumulators fold into a four-level stack by the
+// post-order of the tree (the binary-counter rule below), which adds exactly
+// the same pairs in the same roles as ggml.
+//
+// Segments are padded to a multiple of 4 k-steps with w = -0 and x = +0: the
+// product is -0 and acc + (-0) == acc for every acc (+0 stays +0, -0 stays -0),
+// so padding leaves every chain bit-identical.
+
+__host__ __device__ constexpr int bitrev4(int s) {
+  return ((s & 1) << 3) | ((s & 2) << 1) | ((s & 4) >> 1) | ((s & 8) >> 3);
+}
+
+// One output, the reference's one-thread-per-output form; also the planted
+// `plain` fault (a sequential binary32 sum without fma, Shaders.lean:65-68).
+__device__ __forceinline__ float dot_tail(const float *w, const float *x, int np, int K, float sumf, int flavor) {
+  int tl = K - np;
+  if (flavor == 0) {  // pinned: separate product and sum
+    for (int i = np; i < K; i++) sumf = __fadd_rn(sumf, __fmul_rn(w[i], x[i]));
+  } else {  // stock: clang's form (Shaders.lean:80-90)
+    int nq = tl >= 4 ? (tl & ~3) : 0;
+    for (int i = np; i < np + nq; i++) sumf = __fadd_rn(sumf, __fmul_rn(w[i], x[i]));
+    for (int i = np + nq; i < K; i++) sumf = __fmaf_rn(w[i], x[i], sumf);
+  }
+  return sumf;
+}
+
+__global__ void k_mul_mat_naive(const float *__restrict__ w, const float *__restrict__ x, float *__restrict__ y,
+                                int K, int M, int64_t R, int64_t N, int64_t wbs, int plain, int flavor) {
+  int64_t total = R * (int64_t)M;
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t t = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; t < total; t += stride) {
+    int64_t r = t / M;
+    int m = (int)(t % M);
+    const float *wr = w + (r / N) * wbs + (int64_t)m * K;
+    const float *xr = x + r * K;
+    if (plain) {
+      float s = 0.0f;
+      for (int i = 0; i < K; i++) s = __fadd_rn(s, __fmul_rn(wr[i], xr[i]));
+      y[t] = s;
+      continue;
+    }
+    float a[16];
+#pragma unroll
+    for (int j = 0; j < 16; j++) a[j] = 0.0f;
+    int np = K & ~15;
+    for (int i = 0; i < np; i += 16) {
+#pragma unroll
+      for (int j = 0; j < 16; j++) a[j] = __fmaf_rn(wr[i + j], xr[i + j], a[j]);
+    }
+#pragma unroll
+    for (int l = 0; l < 4; l++) a[l] = __fadd_rn(a[l], a[8 + l]);
+#pragma unroll
+    for (int l = 0; l < 4; l++) a[4 + l] = __fadd_rn(a[4 + l], a[12 + l]);
+#pragma unroll
+    for (int l = 0; l < 4; l++) a[l] = __fadd_rn(a[l], a[4 + l]);
+    float sumf = __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3]));
+    y[t] = dot_tail(wr, xr, np, K, sumf, flavor);
+  }
+}
+
+// Pack `rows` rows of K floats (per batch) into dst[batch][Kq][rows_p], K reordered
+// class-major (leaf order) over the first np = 16*seg elements, each segment
+// padded to segp with `pad`. Grid: (ceil(rows/32), ceil(segp/8), batches).
+__global__ void k_mm_pack(const float *__restrict__ src, int rows, int K, int64_t src_batch, int seg, int segp,
+                          int rows_p, float pad, float *__restrict__ dst) {
+  __shared__ float tile[32][129];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
+  const int r0 = blockIdx.x * 32;
+  const int c0 = blockIdx.y * 8;  // chunk (of 16 k) index base
+  const int b = blockIdx.z;
+  const int Kq = 16 * segp;
+  const float *s = src + (int64_t)b * src_batch;
+  for (int rr = ty; rr < 32; rr += 8) {
+    int r = r0 + rr;
+    for (int kk = tx; kk < 128; kk += 32) {
+      int k = (c0 * 16) + kk;
+      float v = 0.0f;
+      if (r < rows && (c0 + kk / 16) < seg) v = s[(int64_t)r * K + k];
+      tile[rr][kk] = v;
+    }
+  }
+  __syncthreads();
+  float *d = dst + (int64_t)b * Kq * rows_p;
+  for (int o = ty; o < 128; o += 8) {
+    int j = o >> 3, c = o & 7;
+    int cg = c0 + c;
+    if (cg >= segp) continue;
+    int kq = bitrev4(j) * segp + cg;
+    float v = cg < seg ? tile[tx][16 * c + j] : pad;
+    d[(int64_t)kq * rows_p + r0 + tx] = v;
+  }
+}
+
+namespace mm {
+constexpr int BM = 128;  // w rows (m) per CTA
+constexpr int BN = 64;   // x rows (r) per CTA
+constexpr int BK = 16;   // packed k per stage
+constexpr int NS = 4;    // pipeline stages
+constexpr int THREADS = 256;
+constexpr int TM = 4, TN = 8;
+constexpr int STAGE_FLOATS = BK * (BM + BN);
+}  // namespace mm
+
+__device__ __forceinline__ void cp_async16(void *smem, const void *gmem) {
+  uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem));
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// Fold the finished chain of leaf S into the stack (post-order of the tree).
+template <int S>
+__device__ __forceinline__ void fold(float (&run)[mm::TM * mm::TN], float (&st)[4][mm::TM * mm::TN]) {
+  constexpr int L0 = (S & 1) ? 1 : 0;
+  constexpr int L1 = (S & 3) == 3 ? 1 : 0;
+  constexpr int L2 = (S & 7) == 7 ? 1 : 0;
+  constexpr int L3 = (S & 15) == 15 ? 1 : 0;
+#pragma unroll
+  for (int i = 0; i < mm::TM * mm::TN; i++) {
+    float v = run[i];
+    if (!L0) { st[0][i] = v; continue; }
+    v = __fadd_rn(st[0][i], v);
+    if (!L1) { st[1][i] = v; continue; }
+    v = __fadd_rn(st[1][i], v);
+    if (!L2) { st[2][i] = v; continue; }
+    v = __fadd_rn(st[2][i], v);
+    if (!L3) { st[3][i] = v; continue; }
+    run[i] = __fadd_rn(st[3][i], v);  // the whole tree: sumf
+  }
+}
+
+struct MMArgs {
+  const float *wp;  // packed w [Wb][Kq][Mp]
+  const float *xp;  // packed x [Bx][Kq][Np]
+  const float *w;   // original w, for the tail
+  const float *x;   // original x, for the tail
+  float *y;
+  int K, M, np, segp, Mp, Np;
+  int64_t Nx;       // x rows per batch
+  int64_t wbs;      // w batch stride (elements of the original w), 0 = shared
+  int r_tiles;      // r tiles per batch
+  int flavor;
+};
+
+__global__ void __launch_bounds__(mm::THREADS, 1) k_mul_mat_fast(MMArgs a) {
+  using namespace mm;
+  extern __shared__ __align__(16) float smem[];
+  const int tid = threadIdx.x;
+  const int tm = tid & 31;   // m group: m = m0 + 4*tm + [0,4)
+  const int tn = tid >> 5;   // r group: r = r0 + 8*tn + [0,8)
+  const int m0 = blockIdx.x * BM;
+  const int bx = blockIdx.y / a.r_tiles;          // batch
+  const int rt = blockIdx.y % a.r_tiles;
+  const int64_t rl0 = (int64_t)rt * BN;            // first row within the batch
+  const int Kq = 16 * a.segp;
+  const float *wp = a.wp + (a.wbs ? (int64_t)bx * Kq * a.Mp : 0) + m0;
+  const float *xp = a.xp + (int64_t)bx * Kq * a.Np + rl0;
+  const int nstages = Kq / BK;
+
+  auto issue = [&](int st) {
+    float *ws = smem + (st % NS) * STAGE_FLOATS;
+    float *xs = ws + BK * BM;
+    const int k0 = st * BK;
+    // 16 x 128 floats of w and 16 x 64 of x: 768 16-byte copies, three per thread.
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+      int q = tid + i * THREADS;
+      if (q < BK * BM / 4) {
+        int row = q / (BM / 4), col = (q % (BM / 4)) * 4;
+        cp_async16(ws + row * BM + col, wp + (int64_t)(k0 + row) * a.Mp + col);
+      } else {
+        q -= BK * BM / 4;
+        int row = q / (BN / 4), col = (q % (BN / 4)) * 4;
+        cp_async16(xs + row * BN + col, xp + (int64_t)(k0 + row) * a.Np + col);
+      }
+    }
+  };
+
+#pragma unroll
+  for (int s = 0; s < NS - 1; s++) {
+    if (s < nstages) issue(s);
+    cp_async_commit();
+  }
+
+  float run[TM * TN];
+  float st[4][TM * TN];
+  const int groups_per_seg = a.segp / 4;
+  int g = 0;  // global group (4 packed k-steps) index
+
+#pragma unroll
+  for (int S = 0; S < 16; S++) {
+#pragma unroll
+    for (int i = 0; i < TM * TN; i++) run[i] = 0.0f;
+    for (int gi = 0; gi < groups_per_seg; gi++, g++) {
+      const int stg = g >> 2;
+      if ((g & 3) == 0) {
+        cp_async_wait<NS - 2>();
+        __syncthreads();
+        if (stg + NS - 1 < nstages) issue(stg + NS - 1);
+        cp_async_commit();
+      }
+      const float *ws = smem + (stg % NS) * STAGE_FLOATS;
+      const float *xs = ws + BK * BM;
+      const int row0 = (g & 3) * 4;
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        const float4 wv = *reinterpret_cast<const float4 *>(ws + (row0 + kk) * BM + tm * 4);
+        const float4 x0 = *reinterpret_cast<const float4 *>(xs + (row0 + kk) * BN + tn * 8);
+        const float4 x1 = *reinterpret_cast<const float4 *>(xs + (row0 + kk) * BN + tn * 8 + 4);
+        const float wr[4] = {wv.x, wv.y, wv.z, wv.w};
+        const float xr[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int j = 0; j < TN; j++)
+#pragma unroll
+          for (int i = 0; i < TM; i++) run[j * TM + i] = __fmaf_rn(wr[i], xr[j], run[j * TM + i]);
+      }
+    }
+    switch (S) {
+      case 0: fold<0>(run, st); break;
+      case 1: fold<1>(run, st); break;
+      case 2: fold<2>(run, st); break;
+      case 3: fold<3>(run, st); break;
+      case 4: fold<4>(run, st); break;
+      case 5: fold<5>(run, st); break;
+      case 6: fold<6>(run, st); break;
+      case 7: fold<7>(run, st); break;
+      case 8: fold<8>(run, st); break;
+      case 9: fold<9>(run, st); break;
+      case 10: fold<10>(run, st); break;
+      case 11: fold<11>(run, st); break;
+      case 12: fold<12>(run, st); break;
+      case 13: fold<13>(run, st); break;
+      case 14: fold<14>(run, st); break;
+      default: fold<15>(run, st); break;
+    }
+  }
+  cp_async_wait<0>();
+
+  // Epilogue: the tail (K mod 16 elements, in order) and the store.
+  const int64_t rbase = (int64_t)bx * a.Nx;
+#pragma unroll
+  for (int j = 0; j < TN; j++) {
+    const int64_t rl = rl0 + tn * 8 + j;
+    if (rl >= a.Nx) continue;
+    const int64_t r = rbase + rl;
+#pragma unroll
+    for (int i = 0; i < TM; i++) {
+      const int m = m0 + tm * 4 + i;
+      if (m >= a.M) continue;
+      float v = run[j * TM + i];
+      if (a.np < a.K) {
+        const float *wr = a.w + (a.wbs ? (int64_t)bx * a.wbs : 0) + (int64_t)m * a.K;
+        const float *xr = a.x + r * a.K;
+        v = dot_tail(wr, xr, a.np, a.K, v, a.flavor);
+      }
+      a.y[r * a.M + m] = v;
+    }
+  }
+}
+
+// $SHLO_MUL_MAT_PATH = naive | fast forces one of the two exact paths (both give
+// the same bits; the tests run each); unset, the size decides.
+static int mm_path() {
+  const char *e = getenv("SHLO_MUL_MAT_PATH");
+  if (e && !strcmp(e, "naive")) return 1;
+  if (e && !strcmp(e, "fast")) return 2;
+  return 0;
+}
+
+static int pack_operand(Device *dev, const float *src, int rows, int K, int64_t src_batch, int batches, int seg,
+                        int segp, int rows_p, float pad, Buffer **out) {
+  size_t bytes = (size_t)batches * 16 * segp * rows_p * sizeof(float);
+  SHLO_TRY(buffer_alloc(dev, bytes, out));
+  dim3 grid((rows_p + 31) / 32, (segp + 7) / 8, batches);
+  k_mm_pack<<<grid, 256, 0, dev->stream>>>(src, rows, K, src_batch, seg, segp, rows_p, pad, (float *)(*out)->ptr);
+  if (launch_check("mul_mat pack")) {
+    buffer_release(*out);
+    return 1;
+  }
+  return 0;
+}
+
+int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
+  const int64_t K = p[0], M = p[1], R = p[2], wbs = p[3], N = p[4];
+  const int plain = p[5] != 0;
+  SHLO_TRY(require_dtype(w, kF32, "mul_mat") || require_dtype(x, kF32, "mul_mat"));
+  if (K <= 0 || N <= 0 || R % N) return fail("mul_mat: K=%lld R=%lld N=%lld not carried", (long long)K, (long long)R, (long long)N);
+  const int64_t nb = R / N;
+  SHLO_TRY(check_elems(x, R * K, "mul_mat x"));
+  SHLO_TRY(check_elems(w, (wbs ? (nb - 1) * wbs : 0) + M * K, "mul_mat w"));
+  if (wbs && wbs < M * K) return fail("mul_mat: w batch stride %lld below M*K", (long long)wbs);
+  int64_t shape[1] = {R * M};
+  Arr *o;
+  SHLO_TRY(new_array(dev, kF32, shape, 1, &o));
+  const int flavor = current_flavor();
+  const int64_t np = K & ~(int64_t)15;
+  int path = mm_path();
+  bool fast = !plain && np >= 16 && (path == 2 || (path == 0 && R * M >= 4096));
+  if (R * M == 0) {
+    *out = o;
+    return 0;
+  }
+  if (!fast) {
+    k_mul_mat_naive<<<grid_for(R * M, 256, dev), 256, 0, dev->stream>>>(
+        (const float *)data_ptr(w), (const float *)data_ptr(x), (float *)o->buf->ptr, (int)K, (int)M, R, N, wbs, plain,
+        flavor);
+    if (launch_check("mul_mat")) {
+      shlo_release(o);
+      return 1;
+    }
+    *out = o;
+    return 0;
+  }
+  const int seg = (int)(np / 16);
+  const int segp = (seg + 3) & ~3;
+  const int Mp = (int)((M + mm::BM - 1) / mm::BM * mm::BM);
+  const int64_t Bx = wbs ? nb : 1;
+  const int64_t Nx = wbs ? N : R;
+  const int Np = (int)((Nx + mm::BN - 1) / mm::BN * mm::BN);
+  const int Wb = wbs ? (int)nb : 1;
+  // The packed w is derived from w's storage, which never changes: keep it.
+  Buffer *wpk = nullptr;
+  {
+    char key[160];
+    snprintf(key, sizeof key, "mm:%lld:%lld:%lld:%d:%lld", (long long)w->offset, (long long)K, (long long)M, Wb,
+             (long long)wbs);
+    std::lock_guard<std::mutex> lk(w->buf->derived_mu);
+    auto it = w->buf->derived.find(key);
+    if (it != w->buf->derived.end()) {
+      wpk = it->second;
+      buffer_retain(wpk);
+    } else {
+      if (pack_operand(dev, (const float *)data_ptr(w), (int)M, (int)K, wbs, Wb, seg, segp, Mp, -0.0f, &wpk)) {
+        shlo_release(o);
+        return 1;
+      }
+      if (!w->buf->graph_owned) {
+        buffer_retain(wpk);
+        w->buf->derived[key] = wpk;
+      }
+    }
+  }
+  Buffer *xpk;
+  if (pack_operand(dev, (const float *)data_ptr(x), (int)Nx, (int)K, Nx * K, (int)Bx, seg, segp, Np, 0.0f, &xpk)) {
+    buffer_release(wpk);
+    shlo_release(o);
+    return 1;
+  }
+  MMArgs a;
+  a.wp = (const float *)wpk->ptr;
+  a.xp = (const float *)xpk->ptr;
+  a.w = (const float *)data_ptr(w);
+  a.x = (const float *)data_ptr(x);
+  a.y = (float *)o->buf->ptr;
+  a.K = (int)K;
+  a.M = (int)M;
+  a.np = (int)np;
+  a.segp = segp;
+  a.Mp = Mp;
+  a.Np = Np;
+  a.Nx = Nx;
+  a.wbs = wbs;
+  a.r_tiles = Np / mm::BN;
+  a.flavor = flavor;
+  const size_t smem = (size_t)mm::NS * mm::STAGE_FLOATS * sizeof(float);
+  static bool attr_done[64] = {false};
+  if (!attr_done[dev->id]) {
+    if (cuda_check(cudaFuncSetAttribute(k_mul_mat_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                   "mul_mat attribute")) {
+      buffer_release(wpk);
+      buffer_release(xpk);
+      shlo_release(o);
+      return 1;
+    }
+    attr_done[dev->id] = true;
+  }
+  dim3 grid(Mp / mm::BM, (unsigned)(Bx * a.r_tiles));
+  k_mul_mat_fast<<<grid, mm::THREADS, smem, dev->stream>>>(a);
+  int rc = launch_check("mul_mat");
+  buffer_release(wpk);
+  buffer_release(xpk);
+  if (rc) {
+    shlo_release(o);
+    return 1;
+  }
+  *out = o;
+  return 0;
+}
+
+// ============================================================== soft_max ====
+// Shaders.lean:100-123 / ggml_compute_forward_soft_max_f32 with
+// ggml_vec_soft_max_f32 (vec.cpp): wv = x*scale; max; each four-lane group
+// e_l = ggml_v_expf(wv_l - max), y = e, part = (e0+e1)+(e2+e3); the parts are
+// added to a binary64 sum in group order; inv = (float)(1.0/sum); y *= inv.
+//
+// One warp per row. The max is an exact order-free reduction: for rows without
+// NaN it is the largest value, and which of +0/-0 it is cannot change any
+// output (wv - max is then +-0 or the same nonzero value, and ggml_v_expf(+-0)
+// is 1). Rows with a NaN take the sequential scan of the spec. The binary64
+// sum is the spec's serial chain, run by lane 0 over the parts in order.
+// Rows whose length is not a multiple of 4 are refused by the caller.
+
+template <int G>  // float4 groups per lane kept in registers (0 = stream through memory)
+__global__ void g_soft_max(const float *__restrict__ x, float *__restrict__ y, int ncols, int64_t rows, float sc,
+                           int float_sum) {
+  extern __shared__ float parts_all[];
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  const int wpb = blockDim.x >> 5;
+  const int ng = ncols / 4;
+  float *parts = parts_all + wib * (G > 0 ? G * 32 : 256);
+  for (int64_t row = (int64_t)blockIdx.x * wpb + wib; row < rows; row += (int64_t)gridDim.x * wpb) {
+    const float4 *xr = reinterpret_cast<const float4 *>(x + row * ncols);
+    float4 *yr = reinterpret_cast<float4 *>(y + row * ncols);
+    float4 v[G > 0 ? G : 1];
+    float mx = -INFINITY;
+    bool nan = false;
+    if (G > 0) {
+#pragma unroll
+      for (int i = 0; i < G; i++) {
+        int gi = lane + 32 * i;
+        if (gi < ng) {
+          float4 t = xr[gi];
+          t.x = __fmul_rn(t.x, sc); t.y = __fmul_rn(t.y, sc); t.z = __fmul_rn(t.z, sc); t.w = __fmul_rn(t.w, sc);
+          v[i] = t;
+          nan |= (t.x != t.x) | (t.y != t.y) | (t.z != t.z) | (t.w != t.w);
+          mx = fmaxf(mx, fmaxf(fmaxf(t.x, t.y), fmaxf(t.z, t.w)));
+        }
+      }
+    } else {
+      for (int gi = lane; gi < ng; gi += 32) {
+        float4 t = xr[gi];
+        t.x = __fmul_rn(t.x, sc); t.y = __fmul_rn(t.y, sc); t.z = __fmul_rn(t.z, sc); t.w = __fmul_rn(t.w, sc);
+        nan |= (t.x != t.x) | (t.y != t.y) | (t.z != t.z) | (t.w != t.w);
+        mx = fmaxf(mx, fmaxf(fmaxf(t.x, t.y), fmaxf(t.z, t.w)));
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    if (__any_sync(0xffffffffu, nan)) {
+      if (lane == 0) {
+        float m = -INFINITY;
+        for (int i = 0; i < ncols; i++) {
+          float wv = __fmul_rn(x[row * ncols + i], sc);
+          m = (m > wv) ? m : wv;
+        }
+        mx = m;
+      }
+      mx = __shfl_sync(0xffffffffu, mx, 0);
+    }
+    double sum = 0.0;
+    float fs = 0.0f;
+    // Chunks of 32*max(G,8) groups: parts into shared memory, lane 0 chains them.
+    const int chunk = 32 * (G > 0 ? G : 8);
+    for (int c0 = 0; c0 < ng; c0 += chunk) {
+#pragma unroll
+      for (int i = 0; i < (G > 0 ? G : 8); i++) {
+        int gi = c0 + lane + 32 * i;
+        if (gi < ng) {
+          float4 t;
+          if (G > 0) {
+            t = v[i];
+          } else {
+            t = xr[gi];
+            t.x = __fmul_rn(t.x, sc); t.y = __fmul_rn(t.y, sc); t.z = __fmul_rn(t.z, sc); t.w = __fmul_rn(t.w, sc);
+          }
+          float4 e;
+          e.x = ggml_v_expf(__fsub_rn(t.x, mx));
+          e.y = ggml_v_expf(__fsub_rn(t.y, mx));
+          e.z = ggml_v_expf(__fsub_rn(t.z, mx));
+          e.w = ggml_v_expf(__fsub_rn(t.w, mx));
+          if (G > 0) v[i] = e;
+          else yr[gi] = e;
+          parts[lane + 32 * i] = __fadd_rn(__fadd_rn(e.x, e.y), __fadd_rn(e.z, e.w));
+        }
+      }
+      __syncwarp();
+      if (lane == 0) {
+        int n = ng - c0 < chunk ? ng - c0 : chunk;
+        for (int k = 0; k < n; k++) {
+          float pv = parts[k];
+          sum = __dadd_rn(sum, (double)pv);
+          fs = __fadd_rn(fs, pv);
+        }
+      }
+      __syncwarp();
+    }
+    float inv;
+    if (lane == 0) inv = float_sum ? __fdiv_rn(1.0f, fs) : __double2float_rn(__ddiv_rn(1.0, sum));
+    inv = __shfl_sync(0xffffffffu, inv, 0);
+    if (G > 0) {
+#pragma unroll
+      for (int i = 0; i < G; i++) {
+        int gi = lane + 32 * i;
+        if (gi < ng) {
+          float4 e = v[i];
+          e.x = __fmul_rn(e.x, inv); e.y = __fmul_rn(e.y, inv); e.z = __fmul_rn(e.z, inv); e.w = __fmul_rn(e.w, inv);
+          yr[gi] = e;
+        }
+      }
+    } else {
+      for (int gi = lane; gi < ng; gi += 32) {
+        float4 e = yr[gi];
+        e.x = __fmul_rn(e.x, inv); e.y = __fmul_rn(e.y, inv); e.z = __fmul_rn(e.z, inv); e.w = __fmul_rn(e.w, inv);
+        yr[gi] = e;
+      }
+    }
+    __syncwarp();
+  }
+}
+
+int k_soft_max(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
+  const int64_t ncols = p[0], rows = p[1];
+  const float sc = bitsf_host(p[2]);
+  const int float_sum = p[3] != 0;
+  SHLO_TRY(require_dtype(x, kF32, "soft_max"));
+  if (ncols % 4)
+    return fail("soft_max: a row of %lld has a %lld-element tail that ggml-cpu sends through the platform expf, "
+                "which is not carried", (long long)ncols, (long long)(ncols % 4));
+  SHLO_TRY(check_elems(x, ncols * rows, "soft_max"));
+  int64_t shape[1] = {ncols * rows};
+  Arr *o;
+  SHLO_TRY(new_array(dev, kF32, shape, 1, &o));
+  if (ncols * rows > 0) {
+    const int wpb = 4;
+    int64_t blocks = (rows + wpb - 1) / wpb;
+    if (blocks > (int64_t)dev->sm_count * 16) blocks = (int64_t)dev->sm_count * 16;
+    const float *xp = (const float *)data_ptr(x);
+    float *yp = (float *)o->buf->ptr;
+    int ng = (int)(ncols / 4);
+    if (ng <= 32 * 2)
+      g_soft_max<2><<<(unsigned)blocks, wpb * 32, wpb * 64 * sizeof(float), dev->stream>>>(xp, yp, (int)ncols, rows, sc, float_sum);
+    else if (ng <= 32 * 8)
+      g_soft_max<8><<<(unsigned)blocks, wpb * 32, wpb * 256 * sizeof(float), dev->stream>>>(xp, yp, (int)ncols, rows, sc, float_sum);
+    else
+      g_soft_max<0><<<(unsigned)blocks, wpb * 32, wpb * 256 * sizeof(float), dev->stream>>>(xp, yp, (int)ncols, rows, sc, float_sum);
+    if (launch_check("soft_max")) {
+      shlo_release(o);
+      return 1;
+    }
+  }
+  *out = o;
+  return 0;
+}
+
+// ================================================================== norm ====
+// Shaders.lean:130-166 / ggml_compute_forward_norm_f32 without Accelerate:
+// sum = binary64 sum of the row in order; mean = (float)sum / (float)N (a
+// correctly rounded binary32 division); s2 = binary64 sum, in order, of the
+// four-lane groups (d0^2+d1^2)+(d2^2+d3^2), d = x - mean, then of the tail
+// elements' d^2; var = (float)(s2 / N); scale = 1.0f / sqrtf(var + eps); y =
+// (x - mean) * scale.
+//
+// Each warp owns 32 rows; lane l runs row l's two serial binary64 chains. The
+// rows stream through a 32x33 shared-memory tile in chunks of 32 columns, so
+// every global access is a coalesced row segment.
+
+__global__ void g_norm(const float *__restrict__ x, float *__restrict__ y, int ncols, int64_t rows, float eps,
+                       int gpu_ops) {
+  __shared__ float tiles[8][32][33];
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  float(*tile)[33] = tiles[wib];
+  const int64_t nblk = (rows + 31) / 32;
+  for (int64_t blk = (int64_t)blockIdx.x * 8 + wib; blk < nblk; blk += (int64_t)gridDim.x * 8) {
+    const int64_t r0 = blk * 32;
+    const int nr = rows - r0 < 32 ? (int)(rows - r0) : 32;
+    auto load_tile = [&](int c0) {
+#pragma unroll 8
+      for (int rr = 0; rr < 32; rr++) {
+        float v = 0.0f;
+        if (rr < nr && c0 + lane < ncols) v = x[(r0 + rr) * ncols + c0 + lane];
+        tile[rr][lane] = v;
+      }
+      __syncwarp();
+    };
+    const int nb = ncols & ~3;
+    double sum = 0.0;
+    float fsum = 0.0f;
+    for (int c0 = 0; c0 < ncols; c0 += 32) {
+      load_tile(c0);
+      int n = ncols - c0 < 32 ? ncols - c0 : 32;
+      for (int c = 0; c < n; c++) {
+        float v = tile[lane][c];
+        sum = __dadd_rn(sum, (double)v);
+        fsum = __fadd_rn(fsum, v);
+      }
+      __syncwarp();
+    }
+    float mean = gpu_ops ? __fdividef(fsum, (float)ncols) : __fdiv_rn(__double2float_rn(sum), (float)ncols);
+    double s2 = 0.0;
+    float fs2 = 0.0f;
+    for (int c0 = 0; c0 < ncols; c0 += 32) {
+      load_tile(c0);
+      int n = ncols - c0 < 32 ? ncols - c0 : 32;
+      int c = 0;
+      for (; c + 3 < n && c0 + c + 3 < nb; c += 4) {
+        float d0 = __fsub_rn(tile[lane][c], mean), d1 = __fsub_rn(tile[lane][c + 1], mean);
+        float d2 = __fsub_rn(tile[lane][c + 2], mean), d3 = __fsub_rn(tile[lane][c + 3], mean);
+        float q = __fadd_rn(__fadd_rn(__fmul_rn(d0, d0), __fmul_rn(d1, d1)), __fadd_rn(__fmul_rn(d2, d2), __fmul_rn(d3, d3)));
+        s2 = __dadd_rn(s2, (double)q);
+        fs2 = __fadd_rn(fs2, __fmul_rn(d0, d0));
+        fs2 = __fadd_rn(fs2, __fmul_rn(d1, d1));
+        fs2 = __fadd_rn(fs2, __fmul_rn(d2, d2));
+        fs2 = __fadd_rn(fs2, __fmul_rn(d3, d3));
+      }
+      for (; c < n; c++) {
+        float d = __fsub_rn(tile[lane][c], mean);
+        float q = __fmul_rn(d, d);
+        s2 = __dadd_rn(s2, (double)q);
+        fs2 = __fadd_rn(fs2, q);
+      }
+      __syncwarp();
+    }
+    float scl;
+    if (gpu_ops) {
+      scl = __fdividef(1.0f, sqrtf(__fadd_rn(__fdividef(fs2, (float)ncols), eps)));
+    } else {
+      float var = __double2float_rn(__ddiv_rn(s2, (double)ncols));
+      scl = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    }
+    for (int c0 = 0; c0 < ncols; c0 += 32) {
+      if (c0 + lane >= ncols) continue;
+#pragma unroll 8
+      for (int rr = 0; rr < 32; rr++) {
+        float m = __shfl_sync(0xffffffffu, mean, rr);
+        float s = __shfl_sync(0xffffffffu, scl, rr);
+        if (rr < nr) {
+          int64_t i = (r0 + rr) * ncols + c0 + lane;
+          y[i] = __fmul_rn(__fsub_rn(x[i], m), s);
+        }
+      }
+    }
+  }
+}
+
+int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
+  const int64_t ncols = p[0], rows = p[1];
+  const float eps = bitsf_host(p[2]);
+  SHLO_TRY(require_dtype(x, kF32, "norm"));
+  SHLO_TRY(check_elems(x, ncols * rows, "norm"));
+  int64_t shape[1] = {ncols * rows};
+  Arr *o;
+  SHLO_TRY(new_array(dev, kF32, shape, 1, &o));
+  if (ncols * rows > 0) {
+    int64_t nblk = (rows + 31) / 32;
+    int64_t blocks = (nblk + 7) / 8;
+    if (blocks > (int64_t)dev->sm_count * 8) blocks = (int64_t)dev->sm_count * 8;
+    g_norm<<<(unsigned)blocks, 256, 0, dev->stream>>>((const float *)data_ptr(x), (float *)o->buf->ptr, (int)ncols,
+                                                       rows, eps, p[3] != 0);
+    if (launch_check("norm")) {
+      shlo_release(o);
+      return 1;
+    }
+  }
+  *out = o;
+  return 0;
+}
+
+// =========================================================== elementwise ====
+
+// silu: Shaders.lean:172-179 (ggml_vec_silu_f32's four-lane body):
+// y = x / (1 + ggml_v_expf(0 - x)), a correctly rounded division.
+__global__ void g_silu(const float *__restrict__ x, float *__restrict__ y, int64_t n, int gpu_ops) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float v = x[i];
+    if (gpu_ops) y[i] = __fdividef(v, __fadd_rn(1.0f, __expf(-v)));
+    else y[i] = __fdiv_rn(v, __fadd_rn(1.0f, ggml_v_expf(__fsub_rn(0.0f, v))));
+  }
+}
+
+// gelu_erf: Shaders.lean:186-199 (ggml_vec_gelu_erf_f32):
+// y = (0.5f*x) * (1.0f + erff(x*SQRT_2_INV)) with the correctly rounded erff; a
+// NaN input returns itself quieted, as every arm64 step does.
+__global__ void g_gelu_erf(const float *__restrict__ x, float *__restrict__ y, int64_t n, int gpu_erf) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float v = x[i];
+    float ev;
+    if (gpu_erf) {
+      // The planted fault: GELU's tanh form (SQRT_2_OVER_PI, GELU_COEF_A of vec.h).
+      ev = tanhf(__fmul_rn(__fmul_rn(bitsf(0x3F4C422Au), v),
+                           __fadd_rn(1.0f, __fmul_rn(__fmul_rn(bitsf(0x3D372713u), v), v))));
+    } else {
+      ev = shlo_erf::erff_cr(__fmul_rn(v, bitsf(0x3F3504F3u)));
+    }
+    float r = __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, ev));
+    uint32_t b = fbits(v);
+    if ((b & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(b | 0x00400000u);
+    y[i] = r;
+  }
+}
+
+// erff_map: Shaders.lean:204-208: y[t] = bits(erff(bits^-1(base + t))).
+__global__ void g_erff_map(uint32_t base, int64_t n, uint32_t *__restrict__ y) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
+    y[i] = fbits(shlo_erf::erff_cr(bitsf(base + (uint32_t)i)));
+}
+
+// divide and sqrt: SoftFloat.lean:262-305, correctly rounded binary32 with the
+// soft-float NaN rules: a NaN operand is returned quieted (the first one
+// first), an invalid operation gives 0x7FC00000; sqrt returns +inf, a positive
+// NaN (unquieted) and +-0 unchanged, and 0x7FC00000 for any negative input.
+__global__ void g_divide(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ y, int64_t n) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float u = a[i], v = b[i];
+    uint32_t ub = fbits(u), vb = fbits(v);
+    float r;
+    if ((ub & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(ub | 0x00400000u);
+    else if ((vb & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(vb | 0x00400000u);
+    else {
+      r = __fdiv_rn(u, v);
+      if (r != r) r = bitsf(0x7FC00000u);
+    }
+    y[i] = r;
+  }
+}
+
+__global__ void g_sqrt(const float *__restrict__ a, float *__restrict__ y, int64_t n) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    float u = a[i];
+    uint32_t b = fbits(u);
+    float r;
+    if ((b & 0x7FFFFFFFu) == 0) r = u;
+    else if (b >> 31) r = bitsf(0x7FC00000u);
+    else if (b >= 0x7F800000u) r = u;
+    else r = __fsqrt_rn(u);
+    y[i] = r;
+  }
+}
+
+// Binary64 on uint64 bit patterns (SoftFloat.lean:137-259, Shaders.lean:231-257):
+// the GPU's IEEE binary64 units, with arm64's NaN rules written out (a NaN
+// operand quieted, the first one first; invalid -> 0x7FF8000000000000), floor
+// exact, and the conversion to int64 truncating with saturation (NaN -> 0).
+#define QNAN64 0x7FF8000000000000ull
+__device__ __forceinline__ bool nan64(uint64_t v) { return (v & 0x7FFFFFFFFFFFFFFFull) > 0x7FF0000000000000ull; }
+
+__global__ void g_f64_ew(const uint64_t *__restrict__ a, const uint64_t *__restrict__ b, uint64_t *__restrict__ y,
+                         int64_t n, int op) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    uint64_t u = a[i];
+    uint64_t r;
+    if (op == 4) {  // floor
+      r = nan64(u) ? (u | 0x8000000000000ull) : (uint64_t)__double_as_longlong(floor(__longlong_as_double((long long)u)));
+    } else if (op == 5) {  // to int64, toward zero, saturating
+      double d = __longlong_as_double((long long)u);
+      if (nan64(u)) r = 0;
+      else if (d >= 9223372036854775808.0) r = 0x7FFFFFFFFFFFFFFFull;
+      else if (d <= -9223372036854775808.0) r = 0x8000000000000000ull;
+      else r = (uint64_t)__double2ll_rz(d);
+    } else {
+      uint64_t v = b[i];
+      if (nan64(u)) r = u | 0x8000000000000ull;
+      else if (nan64(v)) r = v | 0x8000000000000ull;
+      else {
+        double x = __longlong_as_double((long long)u), z = __longlong_as_double((long long)v), q;
+        switch (op) {
+          case 0: q = __dadd_rn(x, z); break;
+          case 1: q = __dsub_rn(x, z); break;
+          case 2: q = __dmul_rn(x, z); break;
+          default: q = __ddiv_rn(x, z); break;
+        }
+        r = (q != q) ? QNAN64 : (uint64_t)__double_as_longlong(q);
+      }
+    }
+    y[i] = r;
+  }
+}
+
+// Exact widening; a NaN keeps its payload and is not quieted (SoftFloat.lean:73-85).
+__global__ void g_f64_of_f32(const float *__restrict__ a, uint64_t *__restrict__ y, int64_t n) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    uint32_t b = fbits(a[i]);
+    uint64_t r;
+    if ((b & 0x7FFFFFFFu) > 0x7F800000u)
+      r = ((uint64_t)(b >> 31) << 63) | 0x7FF0000000000000ull | ((uint64_t)(b & 0x7FFFFFu) << 29);
+    else
+      r = (uint64_t)__double_as_longlong((double)a[i]);
+    y[i] = r;
+  }
+}
+
+// Round to nearest even with subnormals; a NaN is quieted, payload kept (SoftFloat.lean:95-120).
+__global__ void g_f32_of_f64(const uint64_t *__restrict__ a, float *__restrict__ y, int64_t n) {
+  int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
+    uint64_t d = a[i];
+    float r;
+    if (nan64(d))
+      r = bitsf((uint32_t)((d >> 63) << 31) | 0x7FC00000u | (uint32_t)((d & 0xFFFFFFFFFFFFFull) >> 29));
+    else
+      r = __double2float_rn(__longlong_as_double((long long)d));
+    y[i] = r;
+  }
+}
+
+template <typename K, typename... Args>
+static int launch_ew(Device *dev, int64_t n, K kernel, const char *what, Args... args) {
+  if (n <= 0) return 0;
+  kernel<<<grid_for(n, 256, dev, 16), 256, 0, dev->stream>>>(args...);
+  return launch_check(what);
+}
+
+static int simple_out(Device *dev, int dt, int64_t n, Arr **o) {
+  int64_t shape[1] = {n};
+  return new_array(dev, (uint8_t)dt, shape, 1, o);
+}
+
+int k_silu(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
+  int64_t n = p[0];
+  SHLO_TRY(require_dtype(x, kF32, "silu") || check_elems(x, n, "silu"));
+  Arr *o;
+  SHLO_TRY(simple_out(dev, kF32, n, &o));
+  if (launch_ew(dev, n, g_silu, "silu", (const float *)data_ptr(x), (float *)o->buf->ptr, n, (int)(p[1] != 0))) {
+    shlo_release(o);
+    return 1;
+  }
+  *out = o;
+  return 0;
+}
+
+int k_gelu_erf(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
+  int64_t n = p[0];
+  SHLO_TRY(require_dtype(x, kF32, "gelu_erf") || check_elems(x, n, "gelu_erf"));
+  if (current_flavor() == 1 && p[1] == 0)
+    return fail("gelu_erf: the stock build's erff is Apple libsystem_m's platform erff, which is not carried "
+                "(this backend carries the correctly rounded erff of the pinned build)");
+  Arr *o;
+  SHLO_TRY(simple_out(dev, kF32, n, &o));
+  if (launch_ew(dev, n, g_gelu_erf, "gelu_erf", (const float *)data_ptr(x), (float *)o->buf->ptr, n, (int)(p[1] != 0))) {
+    shlo_release(o);
+    return 1;
+  }
+  *out = o;
+  return 0;
+}
+
+int k_erff_map(Device *dev, const uint32_t *p, Arr **out) {
+  int64_t n = p[1];
+  Arr *o;
+  SHLO_TRY(simple_out(dev, kU32, n, &o));
+  if (launch_ew(dev, n, g_erff_map, "erff_map", p[0], n, (uint32_t *)o->buf->ptr)) {
+    shlo_release(o);
+    return 1;
+  }
+  *out = o;
+  return 0;
+}
+
+int k_divide(Device *dev, Arr *a, Arr *b, const uint32_t *p, Arr **out) {
+  int64_t n = p[0];
+  SHLO_TRY(require_dtype(a, kF32, "divide") || require_dtype(b, kF32, "divide"));
+  SHLO_TRY(check_elems(a, n, "divide") || check_elems(b, n, "divide"));
+  Arr *o;
+  SHLO_TRY(simple_out(dev, kF32, n, &o));
+  if (launch_ew(dev, n, g_divide, "divide", (const float *)data_ptr(a), (const float *)data_ptr(b),
+                (float *)o->buf->ptr, n)) {
+    shlo_release(o);
+    return 1;
+  }
+  *out = o;
+  return 0;
+}
+
+int k_sqrt(Device *dev, Arr *a, const uint32_t *p, Arr **out) {
+  int64_t n = p[0];
+  SHLO_TRY(require_dtype(a, kF32, "sqrt") || check_elems(a, n, "sqrt"));
+  Arr *o;
+  SHLO_TRY(simple_out(dev, kF32, n, &o));
+  if (launch_ew(dev, n, g_sqrt, "sqrt", (const float *)data_ptr(a), (float *)o->buf->ptr, n)) {
+    shlo_release(o);
+    return 1;
+  }
+  *out = o;
+  return 0;
+}
+
+int k_f64_ew(Device *dev, Arr *a, Arr *b, const uint32_t *p, Arr **out) {
+  int64_t n = p[0];
+  int op = (int)p[1];
+  if (op < 0 || op > 5) return fail("f64_ew: op %d not carried", op);
+  SHLO_TRY(require_dtype(a, kU64, "f64_ew") || require_dtype(b, kU64, "f64_ew"));
+  SHLO_TRY(check_elems(a, n, "f64_ew") || check_elems(b, n, "f64_ew"));
+  Arr *o;
+  SHLO_TRY(simple_out(dev, kU64, n, &o));
+  if (launch_ew(dev, n, g_f64_ew, "f64_ew", (const uint64_t *)data_ptr(a), (const uint64_t *)data_ptr(b),
+                (uint64_t *)o->buf->ptr, n, op)) {
+    shlo_release(o);
+    return 1;
+  }
+  *out = o;
+  return 0;
+}
+
+int k_f64_of_f32(Device *dev, Arr *a, const uint32_t *p, Arr **out) {
+  int64_t n = p[0];
+  SHLO_TRY(require_dtype(a, kF32, "f64_of_f32") || check_elems(a, n, "f64_of_f32"));
+  Arr *o;
+  SHLO_TRY(simple_out(dev, kU64, n, &o));
+  if (launch_ew(dev, n, g_f64_of_f32, "f64_of_f32", (const float *)data_ptr(a), (uint64_t *)o->buf->ptr, n)) {
+    shlo_release(o);
+    return 1;
+  }
+  *out = o;
+  return 0;
+}
+
+int k_f32_of_f64(Device *dev, Arr *a, const uint32_t *p, Arr **out) {
+  int64_t n = p[0];
+  SHLO_TRY(require_dtype(a, kU64, "f32_of_f64") || check_elems(a, n, "f32_of_f64"));
+  Arr *o;
+  SHLO_TRY(simple_out(dev, kF32, n, &o));
+  if (launch_ew(dev, n, g_f32_of_f64, "f32_of_f64", (const uint64_t *)data_ptr(a), (float *)o->buf->ptr, n)) {
+    shlo_release(o);
+    return 1;
+  }
+  *out = o;
+  return 0;
+}
+
+}  // namespace shlo

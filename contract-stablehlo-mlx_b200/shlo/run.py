@@ -1,0 +1,128 @@
+"""StablehloMlx/Kernels/Run.lean restated: dispatch the exact kernels.
+
+Each kernel is created once by name (Run.lean:19-25, `"smlx_" ++ name`) and
+applied to arrays that stay on the device; the scalar parameters travel as an
+8-word uint32 array (Run.lean:51-52). Inputs under 8 elements are padded with
+zeros (Run.lean:37-43) -- a Metal binding quirk the CUDA backend does not need,
+kept so the call sequence is the reference's.
+
+The Metal source and header strings are not carried: the CUDA backend selects
+its kernel by name and ignores them.
+"""
+from __future__ import annotations
+
+from . import mlx as M
+
+# Binding names per kernel (StablehloMlx/Kernels/Shaders.lean globals).
+SPECS = {
+    "mul_mat": (["w", "x", "p"], ["y"]),
+    "soft_max": (["x", "p"], ["y"]),
+    "norm": (["x", "p"], ["y"]),
+    "silu": (["x", "p"], ["y"]),
+    "gelu_erf": (["x", "erffTable", "p"], ["y"]),
+    "erff_map": (["erffTable", "p"], ["y"]),
+    "divide": (["a", "b", "p"], ["y"]),
+    "sqrt": (["a", "p"], ["y"]),
+    "f64_ew": (["a", "b", "p"], ["y"]),
+    "f64_of_f32": (["a", "p"], ["y"]),
+    "f32_of_f64": (["a", "p"], ["y"]),
+}
+
+_cache: dict = {}
+
+
+def kernel(name: str) -> M.Kernel:
+    k = _cache.get(name)
+    if k is None:
+        if name not in SPECS:
+            raise M.ShloError("no generated kernel %s" % name)
+        ins, outs = SPECS[name]
+        k = M.kernel_new("smlx_" + name, ins, outs, "", "")
+        _cache[name] = k
+    return k
+
+
+def run(name: str, inputs, out_shape, out_dtype: int, threads: int, tg: int) -> M.Arr:
+    """Run.lean:34-45."""
+    k = kernel(name)
+    padded = []
+    for a in inputs:
+        n = 1
+        for d in M.shape(a):
+            n *= d
+        if n >= 8:
+            padded.append(a)
+            continue
+        pad = M.astype(M.u32_arr([0] * (8 - n)), M.dtype(a))
+        padded.append(M.concat([M.reshape(a, [n]), pad], 0))
+    outs = M.kernel_apply(k, padded, [out_shape], bytes([out_dtype]), [max(threads, 1), 1, 1], [tg, 1, 1])
+    return outs[0]
+
+
+def params(ws) -> M.Arr:
+    """Run.lean:51-52: the parameter words, padded to 8."""
+    ws = list(ws) + [0] * (8 - len(ws))
+    return M.u32_arr(ws)
+
+
+_erff_table = None
+
+
+def erff_table() -> M.Arr:
+    """Run.lean:54-60 binds a coefficient table here; the correctly rounded erff
+    of this backend needs none, so the binding gets a placeholder of 8 zeros."""
+    global _erff_table
+    if _erff_table is None:
+        _erff_table = M.of_bytes(bytes(32), [8], M.dtF32)
+    return _erff_table
+
+
+def mul_mat(w, x, K, M_, R, N, w_batch_stride, plain=False):
+    """Run.lean:62-65: ggml_mul_mat's dot order; w is [Wb, M, K], x is [R, K] with
+    R = batch * N; the result is [R, M]."""
+    return run("mul_mat", [w, x, params([K, M_, R, w_batch_stride, N, 1 if plain else 0])], [R * M_], M.dtF32,
+               R * M_, 64)
+
+
+def soft_max(x, ncols, rows, scale_bits, float_sum=False):
+    return run("soft_max", [x, params([ncols, rows, scale_bits, 1 if float_sum else 0])], [rows * ncols], M.dtF32,
+               rows, 64)
+
+
+def norm(x, ncols, rows, eps_bits, gpu_ops=False):
+    return run("norm", [x, params([ncols, rows, eps_bits, 1 if gpu_ops else 0])], [rows * ncols], M.dtF32, rows, 64)
+
+
+def silu(x, count, gpu_ops=False):
+    return run("silu", [x, params([count, 1 if gpu_ops else 0])], [count], M.dtF32, count, 64)
+
+
+def gelu_erf(x, count, gpu_erf=False):
+    return run("gelu_erf", [x, erff_table(), params([count, 1 if gpu_erf else 0])], [count], M.dtF32, count, 64)
+
+
+def erff_map(base, count):
+    return run("erff_map", [erff_table(), params([base, count])], [count], M.dtU32, count, 256)
+
+
+def divide(a, b, count):
+    return run("divide", [a, b, params([count])], [count], M.dtF32, count, 256)
+
+
+def sqrt(a, count):
+    return run("sqrt", [a, params([count])], [count], M.dtF32, count, 256)
+
+
+F64_ADD, F64_SUB, F64_MUL, F64_DIV, F64_FLOOR, F64_TO_I64 = range(6)
+
+
+def f64_ew(op, a, b, count):
+    return run("f64_ew", [a, b, params([count, op])], [count], M.dtU64, count, 256)
+
+
+def f64_of_f32(a, count):
+    return run("f64_of_f32", [a, params([count])], [count], M.dtU64, count, 256)
+
+
+def f32_of_f64(a, count):
+    return run("f32_of_f64", [a, params([count])], [count], M.dtF32, count, 256)

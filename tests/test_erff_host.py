@@ -1,0 +1,81 @@
+"""The correctly rounded erff of the CUDA library, built for the host, against
+the oracle (erfl with binary128 hard cases) -- no GPU needed.
+
+Both paths of contract-stablehlo-mlx_b200/csrc/erff_cr.cuh are checked: the
+fast path (binary64 erf + rounding test) and the double-double series alone,
+which the fast path falls back to near rounding midpoints.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+from oracle import oracle as O
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+SO = os.path.join(HERE, "helpers", "liberff_host.so")
+
+
+@pytest.fixture(scope="module")
+def host():
+    src = os.path.join(HERE, "helpers", "erff_host.cpp")
+    hdr = os.path.join(HERE, "..", "contract-stablehlo-mlx_b200", "csrc", "erff_cr.cuh")
+    if not os.path.exists(SO) or os.path.getmtime(SO) < max(os.path.getmtime(src), os.path.getmtime(hdr)):
+        subprocess.run(["/usr/bin/g++", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared", src, "-o", SO],
+                       check=True)
+    L = ctypes.CDLL(SO)
+    p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
+    for f in (L.erff_cr_bits, L.erff_slow_bits):
+        f.argtypes = [p, p, ctypes.c_long]
+    return L
+
+
+def sample_bits():
+    rng = np.random.default_rng(2024)
+    parts = [rng.integers(0, 2**32, 1 << 18, dtype=np.uint64).astype(np.uint32)]
+    # dense slices: tiny and subnormal inputs, around 1, and the approach to +-1 (|x| near 3.9-4)
+    for lo in (0x00000000, 0x00800000, 0x3F800000, 0x407A0000, 0x40800000 - 4096, 0x33000000, 0x39800000):
+        parts.append(np.arange(lo, lo + 8192, dtype=np.uint64).astype(np.uint32))
+    s = np.concatenate(parts)
+    return np.concatenate([s, s | np.uint32(0x80000000)])
+
+
+def oracle_bits(xb):
+    out = np.empty_like(xb)
+    # orc_erff_range covers consecutive patterns; sample per element via the scalar entry
+    L = O.lib()
+    f = xb.view(np.float32)
+    for i in range(xb.size):
+        out[i] = np.float32(L.orc_erff_cr(float(f[i]))).view(np.uint32)
+    return out
+
+
+@pytest.fixture(scope="module")
+def sample_and_want():
+    xb = sample_bits()
+    return xb, oracle_bits(xb)
+
+
+def test_fast_path_matches_oracle(host, sample_and_want):
+    xb, want = sample_and_want
+    got = np.empty_like(xb)
+    host.erff_cr_bits(xb, got, xb.size)
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, "first mismatch x=%08x got %08x want %08x" % (xb[bad[0]], got[bad[0]], want[bad[0]])
+
+
+def test_series_alone_matches_oracle(host, sample_and_want):
+    xb, want = sample_and_want
+    got = np.empty_like(xb)
+    host.erff_slow_bits(xb, got, xb.size)
+    bad = np.nonzero(got != want)[0]
+    assert bad.size == 0, "first mismatch x=%08x got %08x want %08x" % (xb[bad[0]], got[bad[0]], want[bad[0]])
+
+
+def test_nan_inf_zero(host):
+    xb = np.array([0x7FC00000, 0x7F800001, 0xFFA00000, 0x7F800000, 0xFF800000, 0, 0x80000000], dtype=np.uint32)
+    got = np.empty_like(xb)
+    host.erff_cr_bits(xb, got, xb.size)
+    assert list(got) == [0x7FC00000, 0x7FC00001, 0xFFE00000, 0x3F800000, 0xBF800000, 0, 0x80000000]
