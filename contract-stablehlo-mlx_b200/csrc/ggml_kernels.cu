@@ -61,7 +61,8 @@ static int require_dtype(Arr *a, int dt, const char *what) {
 // grouped as (v0+v1)+(v2+v3); then the tail of K mod 16 elements.
 //
 // The tree is a perfect binary tree whose leaves, left to right, are the
-// classes in bit-reversed order (0, 8, 4, 12, 1, 9, ...). The fast path packs
+// classes 0, 8, 4, 12, 1, 9, 5, 13, 2, 10, 6, 14, 3, 11, 7, 15: class j is
+// leaf 4*(j & 3) + r(j >> 2), with r the 2-bit reversal. The fast path packs
 // each operand k-major with its K reordered so that leaf s's class fills the
 // s-th contiguous segment of the packed K axis. Each class chain is then an
 // ordinary k-ascending register-tiled GEMM over one segment; at each segment
@@ -73,9 +74,14 @@ static int require_dtype(Arr *a, int dt, const char *what) {
 // product is -0 and acc + (-0) == acc for every acc (+0 stays +0, -0 stays -0),
 // so padding leaves every chain bit-identical.
 
-__host__ __device__ constexpr int bitrev4(int s) {
-  return ((s & 1) << 3) | ((s & 2) << 1) | ((s & 4) >> 1) | ((s & 8) >> 3);
+// The leaf of class j in the reduction tree.
+__host__ __device__ constexpr int leaf_of_class(int j) {
+  return 4 * (j & 3) + (((j >> 2) & 1) << 1 | ((j >> 3) & 1));
 }
+static_assert(leaf_of_class(0) == 0 && leaf_of_class(8) == 1 && leaf_of_class(4) == 2 && leaf_of_class(12) == 3 &&
+                  leaf_of_class(1) == 4 && leaf_of_class(9) == 5 && leaf_of_class(5) == 6 &&
+                  leaf_of_class(13) == 7 && leaf_of_class(2) == 8 && leaf_of_class(15) == 15,
+              "ggml_vec_dot_f32 reduction-tree leaf order");
 
 // One output, the reference's one-thread-per-output form; also the planted
 // `plain` fault (a sequential binary32 sum without fma, Shaders.lean:65-68).
@@ -152,7 +158,7 @@ __global__ void k_mm_pack(const float *__restrict__ src, int rows, int K, int64_
     int j = o >> 3, c = o & 7;
     int cg = c0 + c;
     if (cg >= segp) continue;
-    int kq = bitrev4(j) * segp + cg;
+    int kq = leaf_of_class(j) * segp + cg;
     float v = cg < seg ? tile[tx][16 * c + j] : pad;
     d[(int64_t)kq * rows_p + r0 + tx] = v;
   }

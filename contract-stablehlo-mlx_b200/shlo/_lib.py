@@ -27,7 +27,7 @@ c_arr = ctypes.c_void_p
 c_i64p = ctypes.POINTER(ctypes.c_int64)
 TRACE_FN = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.POINTER(c_arr), ctypes.c_int,
                             ctypes.POINTER(c_arr), ctypes.POINTER(ctypes.c_int), ctypes.c_int,
-                            ctypes.c_char_p, ctypes.c_size_t)
+                            ctypes.c_void_p, ctypes.c_size_t)
 FREE_FN = ctypes.CFUNCTYPE(None, ctypes.c_void_p)
 
 _lib = None

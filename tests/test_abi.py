@@ -55,3 +55,18 @@ def test_errors_are_reported_not_raised_as_faults():
         assert "not carried" in str(e)
     else:
         raise AssertionError("unknown kernel accepted")
+
+
+def test_traced_function_error_travels_back():
+    """A trace error comes back as the apply error (c/smlx_shim.c:337-349), no GPU needed."""
+    from shlo import mlx as M
+
+    def f(args):
+        raise M.ShloError("composite ggml.x: not carried")
+    fn = M.compile_(f, True)
+    try:
+        M.apply(fn, [M.empty_arr()])
+    except M.ShloError as e:
+        assert "traced function" in str(e) and "not carried" in str(e)
+    else:
+        raise AssertionError("error swallowed")
