@@ -1,0 +1,398 @@
+"""Benchmark: bit-exact motion-denoiser steps on B200, through the executor's
+C ABI (BASELINE.json metric; configuration 5).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch-per-gpu B] [--impl shlo|reference]
+
+One process per GPU (torchrun for N > 1). Each rank runs the whole 8-layer
+denoiser module on its own shard of the batch (weak scaling; there is no
+data-path collective: samples are independent). The control plane (barrier,
+max over ranks) is torch.distributed over gloo.
+
+value: sample-steps/s of the whole job with inputs already on the device, timed
+with CUDA events on the library's stream, max over ranks. e2e: the same through
+the public API with the inputs copied from pinned host memory every step and
+the step's output read back to the host. roofline: the dominant kernel
+(mul_mat, ggml_vec_dot_f32 order on FP32 CUDA cores) against the measured
+cuBLAS SGEMM throughput of this GPU. cpu_baseline / --impl reference: the C
+oracle (this repo's restatement of ggml-cpu's arm64 order) on the host cores.
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "contract-stablehlo-mlx_b200")
+for p in (ROOT, PKG):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+import numpy as np  # noqa: E402
+
+METRIC = "bit-exact denoiser steps/s"
+UNIT = "sample-steps/s"
+WORKLOAD = "8-layer motion denoiser, seq 256, d_model 512, 8 heads, FFN 2048 erf-GELU, timestep MLP (silu)"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--batch-per-gpu", type=int, default=64)
+    ap.add_argument("--layers", type=int, default=8)
+    ap.add_argument("--impl", default="shlo", choices=["shlo", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------- clocks ----
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.rows = []
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), "--query-gpu=" + self.FIELDS,
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                self.rows.append(parts)
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+
+        def num(x):
+            try:
+                return float(x)
+            except ValueError:
+                return None
+        sm = [num(r[1]) for r in self.rows if num(r[1])]
+        mx = [num(r[2]) for r in self.rows if num(r[2])]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in self.rows for i in range(4) if r[5 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows),
+                "power_w_max": max([num(r[3]) or 0 for r in self.rows])}
+
+
+# ------------------------------------------------------------ distributed ----
+
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if ws <= 1:
+        return 0, 0, 1, None
+    import torch.distributed as dist
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    return dist.get_rank(), int(os.environ.get("LOCAL_RANK", "0")), ws, dist
+
+
+def all_max(dist, v: float) -> float:
+    if dist is None:
+        return v
+    import torch
+    t = torch.tensor([v], dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(dist):
+    if dist is not None:
+        dist.barrier()
+
+
+# -------------------------------------------------------------- peaks ----
+
+def fp32_peak_tflops(device: int) -> float:
+    """cuBLAS SGEMM (no TF32) throughput of this GPU, best of several 8192^3."""
+    import torch
+    torch.backends.cuda.matmul.allow_tf32 = False
+    torch.backends.cudnn.allow_tf32 = False
+    dev = torch.device("cuda", device)
+    n = 8192
+    a = torch.randn(n, n, device=dev)
+    b = torch.randn(n, n, device=dev)
+    for _ in range(2):
+        torch.matmul(a, b)
+    torch.cuda.synchronize(dev)
+    best = 0.0
+    for _ in range(5):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        torch.matmul(a, b)
+        e.record()
+        e.synchronize()
+        best = max(best, 2 * n ** 3 / (s.elapsed_time(e) * 1e-3) / 1e12)
+    del a, b
+    torch.cuda.empty_cache()
+    return best
+
+
+def measured_peaks() -> dict:
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            return json.load(f)
+    except Exception:
+        return {}
+
+
+def profile_traffic(name: str):
+    """dram bytes per launch from a committed ncu summary (profiles/<name>), or None."""
+    path = os.path.join(ROOT, "profiles", name)
+    try:
+        for line in open(path):
+            if line.startswith("dram_bytes_per_launch:"):
+                return float(line.split(":", 1)[1].split()[0])
+    except OSError:
+        pass
+    return None
+
+
+# ------------------------------------------------------------ our arm ----
+
+class EventTimer:
+    """CUDA events recorded on the library's own stream."""
+
+    def __init__(self, stream_ptr: int, device: int):
+        import torch
+        self.torch = torch
+        self.stream = torch.cuda.ExternalStream(stream_ptr, device=torch.device("cuda", device))
+
+    def time(self, fn, n: int) -> float:
+        t = self.torch
+        s, e = t.cuda.Event(enable_timing=True), t.cuda.Event(enable_timing=True)
+        s.record(self.stream)
+        for _ in range(n):
+            fn()
+        e.record(self.stream)
+        e.synchronize()
+        return s.elapsed_time(e) / 1e3  # seconds
+
+
+def run_shlo(args):
+    rank, local_rank, ws, dist = dist_init()
+    import torch
+
+    import shlo  # noqa: F401  (loads libshlo_cuda)
+    from shlo import denoiser as D
+    from shlo import exec as E
+    from shlo import mlx as M
+    from shlo import run as Run
+
+    torch.cuda.set_device(local_rank)
+    M.set_device(local_rank)
+    M.set_flavor("pinned")
+    cfg = D.Config(layers=args.layers)
+    B = args.batch_per_gpu
+    w = D.init_weights(cfg, seed=1)
+    ins = D.inputs(cfg, B, seed=1 + rank)
+    W = [M.of_numpy(w[n]) for n, _ in D.weight_specs(cfg)]
+    X = [M.of_numpy(a) for a in ins]
+    fn = E.prepare(E.load(D.module_text(cfg, B)), None, True)
+    timer = EventTimer(M.current_stream(), local_rank)
+
+    def step():
+        return M.apply(fn, X + W)[0]
+
+    out = None
+    for _ in range(max(args.warmup, 1)):
+        out = step()
+    M.eval_([out])
+    first = M.to_numpy(out)
+    out = None
+
+    # ---- value: device-resident inputs, K steps, CUDA events, max over ranks
+    holder = []
+    barrier(dist)
+    torch.cuda.synchronize()
+    launches0 = M.launch_count()
+    with Clocks(local_rank) as clk:
+        dt = timer.time(lambda: holder.__setitem__(slice(None), [step()]), args.steps)
+    launches = M.launch_count() - launches0
+    last = M.to_numpy(holder[-1])
+    holder.clear()
+    torch.cuda.synchronize()
+    barrier(dist)
+    dt_max = all_max(dist, dt)
+    deterministic = bool(np.array_equal(first.view(np.uint32), last.view(np.uint32)))
+
+    # ---- e2e: pinned host inputs copied in, output read back, every step
+    pinned_in = [torch.from_numpy(a).pin_memory() for a in ins]
+    pinned_out = torch.empty(first.shape, dtype=torch.float32).pin_memory()
+    h2d = sum(a.numel() * 4 for a in pinned_in)
+    d2h = pinned_out.numel() * 4
+    barrier(dist)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        xs = [M.of_ptr(p.data_ptr(), p.numel() * 4, list(p.shape), M.dtF32) for p in pinned_in]
+        o = M.apply(fn, xs + W)[0]
+        M.to_ptr(o, pinned_out.data_ptr(), d2h)
+    e2e_dt = all_max(dist, time.perf_counter() - t0)
+    barrier(dist)
+
+    # ---- the dominant kernel: mul_mat at the layer's four weight shapes
+    R = B * cfg.seq
+    rng = np.random.default_rng(0)
+    shapes = [(cfg.d, 3 * cfg.d), (cfg.d, cfg.d), (cfg.d, cfg.ffn), (cfg.ffn, cfg.d)]
+    mm_flops, mm_time, mm_launches = 0.0, 0.0, 0
+    per_shape = {}
+    for K, Mm in shapes:
+        wa = M.of_numpy(rng.standard_normal((Mm, K)).astype(np.float32))
+        xa = M.of_numpy(rng.standard_normal((R, K)).astype(np.float32))
+        for _ in range(3):
+            y = Run.mul_mat(wa, xa, K, Mm, R, R, 0)
+        M.eval_([y])
+        n = 20
+        t = timer.time(lambda: Run.mul_mat(wa, xa, K, Mm, R, R, 0), n)
+        mm_flops += 2.0 * K * Mm * R * n
+        mm_time += t
+        mm_launches += n
+        per_shape["%dx%dx%d" % (R, Mm, K)] = round(2.0 * K * Mm * R / (t / n) / 1e12, 2)
+    mm_tflops = mm_flops / mm_time / 1e12
+    # dot_general config 1: [64,256] x [256,128]
+    w1 = M.of_numpy(rng.standard_normal((128, 256)).astype(np.float32))
+    x1 = M.of_numpy(rng.standard_normal((64, 256)).astype(np.float32))
+    for _ in range(5):
+        Run.mul_mat(w1, x1, 256, 128, 64, 64, 0)
+    n1 = 200
+    t1 = timer.time(lambda: Run.mul_mat(w1, x1, 256, 128, 64, 64, 0), n1)
+    cfg1_tflops = 2.0 * 64 * 128 * 256 / (t1 / n1) / 1e12
+
+    peak_sgemm = fp32_peak_tflops(local_rank)
+    sm_count = torch.cuda.get_device_properties(local_rank).multi_processor_count
+    clocks = clk.summary()
+    nominal = sm_count * 128 * 2 * (clocks.get("sm_max_mhz") or 1965.0) * 1e6 / 1e12
+
+    if rank != 0:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
+
+    # ---- CPU baseline (rank 0, N = 1): the oracle on one sample, all host cores
+    cpu = None
+    exact0 = None
+    if ws == 1 and not args.no_cpu_baseline:
+        from oracle import model_oracle as MO
+        cores = os.cpu_count() or 1
+        t = time.perf_counter()
+        ref0 = MO.forward(cfg, w, [a[:1] for a in ins], nthreads=cores)
+        cdt = time.perf_counter() - t
+        exact0 = bool(np.array_equal(ref0.view(np.uint32), first[:1].view(np.uint32)))
+        cpu = {"value": round(1.0 / cdt, 4), "unit": UNIT, "cores": cores, "kind": "port",
+               "sample": "one sample (batch 1) through all %d layers on the C oracle, rows split over %d host threads; "
+                         "%.1f s" % (cfg.layers, cores, cdt)}
+
+    value = ws * B * args.steps / dt_max
+    flops_step = cfg.flops_per_sample() * B
+    line = {
+        "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt_max / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded N(0,1) noisy inputs and host sinusoid timestep embeddings, N(0,0.02) random-init weights",
+        "config": {"workload": WORKLOAD, "global_batch": ws * B, "batch_per_gpu": B, "seq_len": cfg.seq,
+                   "layers": cfg.layers, "parallelism": "dp%d (independent batch shards, no collective)" % ws,
+                   "l2": "no flush: per-step working set (100 MB weights + >1 GB activations at batch 64) exceeds the 126 MB L2",
+                   "ggml_build": "pinned"},
+        "model_tflops": round(flops_step * args.steps * ws / dt_max / 1e12, 2),
+        "roofline": {"bound": "fp32-cuda-core", "kernel": "mul_mat (pack + k_mul_mat_fast)",
+                     "achieved": round(mm_tflops, 2), "peak": round(peak_sgemm, 2), "unit": "TFLOP/s",
+                     "frac": round(mm_tflops / peak_sgemm, 3),
+                     "peak_source": "measured cuBLAS SGEMM (TF32 off), 8192^3, this GPU, this run",
+                     "peak_nominal": round(nominal, 1), "frac_of_nominal": round(mm_tflops / nominal, 3),
+                     "per_shape": per_shape,
+                     "traffic": profile_traffic("mul_mat_denoiser_ffn1.txt")},
+        "dot_general": {"config1_64x256x128_tflops": round(cfg1_tflops, 4),
+                        "config1_us_per_call": round(t1 / n1 * 1e6, 2),
+                        "denoiser_shapes_tflops": round(mm_tflops, 2)},
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(ws * B * args.steps / e2e_dt, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h},
+        "gpu_launches": int(launches),
+        "clocks": clocks,
+        "bit_exact": {"sample0_vs_oracle": exact0, "deterministic_across_steps": deterministic},
+        "hbm_gbs_measured": measured_peaks().get("hbm_gbs"),
+    }
+    print(json.dumps(line), flush=True)
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ------------------------------------------------------ the reference arm ----
+
+def run_reference(args):
+    """The reference's CPU path for this workload: the C oracle (ggml-cpu's arm64
+    order restated; the reference's own ggml_ref cannot be built here), one
+    sample per step through all layers, rows split over every host thread."""
+    if int(os.environ.get("RANK", "0")) != 0:
+        return
+    from oracle import model_oracle as MO
+    from shlo import denoiser as D
+
+    cfg = D.Config(layers=args.layers)
+    w = D.init_weights(cfg, seed=1)
+    ins = D.inputs(cfg, 1, seed=1)
+    cores = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        MO.forward(cfg, w, ins, nthreads=cores)
+    t = time.perf_counter()
+    for _ in range(args.steps):
+        MO.forward(cfg, w, ins, nthreads=cores)
+    dt = time.perf_counter() - t
+    v = args.steps / dt
+    line = {"metric": METRIC, "value": round(v, 4), "unit": UNIT, "impl": "reference", "n_gpus": 0,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 1),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic", "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": cfg.seq,
+                                            "layers": cfg.layers, "parallelism": "host threads"},
+            "cpu_baseline": {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": "each step: one sample through all %d layers on the C oracle" % cfg.layers},
+            "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_shlo(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -15,6 +15,11 @@ namespace shlo {
 __device__ __forceinline__ uint32_t fbits(float f) { return __float_as_uint(f); }
 __device__ __forceinline__ float bitsf(uint32_t u) { return __uint_as_float(u); }
 
+// arm64's default NaN, what an invalid operation (inf*0, inf-inf, 0/0) gives
+// there (FPCR.DN clear produces it for invalid operations; the GPU's own NaN is
+// 0x7FFFFFFF). The reductions return it for every NaN result.
+__device__ __forceinline__ float arm_nan(float v) { return v != v ? __uint_as_float(0x7FC00000u) : v; }
+
 // ggml_v_expf, one lane (StablehloMlx/Kernels/Math.lean:28-49): ggml-cpu's NEON
 // exp ("adapted from arm limited optimized routine"), with vfmaq_f32(a, b, c)
 // = fma(b, c, a) and vfmsq_f32(a, b, c) = fma(-b, c, a).
@@ -109,7 +114,7 @@ __global__ void k_mul_mat_naive(const float *__restrict__ w, const float *__rest
     if (plain) {
       float s = 0.0f;
       for (int i = 0; i < K; i++) s = __fadd_rn(s, __fmul_rn(wr[i], xr[i]));
-      y[t] = s;
+      y[t] = arm_nan(s);
       continue;
     }
     float a[16];
@@ -127,7 +132,7 @@ __global__ void k_mul_mat_naive(const float *__restrict__ w, const float *__rest
 #pragma unroll
     for (int l = 0; l < 4; l++) a[l] = __fadd_rn(a[l], a[4 + l]);
     float sumf = __fadd_rn(__fadd_rn(a[0], a[1]), __fadd_rn(a[2], a[3]));
-    y[t] = dot_tail(wr, xr, np, K, sumf, flavor);
+    y[t] = arm_nan(dot_tail(wr, xr, np, K, sumf, flavor));
   }
 }
 
@@ -329,7 +334,7 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mul_mat_fast(MMArgs a) {
         const float *xr = a.x + r * a.K;
         v = dot_tail(wr, xr, a.np, a.K, v, a.flavor);
       }
-      a.y[r * a.M + m] = v;
+      a.y[r * a.M + m] = arm_nan(v);
     }
   }
 }
@@ -570,14 +575,16 @@ __global__ void g_soft_max(const float *__restrict__ x, float *__restrict__ y, i
         int gi = lane + 32 * i;
         if (gi < ng) {
           float4 e = v[i];
-          e.x = __fmul_rn(e.x, inv); e.y = __fmul_rn(e.y, inv); e.z = __fmul_rn(e.z, inv); e.w = __fmul_rn(e.w, inv);
+          e.x = arm_nan(__fmul_rn(e.x, inv)); e.y = arm_nan(__fmul_rn(e.y, inv));
+          e.z = arm_nan(__fmul_rn(e.z, inv)); e.w = arm_nan(__fmul_rn(e.w, inv));
           yr[gi] = e;
         }
       }
     } else {
       for (int gi = lane; gi < ng; gi += 32) {
         float4 e = yr[gi];
-        e.x = __fmul_rn(e.x, inv); e.y = __fmul_rn(e.y, inv); e.z = __fmul_rn(e.z, inv); e.w = __fmul_rn(e.w, inv);
+        e.x = arm_nan(__fmul_rn(e.x, inv)); e.y = arm_nan(__fmul_rn(e.y, inv));
+        e.z = arm_nan(__fmul_rn(e.z, inv)); e.w = arm_nan(__fmul_rn(e.w, inv));
         yr[gi] = e;
       }
     }
@@ -696,14 +703,14 @@ __global__ void g_norm(const float *__restrict__ x, float *__restrict__ y, int n
       scl = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
     }
     for (int c0 = 0; c0 < ncols; c0 += 32) {
-      if (c0 + lane >= ncols) continue;
 #pragma unroll 8
       for (int rr = 0; rr < 32; rr++) {
+        // every lane takes part in the shuffles; only the store is predicated
         float m = __shfl_sync(0xffffffffu, mean, rr);
         float s = __shfl_sync(0xffffffffu, scl, rr);
-        if (rr < nr) {
+        if (rr < nr && c0 + lane < ncols) {
           int64_t i = (r0 + rr) * ncols + c0 + lane;
-          y[i] = __fmul_rn(__fsub_rn(x[i], m), s);
+          y[i] = arm_nan(__fmul_rn(__fsub_rn(x[i], m), s));
         }
       }
     }
@@ -741,8 +748,17 @@ __global__ void g_silu(const float *__restrict__ x, float *__restrict__ y, int64
   int64_t stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
     float v = x[i];
-    if (gpu_ops) y[i] = __fdividef(v, __fadd_rn(1.0f, __expf(-v)));
-    else y[i] = __fdiv_rn(v, __fadd_rn(1.0f, ggml_v_expf(__fsub_rn(0.0f, v))));
+    if (gpu_ops) {
+      y[i] = __fdividef(v, __fadd_rn(1.0f, __expf(-v)));
+      continue;
+    }
+    float r = __fdiv_rn(v, __fadd_rn(1.0f, ggml_v_expf(__fsub_rn(0.0f, v))));
+    // arm64: a NaN input comes back quieted (every step passes it through); an
+    // invalid division (-inf / inf) gives the default NaN.
+    uint32_t b = fbits(v);
+    if ((b & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(b | 0x00400000u);
+    else if (r != r) r = bitsf(0x7FC00000u);
+    y[i] = r;
   }
 }
 
@@ -764,6 +780,7 @@ __global__ void g_gelu_erf(const float *__restrict__ x, float *__restrict__ y, i
     float r = __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, ev));
     uint32_t b = fbits(v);
     if ((b & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(b | 0x00400000u);
+    else if (r != r) r = bitsf(0x7FC00000u);  // -inf * 0: arm64's default NaN
     y[i] = r;
   }
 }

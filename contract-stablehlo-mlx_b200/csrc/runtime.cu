@@ -33,7 +33,12 @@ int cuda_check(cudaError_t e, const char *what) {
   return fail("%s: CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
 }
 
-int launch_check(const char *what) { return cuda_check(cudaGetLastError(), what); }
+static std::atomic<uint64_t> g_launches{0};
+
+int launch_check(const char *what) {
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return cuda_check(cudaGetLastError(), what);
+}
 
 // ---------------------------------------------------------------- dtypes ----
 
@@ -397,6 +402,18 @@ int shlo_set_flavor(int flavor) {
 
 int shlo_get_flavor(int *flavor) {
   *flavor = current_flavor();
+  return 0;
+}
+
+int shlo_current_stream(void **stream) {
+  Device *d;
+  SHLO_TRY(current_device(&d));
+  *stream = (void *)d->stream;
+  return 0;
+}
+
+int shlo_launch_count(uint64_t *count) {
+  *count = g_launches.load();
   return 0;
 }
 

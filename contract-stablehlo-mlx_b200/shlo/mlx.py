@@ -86,6 +86,16 @@ def of_numpy(a: np.ndarray, dt: int | None = None) -> Arr:
     return Arr(o.value)
 
 
+def of_ptr(ptr: int, nbytes: int, shape_: Sequence[int], dt: int) -> Arr:
+    """ofBytes from raw host memory (e.g. a pinned buffer)."""
+    return _out(load().shlo_of_bytes, ctypes.c_void_p(ptr), nbytes, _i64(shape_), len(shape_), dt)
+
+
+def to_ptr(a: Arr, ptr: int, cap: int) -> None:
+    """toBytes into raw host memory."""
+    check(load().shlo_to_bytes(a.h, ctypes.c_void_p(ptr), cap))
+
+
 def to_bytes(a: Arr) -> bytes:
     L = load()
     n = ctypes.c_size_t()
@@ -295,6 +305,19 @@ def device_count() -> int:
     n = ctypes.c_int()
     check(load().shlo_device_count(ctypes.byref(n)))
     return n.value
+
+
+def current_stream() -> int:
+    """The cudaStream_t (as an integer) the current device's work is queued on."""
+    s = ctypes.c_void_p()
+    check(load().shlo_current_stream(ctypes.byref(s)))
+    return s.value or 0
+
+
+def launch_count() -> int:
+    c = ctypes.c_uint64()
+    check(load().shlo_launch_count(ctypes.byref(c)))
+    return c.value
 
 
 def set_flavor(flavor: str) -> None:

@@ -154,6 +154,14 @@ void shlo_fn_free(shlo_fn f);
 int shlo_apply(shlo_fn f, const shlo_arr *inputs, int n_inputs, shlo_arr *outputs,
                int *n_outputs, int max_outputs);
 
+/* ---- measurement hooks (no counterpart in the reference: its shim has no timing) ---- */
+
+/* The CUDA stream (a cudaStream_t) on which all work of this thread's current
+   device is queued, for timing with CUDA events on the launching stream. */
+int shlo_current_stream(void **stream);
+/* How many kernels this library has launched since it was loaded, all devices. */
+int shlo_launch_count(uint64_t *count);
+
 /* ---- test-driver helpers (Mlx.lean:69-73) ---- */
 
 /* smlx_libm_erff_range: this platform's binary32 erff over `count`

@@ -13,6 +13,10 @@
 
 static inline uint32_t fbits(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
 static inline float bitsf(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+/* arm64's default NaN: what an invalid operation (inf*0, inf-inf, 0/0) gives on
+   the reference's CPU (x86 would give 0xFFC00000). Results of the reductions
+   that are NaN are reported as this value. */
+static inline float arm_nan(float v) { return v != v ? bitsf(0x7FC00000u) : v; }
 
 /* ---- input streams: ref/ggml_ref.c:21-30 ---------------------------------- */
 
@@ -164,7 +168,7 @@ static void mm_rows(void *p, long r0, long r1) {
 		const float *wb = c->w + (r / c->N) * c->wbs;
 		const float *xr = c->x + r * (long)c->K;
 		for (int m = 0; m < c->M; m++)
-			c->y[r * (long)c->M + m] = dot_ggml(wb + (long)m * c->K, xr, c->K, c->flavour);
+			c->y[r * (long)c->M + m] = arm_nan(dot_ggml(wb + (long)m * c->K, xr, c->K, c->flavour));
 	}
 }
 
@@ -204,7 +208,7 @@ static void sm_rows(void *p, long r0, long r1) {
 			y[i] = v;
 		}
 		float inv = (float)(1.0 / sum);
-		for (int k = 0; k < n; k++) y[k] = y[k] * inv;
+		for (int k = 0; k < n; k++) y[k] = arm_nan(y[k] * inv);
 	}
 	free(wv);
 }
@@ -235,7 +239,7 @@ static void nm_rows(void *p, long r0, long r1) {
 		for (; i < n; i++) { float d = x[i] - mean; float q = d * d; s2 += (double)q; }
 		float var = (float)(s2 / (double)n);
 		float scl = 1.0f / sqrtf(var + c->eps);
-		for (int k = 0; k < n; k++) y[k] = (x[k] - mean) * scl;
+		for (int k = 0; k < n; k++) y[k] = arm_nan((x[k] - mean) * scl);
 	}
 }
 void orc_norm(const float *x, float *y, int ncols, int rows, float eps, int nthreads) {
@@ -246,14 +250,21 @@ void orc_norm(const float *x, float *y, int ncols, int rows, float eps, int nthr
 /* ---- silu: Shaders.lean:172-179 (ggml_vec_silu_f32: x / (1 + ggml_v_expf(0 - x))
  * on the four-lane body of each row; the row tail is x / (1 + expf(-x)) with
  * the correctly rounded expf). */
+/* arm64's NaN rules for silu: a NaN input passes through every step quieted;
+   an invalid division (-inf / inf) gives the default NaN. */
+static float silu_nan(float x, float r) {
+	uint32_t b = fbits(x);
+	if ((b & 0x7FFFFFFFu) > 0x7F800000u) return bitsf(b | 0x00400000u);
+	return arm_nan(r);
+}
 void orc_silu(const float *x, float *y, int ncols, int rows) {
 	for (long r = 0; r < rows; r++) {
 		const float *xr = x + r * (long)ncols;
 		float *yr = y + r * (long)ncols;
 		int i = 0;
 		for (; i + 3 < ncols; i += 4)
-			for (int l = 0; l < 4; l++) yr[i + l] = xr[i + l] / (1.0f + orc_ggml_v_expf(0.0f - xr[i + l]));
-		for (; i < ncols; i++) yr[i] = xr[i] / (1.0f + orc_expf_cr(-xr[i]));
+			for (int l = 0; l < 4; l++) yr[i + l] = silu_nan(xr[i + l], xr[i + l] / (1.0f + orc_ggml_v_expf(0.0f - xr[i + l])));
+		for (; i < ncols; i++) yr[i] = silu_nan(xr[i], xr[i] / (1.0f + orc_expf_cr(-xr[i])));
 	}
 }
 
@@ -261,7 +272,7 @@ void orc_silu(const float *x, float *y, int ncols, int rows) {
 static float gelu_one(float x) {
 	uint32_t b = fbits(x);
 	if ((b & 0x7FFFFFFFu) > 0x7F800000u) return bitsf(b | 0x00400000u);
-	return (0.5f * x) * (1.0f + orc_erff_cr(x * bitsf(0x3F3504F3)));
+	return arm_nan((0.5f * x) * (1.0f + orc_erff_cr(x * bitsf(0x3F3504F3))));
 }
 struct ge_ctx { const float *x; float *y; };
 static void ge_rows(void *p, long r0, long r1) {

@@ -70,17 +70,15 @@ def test_mul_mat_signed_zeros_and_specials(path, monkeypatch):
     tiny = rng.random(w.shape) < 0.1
     w[tiny] = np.float32(-1e-30)
     x[:, :7] = np.float32(1e-20)
-    w[5, :] = -0.0
-    x[7, :] = 0.0
+    w[5, :] = np.float32(-1e-30)  # every product of row 5 and input 7 rounds to -0: the output is -0
+    x[7, :] = np.float32(1e-30)
     w[9, 3] = np.inf
     x[11, 40] = -np.inf
     got = M.to_numpy(Run.mul_mat(M.of_numpy(w), M.of_numpy(x), K, Mm, R, R, 0))
     want = O.mul_mat(w, x, K, Mm, R, R, 0, O.PINNED)
-    g, wnt = bits(got), bits(want)
-    nan = np.isnan(want.reshape(-1))
-    assert np.array_equal(np.isnan(got.reshape(-1)), nan)
-    assert np.array_equal(g[~nan], wnt[~nan])
-    assert np.count_nonzero(g == 0x80000000) > 0  # some outputs are -0
+    assert_bits(got, want, "mul_mat specials")  # invalid products give arm64's default NaN in both
+    assert np.count_nonzero(bits(got) == 0x80000000) > 0  # some outputs are -0
+    assert np.count_nonzero(np.isnan(got)) > 0
 
 
 def softmax_config2(seed=0):
@@ -144,14 +142,10 @@ def specials32(n=1 << 16, seed=1):
 
 def test_silu_and_gelu():
     xb = specials32()
-    ok = (xb & 0x7FFFFFFF) <= 0x7F800000  # silu: NaN outputs are canonical on the GPU (as in the reference's Metal kernel)
-    x = xb[ok].view(np.float32)
+    x = xb.view(np.float32)
     x = x[: (x.size // 4) * 4]
     got = M.to_numpy(Run.silu(M.of_numpy(x), x.size))
-    want = O.silu(x, x.size, 1)
-    nan = np.isnan(want)
-    assert np.array_equal(np.isnan(got), nan)
-    assert_bits(got[~nan], want[~nan], "silu")
+    assert_bits(got, O.silu(x, x.size, 1), "silu")
     xg = xb.view(np.float32)
     got = M.to_numpy(Run.gelu_erf(M.of_numpy(xg), xg.size))
     want = O.gelu_erf(xg)

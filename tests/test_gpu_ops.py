@@ -82,7 +82,14 @@ def test_case_pinned(oc, path, pins, monkeypatch):
             pytest.fail("%s [%s]: %s" % (oc.name, "compiled" if compile else "uncompiled",
                                          first_diff(got, G.oracle_output(c, inputs, O.PINNED))))
     if path == "auto":
-        st, got = run_module(text, ins, oc.fault, True)
+        fault = oc.fault
+        if fault.dotPlain and c.extra["K"] < 16:
+            # In the pinned build ggml's tail is a separate multiply and add, so for
+            # K < 16 the planted sequential sum (written against the stock build's
+            # fmaf tail, Tests/OpTests.lean:121) is ggml's own order: plant the
+            # built-in matmul instead.
+            fault = L.Faults(dotBuiltin=True)
+        st, got = run_module(text, ins, fault, True)
         if st == "ok":
             assert hashlib.sha256(got).hexdigest() != want, "planted fault (%s) not caught" % oc.fault_name
 
