@@ -1,0 +1,337 @@
+/*
+ * The Lean side of the boundary: the 25 `smlx_*` symbols that
+ * StablehloMlx/Mlx.lean:16-73 declares with @[extern], over the plain C ABI of
+ * include/shlo_cuda.h. This file takes the place of the reference's
+ * c/smlx_shim.c in the Lean build (lakefile.lean:23-31); it unpacks Lean
+ * objects, makes one shlo_* call, and boxes the result -- no numerics here.
+ *
+ * Build (where Lean 4 is installed): compile with the Lean include path and
+ * link against libshlo_cuda.so, e.g.
+ *   cc -O2 -fPIC -I$(lean --print-prefix)/include -Iinclude -c shlo_cuda_lean.c
+ */
+#include <lean/lean.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "../../include/shlo_cuda.h"
+
+/* IO.Error.toString, exported by the Lean runtime. */
+extern lean_object *lean_io_error_to_string(lean_object *err);
+
+static lean_obj_res io_err(const char *what) {
+	char b[4400];
+	snprintf(b, sizeof b, "%s: %s", what, shlo_last_error());
+	return lean_io_result_mk_error(lean_mk_io_user_error(lean_mk_string(b)));
+}
+
+/* ---- external classes: Arr, Kernel, Fn ---- */
+
+static void noop_foreach(void *p, b_lean_obj_arg f) { (void)p; (void)f; }
+static void arr_finalize(void *p) { shlo_release((shlo_arr)p); }
+static void kern_finalize(void *p) { shlo_kernel_free((shlo_kernel)p); }
+static void fn_finalize(void *p) { shlo_fn_free((shlo_fn)p); }
+static lean_external_class *arr_class, *kern_class, *fn_class;
+
+static lean_object *box_arr(shlo_arr a) {
+	if (!arr_class) arr_class = lean_register_external_class(arr_finalize, noop_foreach);
+	return lean_alloc_external(arr_class, a);
+}
+static shlo_arr unbox_arr(b_lean_obj_arg o) { return (shlo_arr)lean_get_external_data(o); }
+
+static int shape_of(b_lean_obj_arg arr, int64_t *out, int max) {
+	size_t n = lean_array_size(arr);
+	if ((int)n > max) return -1;
+	for (size_t i = 0; i < n; i++) out[i] = (int64_t)lean_unbox(lean_array_get_core(arr, i));
+	return (int)n;
+}
+
+static lean_obj_res ok_arr(int rc, shlo_arr r, const char *what) {
+	if (rc) return io_err(what);
+	return lean_io_result_mk_ok(box_arr(r));
+}
+
+static lean_object *shape_to_lean(const int64_t *s, int n) {
+	lean_object *r = lean_alloc_array(0, (size_t)n);
+	for (int i = 0; i < n; i++) r = lean_array_push(r, lean_box((size_t)s[i]));
+	return r;
+}
+
+/* ---- construction and readback (Mlx.lean:16, 39-42) ---- */
+
+LEAN_EXPORT lean_obj_res smlx_empty(lean_obj_arg u) {
+	(void)u;
+	return box_arr(shlo_empty());
+}
+
+LEAN_EXPORT lean_obj_res smlx_of_bytes(b_lean_obj_arg data, b_lean_obj_arg shape, uint8_t dt, lean_obj_arg w) {
+	(void)w;
+	int64_t s[SHLO_MAX_RANK];
+	int n = shape_of(shape, s, SHLO_MAX_RANK);
+	if (n < 0) return io_err("ofBytes: rank above 16");
+	shlo_arr r = NULL;
+	int rc = shlo_of_bytes(lean_sarray_cptr(data), lean_sarray_size(data), s, n, dt, &r);
+	return ok_arr(rc, r, "ofBytes");
+}
+
+LEAN_EXPORT lean_obj_res smlx_to_bytes(b_lean_obj_arg a, lean_obj_arg w) {
+	(void)w;
+	size_t bytes = 0;
+	if (shlo_nbytes(unbox_arr(a), &bytes)) return io_err("toBytes");
+	lean_object *r = lean_alloc_sarray(1, bytes, bytes);
+	if (shlo_to_bytes(unbox_arr(a), lean_sarray_cptr(r), bytes)) {
+		lean_dec(r);
+		return io_err("toBytes");
+	}
+	return lean_io_result_mk_ok(r);
+}
+
+LEAN_EXPORT lean_obj_res smlx_shape(b_lean_obj_arg a, lean_obj_arg w) {
+	(void)w;
+	int64_t s[SHLO_MAX_RANK];
+	int n = 0;
+	if (shlo_shape(unbox_arr(a), s, &n)) return io_err("shape");
+	return lean_io_result_mk_ok(shape_to_lean(s, n));
+}
+
+LEAN_EXPORT lean_obj_res smlx_dtype(b_lean_obj_arg a, lean_obj_arg w) {
+	(void)w;
+	uint8_t d = 0;
+	if (shlo_dtype(unbox_arr(a), &d)) return io_err("dtype");
+	return lean_io_result_mk_ok(lean_box((size_t)d));
+}
+
+/* ---- ops (Mlx.lean:44-58) ---- */
+
+LEAN_EXPORT lean_obj_res smlx_unary(uint32_t op, b_lean_obj_arg a, lean_obj_arg w) {
+	(void)w;
+	shlo_arr r = NULL;
+	return ok_arr(shlo_unary(op, unbox_arr(a), &r), r, "unary");
+}
+
+LEAN_EXPORT lean_obj_res smlx_binary(uint32_t op, b_lean_obj_arg a, b_lean_obj_arg b, lean_obj_arg w) {
+	(void)w;
+	shlo_arr r = NULL;
+	return ok_arr(shlo_binary(op, unbox_arr(a), unbox_arr(b), &r), r, "binary");
+}
+
+LEAN_EXPORT lean_obj_res smlx_where(b_lean_obj_arg c, b_lean_obj_arg a, b_lean_obj_arg b, lean_obj_arg w) {
+	(void)w;
+	shlo_arr r = NULL;
+	return ok_arr(shlo_where(unbox_arr(c), unbox_arr(a), unbox_arr(b), &r), r, "where");
+}
+
+#define SHAPE_OP(NAME, CALL, WHAT)                                                   \
+	LEAN_EXPORT lean_obj_res NAME(b_lean_obj_arg a, b_lean_obj_arg shape, lean_obj_arg w) { \
+		(void)w;                                                                     \
+		int64_t s[SHLO_MAX_RANK];                                                    \
+		int n = shape_of(shape, s, SHLO_MAX_RANK);                                   \
+		if (n < 0) return io_err(WHAT ": rank above 16");                            \
+		shlo_arr r = NULL;                                                           \
+		return ok_arr(CALL(unbox_arr(a), s, n, &r), r, WHAT);                        \
+	}
+SHAPE_OP(smlx_reshape, shlo_reshape, "reshape")
+SHAPE_OP(smlx_transpose, shlo_transpose, "transpose")
+SHAPE_OP(smlx_broadcast, shlo_broadcast, "broadcast")
+
+LEAN_EXPORT lean_obj_res smlx_slice(b_lean_obj_arg a, b_lean_obj_arg start, b_lean_obj_arg stop, b_lean_obj_arg step,
+                                    lean_obj_arg w) {
+	(void)w;
+	int64_t s0[SHLO_MAX_RANK], s1[SHLO_MAX_RANK], s2[SHLO_MAX_RANK];
+	int n = shape_of(start, s0, SHLO_MAX_RANK), m = shape_of(stop, s1, SHLO_MAX_RANK), k = shape_of(step, s2, SHLO_MAX_RANK);
+	if (n < 0 || n != m || n != k) return io_err("slice");
+	shlo_arr r = NULL;
+	return ok_arr(shlo_slice(unbox_arr(a), s0, s1, s2, n, &r), r, "slice");
+}
+
+LEAN_EXPORT lean_obj_res smlx_concat(b_lean_obj_arg xs, uint32_t axis, lean_obj_arg w) {
+	(void)w;
+	size_t n = lean_array_size(xs);
+	shlo_arr *v = (shlo_arr *)malloc(sizeof(shlo_arr) * (n ? n : 1));
+	for (size_t i = 0; i < n; i++) v[i] = unbox_arr(lean_array_get_core(xs, i));
+	shlo_arr r = NULL;
+	int rc = shlo_concat(v, (int)n, axis, &r);
+	free(v);
+	return ok_arr(rc, r, "concatenate");
+}
+
+LEAN_EXPORT lean_obj_res smlx_astype(b_lean_obj_arg a, uint8_t dt, lean_obj_arg w) {
+	(void)w;
+	shlo_arr r = NULL;
+	return ok_arr(shlo_astype(unbox_arr(a), dt, &r), r, "astype");
+}
+
+LEAN_EXPORT lean_obj_res smlx_view(b_lean_obj_arg a, uint8_t dt, lean_obj_arg w) {
+	(void)w;
+	shlo_arr r = NULL;
+	return ok_arr(shlo_view(unbox_arr(a), dt, &r), r, "view");
+}
+
+LEAN_EXPORT lean_obj_res smlx_take(b_lean_obj_arg a, b_lean_obj_arg idx, uint32_t axis, lean_obj_arg w) {
+	(void)w;
+	shlo_arr r = NULL;
+	return ok_arr(shlo_take(unbox_arr(a), unbox_arr(idx), axis, &r), r, "take");
+}
+
+LEAN_EXPORT lean_obj_res smlx_max_axis(b_lean_obj_arg a, uint32_t axis, lean_obj_arg w) {
+	(void)w;
+	shlo_arr r = NULL;
+	return ok_arr(shlo_max_axis(unbox_arr(a), axis, &r), r, "max_axis");
+}
+
+LEAN_EXPORT lean_obj_res smlx_contiguous(b_lean_obj_arg a, lean_obj_arg w) {
+	(void)w;
+	shlo_arr r = NULL;
+	return ok_arr(shlo_contiguous(unbox_arr(a), &r), r, "contiguous");
+}
+
+LEAN_EXPORT lean_obj_res smlx_eval(b_lean_obj_arg xs, lean_obj_arg w) {
+	(void)w;
+	size_t n = lean_array_size(xs);
+	shlo_arr *v = (shlo_arr *)malloc(sizeof(shlo_arr) * (n ? n : 1));
+	for (size_t i = 0; i < n; i++) v[i] = unbox_arr(lean_array_get_core(xs, i));
+	int rc = shlo_eval(v, (int)n);
+	free(v);
+	if (rc) return io_err("eval");
+	return lean_io_result_mk_ok(lean_box(0));
+}
+
+/* ---- kernels (Mlx.lean:60-64) ---- */
+
+LEAN_EXPORT lean_obj_res smlx_kernel_new(b_lean_obj_arg name, b_lean_obj_arg ins, b_lean_obj_arg outs,
+                                         b_lean_obj_arg src, b_lean_obj_arg hdr, lean_obj_arg w) {
+	(void)w;
+	if (!kern_class) kern_class = lean_register_external_class(kern_finalize, noop_foreach);
+	size_t ni = lean_array_size(ins), no = lean_array_size(outs);
+	const char **vi = (const char **)malloc(sizeof(char *) * (ni ? ni : 1));
+	const char **vo = (const char **)malloc(sizeof(char *) * (no ? no : 1));
+	for (size_t i = 0; i < ni; i++) vi[i] = lean_string_cstr(lean_array_get_core(ins, i));
+	for (size_t i = 0; i < no; i++) vo[i] = lean_string_cstr(lean_array_get_core(outs, i));
+	shlo_kernel k = NULL;
+	int rc = shlo_kernel_new(lean_string_cstr(name), vi, (int)ni, vo, (int)no, lean_string_cstr(src),
+	                         lean_string_cstr(hdr), &k);
+	free(vi);
+	free(vo);
+	if (rc) return io_err("kernel");
+	return lean_io_result_mk_ok(lean_alloc_external(kern_class, k));
+}
+
+LEAN_EXPORT lean_obj_res smlx_kernel_apply(b_lean_obj_arg ko, b_lean_obj_arg ins, b_lean_obj_arg shapes,
+                                           b_lean_obj_arg dts, b_lean_obj_arg grid, b_lean_obj_arg tg, lean_obj_arg w) {
+	(void)w;
+	size_t ni = lean_array_size(ins), no = lean_array_size(shapes);
+	if (no > 8 || lean_sarray_size(dts) < no) return io_err("kernel apply: output shapes and dtypes");
+	shlo_arr *vi = (shlo_arr *)malloc(sizeof(shlo_arr) * (ni ? ni : 1));
+	for (size_t i = 0; i < ni; i++) vi[i] = unbox_arr(lean_array_get_core(ins, i));
+	int64_t sh[8][SHLO_MAX_RANK];
+	const int64_t *shp[8];
+	int nd[8];
+	for (size_t i = 0; i < no; i++) {
+		nd[i] = shape_of(lean_array_get_core(shapes, i), sh[i], SHLO_MAX_RANK);
+		shp[i] = sh[i];
+		if (nd[i] < 0) {
+			free(vi);
+			return io_err("kernel apply: rank above 16");
+		}
+	}
+	int64_t g[3], t[3];
+	if (shape_of(grid, g, 3) != 3 || shape_of(tg, t, 3) != 3) {
+		free(vi);
+		return io_err("kernel: grid and threadgroup need 3 entries");
+	}
+	shlo_arr outs[8] = {0};
+	int rc = shlo_kernel_apply((shlo_kernel)lean_get_external_data(ko), vi, (int)ni, shp, nd, lean_sarray_cptr(dts),
+	                           (int)no, g, t, outs);
+	free(vi);
+	if (rc) return io_err("kernel apply");
+	lean_object *r = lean_alloc_array(0, no);
+	for (size_t i = 0; i < no; i++) r = lean_array_push(r, box_arr(outs[i]));
+	return lean_io_result_mk_ok(r);
+}
+
+/* ---- traced functions (Mlx.lean:66-67) ---- */
+
+/* Calls the Lean closure (Array Arr -> IO (Array Arr)) on the inputs; its error
+   message travels back through `err` (c/smlx_shim.c:337-357). */
+static int trampoline(void *payload, const shlo_arr *ins, int nin, shlo_arr *outs, int *nout, int max_out, char *err,
+                      size_t cap) {
+	lean_object *f = (lean_object *)payload;
+	lean_object *args = lean_alloc_array(0, (size_t)nin);
+	for (int i = 0; i < nin; i++) {
+		shlo_retain(ins[i]);
+		args = lean_array_push(args, box_arr(ins[i]));
+	}
+	lean_inc(f);
+	lean_object *r = lean_apply_2(f, args, lean_io_mk_world());
+	if (lean_io_result_is_error(r)) {
+		lean_object *e = lean_io_result_get_error(r);
+		lean_inc(e);
+		lean_object *msg = lean_io_error_to_string(e);
+		snprintf(err, cap, "%s", lean_string_cstr(msg));
+		lean_dec(msg);
+		lean_dec(r);
+		return 1;
+	}
+	lean_object *res = lean_io_result_get_value(r);
+	size_t n = lean_array_size(res);
+	if ((int)n > max_out) {
+		snprintf(err, cap, "%zu outputs, room for %d", n, max_out);
+		lean_dec(r);
+		return 1;
+	}
+	for (size_t i = 0; i < n; i++) {
+		shlo_arr a = unbox_arr(lean_array_get_core(res, i));
+		shlo_retain(a);
+		outs[i] = a;
+	}
+	*nout = (int)n;
+	lean_dec(r);
+	return 0;
+}
+
+static void payload_free(void *p) { lean_dec((lean_object *)p); }
+
+LEAN_EXPORT lean_obj_res smlx_compile(lean_obj_arg f, uint8_t enable, lean_obj_arg w) {
+	(void)w;
+	if (!fn_class) fn_class = lean_register_external_class(fn_finalize, noop_foreach);
+	shlo_fn fn = NULL;
+	if (shlo_compile(trampoline, f, payload_free, enable, &fn)) {
+		lean_dec(f);
+		return io_err("compile");
+	}
+	return lean_io_result_mk_ok(lean_alloc_external(fn_class, fn));
+}
+
+LEAN_EXPORT lean_obj_res smlx_apply(b_lean_obj_arg fo, b_lean_obj_arg ins, lean_obj_arg w) {
+	(void)w;
+	size_t ni = lean_array_size(ins);
+	shlo_arr *vi = (shlo_arr *)malloc(sizeof(shlo_arr) * (ni ? ni : 1));
+	for (size_t i = 0; i < ni; i++) vi[i] = unbox_arr(lean_array_get_core(ins, i));
+	shlo_arr outs[64];
+	int n = 0;
+	int rc = shlo_apply((shlo_fn)lean_get_external_data(fo), vi, (int)ni, outs, &n, 64);
+	free(vi);
+	if (rc) return io_err("apply");
+	lean_object *r = lean_alloc_array(0, (size_t)n);
+	for (int i = 0; i < n; i++) r = lean_array_push(r, box_arr(outs[i]));
+	return lean_io_result_mk_ok(r);
+}
+
+/* ---- test-driver helpers (Mlx.lean:69-73) ---- */
+
+LEAN_EXPORT lean_obj_res smlx_libm_erff_range(uint32_t base, uint32_t count, lean_obj_arg w) {
+	(void)w;
+	lean_object *r = lean_alloc_sarray(1, (size_t)count * 4, (size_t)count * 4);
+	if (shlo_libm_erff_range(base, count, (uint32_t *)lean_sarray_cptr(r))) {
+		lean_dec(r);
+		return io_err("libm_erff_range");
+	}
+	return lean_io_result_mk_ok(r);
+}
+
+LEAN_EXPORT lean_obj_res smlx_count_nonzero(b_lean_obj_arg a, lean_obj_arg w) {
+	(void)w;
+	uint64_t n = 0;
+	if (shlo_count_nonzero(unbox_arr(a), &n)) return io_err("count_nonzero");
+	return lean_io_result_mk_ok(lean_uint64_to_nat(n));
+}
