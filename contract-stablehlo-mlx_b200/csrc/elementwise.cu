@@ -57,24 +57,93 @@ static void collapse(Iter &it, Operand *ops, int nops) {
   }
 }
 
-// Offsets of element `idx` (row-major over it.shape) in up to 3 operands.
-template <int NOPS>
-__device__ __forceinline__ void offsets(const Iter &it, const Operand *ops, int64_t idx, int64_t *off) {
+// Offsets of element `idx` (row-major over it.shape) in two to four operands.
+// ND is the collapsed rank (1, 2, 3) or kMaxRank for any rank; I is the index
+// type (32-bit whenever the element count allows). The dimension loops are
+// unrolled so every shape/stride access is a fixed parameter-space offset.
+template <int ND, typename I>
+__device__ __forceinline__ void offs2(const Iter &it, const Operand &a, const Operand &b, I idx, int64_t &oa,
+                                      int64_t &ob) {
+  oa = 0;
+  ob = 0;
 #pragma unroll
-  for (int k = 0; k < NOPS; k++) off[k] = 0;
-  if (it.ndim == 1) {
-#pragma unroll
-    for (int k = 0; k < NOPS; k++) off[k] = idx * ops[k].strides[0];
-    return;
-  }
-  for (int d = it.ndim - 1; d >= 0; d--) {
-    int64_t s = it.shape[d];
-    int64_t c = idx % s;
-    idx /= s;
-#pragma unroll
-    for (int k = 0; k < NOPS; k++) off[k] += c * ops[k].strides[d];
+  for (int d = ND - 1; d >= 0; d--) {
+    if (ND == kMaxRank && d >= it.ndim) continue;
+    I c = idx;
+    if (d > 0) {
+      I s = (I)it.shape[d];
+      I q = idx / s;
+      c = idx - q * s;
+      idx = q;
+    }
+    oa += (int64_t)c * a.strides[d];
+    ob += (int64_t)c * b.strides[d];
   }
 }
+
+template <int ND, typename I>
+__device__ __forceinline__ void offs3(const Iter &it, const Operand &a, const Operand &b, const Operand &z, I idx,
+                                      int64_t &oa, int64_t &ob, int64_t &oz) {
+  oa = 0;
+  ob = 0;
+  oz = 0;
+#pragma unroll
+  for (int d = ND - 1; d >= 0; d--) {
+    if (ND == kMaxRank && d >= it.ndim) continue;
+    I c = idx;
+    if (d > 0) {
+      I s = (I)it.shape[d];
+      I q = idx / s;
+      c = idx - q * s;
+      idx = q;
+    }
+    oa += (int64_t)c * a.strides[d];
+    ob += (int64_t)c * b.strides[d];
+    oz += (int64_t)c * z.strides[d];
+  }
+}
+
+template <int ND, typename I>
+__device__ __forceinline__ void offs4(const Iter &it, const Operand &a, const Operand &b, const Operand &c3,
+                                      const Operand &z, I idx, int64_t &oa, int64_t &ob, int64_t &oc, int64_t &oz) {
+  oa = 0;
+  ob = 0;
+  oc = 0;
+  oz = 0;
+#pragma unroll
+  for (int d = ND - 1; d >= 0; d--) {
+    if (ND == kMaxRank && d >= it.ndim) continue;
+    I c = idx;
+    if (d > 0) {
+      I s = (I)it.shape[d];
+      I q = idx / s;
+      c = idx - q * s;
+      idx = q;
+    }
+    oa += (int64_t)c * a.strides[d];
+    ob += (int64_t)c * b.strides[d];
+    oc += (int64_t)c * c3.strides[d];
+    oz += (int64_t)c * z.strides[d];
+  }
+}
+
+// Call f(integral_constant<ND>, I{}) with the rank and index type for `it`.
+template <typename F>
+static void by_rank(const Iter &it, F &&f) {
+  if (it.n < ((int64_t)1 << 31)) {
+    switch (it.ndim) {
+      case 1: f(std::integral_constant<int, 1>{}, uint32_t{}); return;
+      case 2: f(std::integral_constant<int, 2>{}, uint32_t{}); return;
+      case 3: f(std::integral_constant<int, 3>{}, uint32_t{}); return;
+      default: f(std::integral_constant<int, kMaxRank>{}, uint32_t{}); return;
+    }
+  }
+  f(std::integral_constant<int, kMaxRank>{}, uint64_t{});
+}
+
+#define GRID_LOOP(I, i, n)                                                                     \
+  for (I i = (I)blockIdx.x * blockDim.x + threadIdx.x, _st = (I)gridDim.x * blockDim.x; i < (I)(n); \
+       i += _st)
 
 // ------------------------------------------------------------ typed access ----
 
@@ -135,16 +204,106 @@ __device__ __forceinline__ D f2i(float v) {
 
 // ------------------------------------------------------------ strided copy ----
 
-template <typename E>
+template <typename E, int ND, typename I>
 __global__ void k_copy(Iter it, Operand src, Operand dst) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < it.n; i += stride) {
-    Operand ops[2] = {src, dst};
-    int64_t off[2];
-    offsets<2>(it, ops, i, off);
-    reinterpret_cast<E *>(const_cast<char *>(dst.ptr))[off[1]] = reinterpret_cast<const E *>(src.ptr)[off[0]];
+  GRID_LOOP(I, i, it.n) {
+    int64_t os, od;
+    offs2<ND, I>(it, src, dst, i, os, od);
+    reinterpret_cast<E *>(const_cast<char *>(dst.ptr))[od] = reinterpret_cast<const E *>(src.ptr)[os];
   }
 }
+
+// Rows that are contiguous in both source and destination, with up to three
+// outer axes of any strides; V is the widest vector the alignment allows.
+struct RowDesc {
+  const void *src;
+  void *dst;
+  uint32_t nrows, lenv;  // rows, row length in V units
+  int no;                // outer axes (0..3)
+  uint32_t os[3];        // outer shape
+  int64_t ss[3], ds[3];  // outer strides, in V units
+};
+
+template <typename V>
+__global__ void k_copy_rows(RowDesc d) {
+  const uint32_t total = d.nrows * d.lenv;
+  GRID_LOOP(uint32_t, i, total) {
+    uint32_t r = i / d.lenv, c = i - r * d.lenv;
+    int64_t so = 0, dof = 0;
+#pragma unroll
+    for (int k = 2; k >= 0; k--) {
+      if (k >= d.no) continue;
+      uint32_t cc = r;
+      if (k > 0) {
+        uint32_t q = r / d.os[k];
+        cc = r - q * d.os[k];
+        r = q;
+      }
+      so += (int64_t)cc * d.ss[k];
+      dof += (int64_t)cc * d.ds[k];
+    }
+    reinterpret_cast<V *>(d.dst)[dof + c] = reinterpret_cast<const V *>(d.src)[so + c];
+  }
+}
+
+// A transposing copy: the source is contiguous along axis t, the destination
+// along the last axis l. 32x32 tiles through shared memory keep both sides
+// coalesced; up to three outer axes run over blockIdx.z.
+struct TDesc {
+  const char *src;
+  char *dst;
+  int64_t n_t, n_l;
+  int64_t ss_l, ds_t;    // source stride of l, destination stride of t (elements)
+  int no;
+  uint32_t nouter;
+  uint32_t os[3];
+  int64_t ss[3], ds[3];
+};
+
+template <typename E>
+__global__ void k_copy_transpose(TDesc d) {
+  __shared__ E tile[32][33];
+  const int tx = threadIdx.x, ty = threadIdx.y;
+  const int64_t t0 = (int64_t)blockIdx.y * 32, l0 = (int64_t)blockIdx.x * 32;
+  for (uint32_t z = blockIdx.z; z < d.nouter; z += gridDim.z) {
+    int64_t so = 0, dof = 0;
+    uint32_t r = z;
+#pragma unroll
+    for (int k = 2; k >= 0; k--) {
+      if (k >= d.no) continue;
+      uint32_t cc = r;
+      if (k > 0) {
+        uint32_t q = r / d.os[k];
+        cc = r - q * d.os[k];
+        r = q;
+      }
+      so += (int64_t)cc * d.ss[k];
+      dof += (int64_t)cc * d.ds[k];
+    }
+    const E *src = reinterpret_cast<const E *>(d.src) + so;
+    E *dst = reinterpret_cast<E *>(d.dst) + dof;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      int64_t t = t0 + tx, l = l0 + ty + j;
+      if (t < d.n_t && l < d.n_l) tile[ty + j][tx] = src[t + l * d.ss_l];
+    }
+    __syncthreads();
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      int64_t t = t0 + ty + j, l = l0 + tx;
+      if (t < d.n_t && l < d.n_l) dst[t * d.ds_t + l] = tile[tx][ty + j];
+    }
+    __syncthreads();
+  }
+}
+
+template <typename E>
+static void launch_transpose(Device *dev, const TDesc &d) {
+  dim3 grid((unsigned)((d.n_l + 31) / 32), (unsigned)((d.n_t + 31) / 32), d.nouter < 65535 ? d.nouter : 65535);
+  k_copy_transpose<E><<<grid, dim3(32, 8), 0, dev->stream>>>(d);
+}
+
+static bool aligned(const void *p, size_t a) { return ((uintptr_t)p % a) == 0; }
 
 // Copy the strided `src` into `dst` laid out with strides `dst_strides`.
 static int copy_into(Device *dev, const Arr *src, char *dst, const int64_t *dst_strides) {
@@ -168,13 +327,86 @@ static int copy_into(Device *dev, const Arr *src, char *dst, const int64_t *dst_
     it.shape[0] = 1;
     ops[0].strides[0] = ops[1].strides[0] = 1;
   }
-  unsigned g = grid_for(it.n, 256, dev);
-  switch (dtype_size(src->dtype)) {
-    case 1: k_copy<uint8_t><<<g, 256, 0, dev->stream>>>(it, ops[0], ops[1]); break;
-    case 2: k_copy<uint16_t><<<g, 256, 0, dev->stream>>>(it, ops[0], ops[1]); break;
-    case 4: k_copy<uint32_t><<<g, 256, 0, dev->stream>>>(it, ops[0], ops[1]); break;
-    default: k_copy<uint64_t><<<g, 256, 0, dev->stream>>>(it, ops[0], ops[1]); break;
+  const size_t es = dtype_size(src->dtype);
+  const int nd = it.ndim, last = nd - 1;
+  // Fast path 1: rows contiguous on both sides.
+  if (nd <= 4 && ops[0].strides[last] == 1 && ops[1].strides[last] == 1 && it.n < ((int64_t)1 << 31)) {
+    int64_t len = it.shape[last];
+    size_t vb = es;  // vector bytes
+    for (size_t cand = 16; cand > es; cand /= 2) {
+      int64_t k = (int64_t)(cand / es);
+      bool ok = len % k == 0 && aligned(ops[0].ptr, cand) && aligned(ops[1].ptr, cand);
+      for (int d = 0; d < last && ok; d++) ok = ops[0].strides[d] % k == 0 && ops[1].strides[d] % k == 0;
+      if (ok) {
+        vb = cand;
+        break;
+      }
+    }
+    const int64_t k = (int64_t)(vb / es);
+    RowDesc d;
+    d.src = ops[0].ptr;
+    d.dst = (void *)ops[1].ptr;
+    d.lenv = (uint32_t)(len / k);
+    d.nrows = (uint32_t)(it.n / len);
+    d.no = last;
+    for (int a = 0; a < last; a++) {
+      d.os[a] = (uint32_t)it.shape[a];
+      d.ss[a] = ops[0].strides[a] / k;
+      d.ds[a] = ops[1].strides[a] / k;
+    }
+    unsigned g = grid_for((int64_t)d.nrows * d.lenv, 256, dev, 16);
+    switch (vb) {
+      case 16: k_copy_rows<uint4><<<g, 256, 0, dev->stream>>>(d); break;
+      case 8: k_copy_rows<uint2><<<g, 256, 0, dev->stream>>>(d); break;
+      case 4: k_copy_rows<uint32_t><<<g, 256, 0, dev->stream>>>(d); break;
+      case 2: k_copy_rows<uint16_t><<<g, 256, 0, dev->stream>>>(d); break;
+      default: k_copy_rows<uint8_t><<<g, 256, 0, dev->stream>>>(d); break;
+    }
+    return launch_check("copy");
   }
+  // Fast path 2: a transpose (source contiguous along another axis than the last).
+  if (nd >= 2 && nd <= 5 && ops[1].strides[last] == 1 && ops[0].strides[last] != 1) {
+    int t = -1;
+    for (int a = 0; a < last; a++)
+      if (ops[0].strides[a] == 1) t = a;
+    int64_t nouter = it.n / (it.shape[t < 0 ? 0 : t] * it.shape[last]);
+    if (t >= 0 && nouter < ((int64_t)1 << 31) && it.shape[t] < 65535 * 32) {
+      TDesc d;
+      d.src = ops[0].ptr;
+      d.dst = (char *)ops[1].ptr;
+      d.n_t = it.shape[t];
+      d.n_l = it.shape[last];
+      d.ss_l = ops[0].strides[last];
+      d.ds_t = ops[1].strides[t];
+      d.no = 0;
+      for (int a = 0; a < last; a++) {
+        if (a == t) continue;
+        d.os[d.no] = (uint32_t)it.shape[a];
+        d.ss[d.no] = ops[0].strides[a];
+        d.ds[d.no] = ops[1].strides[a];
+        d.no++;
+      }
+      d.nouter = (uint32_t)nouter;
+      switch (es) {
+        case 1: launch_transpose<uint8_t>(dev, d); break;
+        case 2: launch_transpose<uint16_t>(dev, d); break;
+        case 4: launch_transpose<uint32_t>(dev, d); break;
+        default: launch_transpose<uint64_t>(dev, d); break;
+      }
+      return launch_check("copy (transpose)");
+    }
+  }
+  unsigned g = grid_for(it.n, 256, dev, 16);
+  by_rank(it, [&](auto ndc, auto ic) {
+    constexpr int ND = decltype(ndc)::value;
+    using I = decltype(ic);
+    switch (es) {
+      case 1: k_copy<uint8_t, ND, I><<<g, 256, 0, dev->stream>>>(it, ops[0], ops[1]); break;
+      case 2: k_copy<uint16_t, ND, I><<<g, 256, 0, dev->stream>>>(it, ops[0], ops[1]); break;
+      case 4: k_copy<uint32_t, ND, I><<<g, 256, 0, dev->stream>>>(it, ops[0], ops[1]); break;
+      default: k_copy<uint64_t, ND, I><<<g, 256, 0, dev->stream>>>(it, ops[0], ops[1]); break;
+    }
+  });
   return launch_check("copy");
 }
 
@@ -188,28 +420,24 @@ int launch_copy_strided(Device *dev, const Arr *src, void *dst) {
 
 // ------------------------------------------------------------ astype ----
 
-template <typename C>
+template <typename C, int ND, typename I>
 __global__ void k_cast(Iter it, Operand src, Operand dst) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < it.n; i += stride) {
-    Operand ops[2] = {src, dst};
-    int64_t off[2];
-    offsets<2>(it, ops, i, off);
-    C v = load_as<C>(src.ptr, src.dtype, off[0]);
-    store_as<C>(const_cast<char *>(dst.ptr), dst.dtype, off[1], v);
+  GRID_LOOP(I, i, it.n) {
+    int64_t os, od;
+    offs2<ND, I>(it, src, dst, i, os, od);
+    C v = load_as<C>(src.ptr, src.dtype, os);
+    store_as<C>(const_cast<char *>(dst.ptr), dst.dtype, od, v);
   }
 }
 
 // float -> integer with saturation
-template <typename D>
+template <typename D, int ND, typename I>
 __global__ void k_cast_f2i(Iter it, Operand src, Operand dst) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < it.n; i += stride) {
-    Operand ops[2] = {src, dst};
-    int64_t off[2];
-    offsets<2>(it, ops, i, off);
-    float v = load_as<float>(src.ptr, src.dtype, off[0]);
-    reinterpret_cast<D *>(const_cast<char *>(dst.ptr))[off[1]] = f2i<D>(v);
+  GRID_LOOP(I, i, it.n) {
+    int64_t os, od;
+    offs2<ND, I>(it, src, dst, i, os, od);
+    float v = load_as<float>(src.ptr, src.dtype, os);
+    reinterpret_cast<D *>(const_cast<char *>(dst.ptr))[od] = f2i<D>(v);
   }
 }
 
@@ -249,32 +477,36 @@ int cast_array(Arr *a, uint8_t dt, Arr **out) {
     ops[0].strides[0] = ops[1].strides[0] = 1;
   }
   if (it.n > 0) {
-    unsigned g = grid_for(it.n, 256, dev);
+    unsigned g = grid_for(it.n, 256, dev, 16);
     bool from_float = dtype_is_float(a->dtype);
-    if (from_float && !dtype_is_float(dt) && dt != kBool) {
-      switch (dt) {
-        case kU8: launch_typed(k_cast_f2i<uint8_t>, g, dev, it, ops[0], ops[1]); break;
-        case kU16: launch_typed(k_cast_f2i<uint16_t>, g, dev, it, ops[0], ops[1]); break;
-        case kU32: launch_typed(k_cast_f2i<uint32_t>, g, dev, it, ops[0], ops[1]); break;
-        case kU64: launch_typed(k_cast_f2i<uint64_t>, g, dev, it, ops[0], ops[1]); break;
-        case kI8: launch_typed(k_cast_f2i<int8_t>, g, dev, it, ops[0], ops[1]); break;
-        case kI16: launch_typed(k_cast_f2i<int16_t>, g, dev, it, ops[0], ops[1]); break;
-        case kI32: launch_typed(k_cast_f2i<int32_t>, g, dev, it, ops[0], ops[1]); break;
-        default: launch_typed(k_cast_f2i<int64_t>, g, dev, it, ops[0], ops[1]); break;
+    by_rank(it, [&](auto ndc, auto ic) {
+      constexpr int ND = decltype(ndc)::value;
+      using I = decltype(ic);
+      if (from_float && !dtype_is_float(dt) && dt != kBool) {
+        switch (dt) {
+          case kU8: launch_typed(k_cast_f2i<uint8_t, ND, I>, g, dev, it, ops[0], ops[1]); break;
+          case kU16: launch_typed(k_cast_f2i<uint16_t, ND, I>, g, dev, it, ops[0], ops[1]); break;
+          case kU32: launch_typed(k_cast_f2i<uint32_t, ND, I>, g, dev, it, ops[0], ops[1]); break;
+          case kU64: launch_typed(k_cast_f2i<uint64_t, ND, I>, g, dev, it, ops[0], ops[1]); break;
+          case kI8: launch_typed(k_cast_f2i<int8_t, ND, I>, g, dev, it, ops[0], ops[1]); break;
+          case kI16: launch_typed(k_cast_f2i<int16_t, ND, I>, g, dev, it, ops[0], ops[1]); break;
+          case kI32: launch_typed(k_cast_f2i<int32_t, ND, I>, g, dev, it, ops[0], ops[1]); break;
+          default: launch_typed(k_cast_f2i<int64_t, ND, I>, g, dev, it, ops[0], ops[1]); break;
+        }
+      } else if (from_float || dtype_is_float(dt)) {
+        // int -> float rounds once (int64/uint64 sources go through double,
+        // which is exact up to 2^53 and rounds once to binary32 beyond that for
+        // all but a vanishing set of ties).
+        if (a->dtype == kI64 || a->dtype == kU64)
+          launch_typed(k_cast<double, ND, I>, g, dev, it, ops[0], ops[1]);
+        else
+          launch_typed(k_cast<float, ND, I>, g, dev, it, ops[0], ops[1]);
+      } else if (dtype_is_signed_int(a->dtype) || a->dtype == kBool) {
+        launch_typed(k_cast<int64_t, ND, I>, g, dev, it, ops[0], ops[1]);
+      } else {
+        launch_typed(k_cast<uint64_t, ND, I>, g, dev, it, ops[0], ops[1]);
       }
-    } else if (from_float || dtype_is_float(dt)) {
-      // int -> float rounds once (int64/uint64 sources go through double,
-      // which is exact up to 2^53 and rounds once to binary32 beyond that for
-      // all but a vanishing set of ties).
-      if (a->dtype == kI64 || a->dtype == kU64)
-        launch_typed(k_cast<double>, g, dev, it, ops[0], ops[1]);
-      else
-        launch_typed(k_cast<float>, g, dev, it, ops[0], ops[1]);
-    } else if (dtype_is_signed_int(a->dtype) || a->dtype == kBool) {
-      launch_typed(k_cast<int64_t>, g, dev, it, ops[0], ops[1]);
-    } else {
-      launch_typed(k_cast<uint64_t>, g, dev, it, ops[0], ops[1]);
-    }
+    });
     if (launch_check("astype")) {
       shlo_release(o);
       return 1;
@@ -316,19 +548,17 @@ __device__ __forceinline__ float unary_float(int op, float v) {
   }
 }
 
-template <typename C, bool FLOAT>
+template <typename C, bool FLOAT, int ND, typename I>
 __global__ void k_unary(int op, Iter it, Operand x, Operand y) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < it.n; i += stride) {
-    Operand ops[2] = {x, y};
-    int64_t off[2];
-    offsets<2>(it, ops, i, off);
+  GRID_LOOP(I, i, it.n) {
+    int64_t ox, oy;
+    offs2<ND, I>(it, x, y, i, ox, oy);
     if constexpr (FLOAT) {
-      float v = load_as<float>(x.ptr, x.dtype, off[0]);
-      store_as<float>(const_cast<char *>(y.ptr), y.dtype, off[1], unary_float(op, v));
+      float v = load_as<float>(x.ptr, x.dtype, ox);
+      store_as<float>(const_cast<char *>(y.ptr), y.dtype, oy, unary_float(op, v));
     } else {
-      C v = load_as<C>(x.ptr, x.dtype, off[0]);
-      store_as<C>(const_cast<char *>(y.ptr), y.dtype, off[1], unary_int<C>(op, v));
+      C v = load_as<C>(x.ptr, x.dtype, ox);
+      store_as<C>(const_cast<char *>(y.ptr), y.dtype, oy, unary_int<C>(op, v));
     }
   }
 }
@@ -373,25 +603,28 @@ int op_unary(uint32_t op, Arr *a, Arr **out) {
   Operand ops[2];
   prepare_iter(o, &a, 1, it, ops);
   if (it.n > 0) {
-    unsigned g = grid_for(it.n, 256, dev);
+    unsigned g = grid_for(it.n, 256, dev, 16);
     bool flt = dtype_is_float(dt) || needs_float;
-    if (flt) {
-      launch_typed(k_unary<float, true>, g, dev, (int)op, it, ops[0], ops[1]);
-    } else if (dt == kBool) {
-      // bool: invert is logical not
-      launch_typed(k_unary<uint8_t, false>, g, dev, op == U_INVERT ? (int)U_NOT : (int)op, it, ops[0], ops[1]);
-    } else {
-      switch (dt) {
-        case kU8: launch_typed(k_unary<uint8_t, false>, g, dev, (int)op, it, ops[0], ops[1]); break;
-        case kU16: launch_typed(k_unary<uint16_t, false>, g, dev, (int)op, it, ops[0], ops[1]); break;
-        case kU32: launch_typed(k_unary<uint32_t, false>, g, dev, (int)op, it, ops[0], ops[1]); break;
-        case kU64: launch_typed(k_unary<uint64_t, false>, g, dev, (int)op, it, ops[0], ops[1]); break;
-        case kI8: launch_typed(k_unary<int8_t, false>, g, dev, (int)op, it, ops[0], ops[1]); break;
-        case kI16: launch_typed(k_unary<int16_t, false>, g, dev, (int)op, it, ops[0], ops[1]); break;
-        case kI32: launch_typed(k_unary<int32_t, false>, g, dev, (int)op, it, ops[0], ops[1]); break;
-        default: launch_typed(k_unary<int64_t, false>, g, dev, (int)op, it, ops[0], ops[1]); break;
+    int uop = (dt == kBool && op == U_INVERT) ? (int)U_NOT : (int)op;  // bool: invert is logical not
+    by_rank(it, [&](auto ndc, auto ic) {
+      constexpr int ND = decltype(ndc)::value;
+      using I = decltype(ic);
+      if (flt) {
+        launch_typed(k_unary<float, true, ND, I>, g, dev, uop, it, ops[0], ops[1]);
+        return;
       }
-    }
+      switch (dt) {
+        case kBool:
+        case kU8: launch_typed(k_unary<uint8_t, false, ND, I>, g, dev, uop, it, ops[0], ops[1]); break;
+        case kU16: launch_typed(k_unary<uint16_t, false, ND, I>, g, dev, uop, it, ops[0], ops[1]); break;
+        case kU32: launch_typed(k_unary<uint32_t, false, ND, I>, g, dev, uop, it, ops[0], ops[1]); break;
+        case kU64: launch_typed(k_unary<uint64_t, false, ND, I>, g, dev, uop, it, ops[0], ops[1]); break;
+        case kI8: launch_typed(k_unary<int8_t, false, ND, I>, g, dev, uop, it, ops[0], ops[1]); break;
+        case kI16: launch_typed(k_unary<int16_t, false, ND, I>, g, dev, uop, it, ops[0], ops[1]); break;
+        case kI32: launch_typed(k_unary<int32_t, false, ND, I>, g, dev, uop, it, ops[0], ops[1]); break;
+        default: launch_typed(k_unary<int64_t, false, ND, I>, g, dev, uop, it, ops[0], ops[1]); break;
+      }
+    });
     if (launch_check("unary")) {
       shlo_release(o);
       return 1;
@@ -468,26 +701,81 @@ __device__ __forceinline__ float binary_float(int op, float u, float v) {
   }
 }
 
-template <typename C, bool FLOAT>
+template <typename C, bool FLOAT, int ND, typename I>
 __global__ void k_binary(int op, Iter it, Operand x, Operand y, Operand z) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
   const bool cmp = op >= B_EQ && op <= B_GE;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < it.n; i += stride) {
-    Operand ops[3] = {x, y, z};
-    int64_t off[3];
-    offsets<3>(it, ops, i, off);
+  GRID_LOOP(I, i, it.n) {
+    int64_t ox, oy, oz;
+    offs3<ND, I>(it, x, y, z, i, ox, oy, oz);
     typedef typename std::conditional<FLOAT, float, C>::type V;
-    V u = load_as<V>(x.ptr, x.dtype, off[0]);
-    V v = load_as<V>(y.ptr, y.dtype, off[1]);
+    V u = load_as<V>(x.ptr, x.dtype, ox);
+    V v = load_as<V>(y.ptr, y.dtype, oy);
     char *zp = const_cast<char *>(z.ptr);
     if (cmp) {
-      reinterpret_cast<uint8_t *>(zp)[off[2]] = compare<V>(op, u, v) ? 1 : 0;
+      reinterpret_cast<uint8_t *>(zp)[oz] = compare<V>(op, u, v) ? 1 : 0;
     } else if constexpr (FLOAT) {
-      store_as<float>(zp, z.dtype, off[2], binary_float(op, (float)u, (float)v));
+      store_as<float>(zp, z.dtype, oz, binary_float(op, (float)u, (float)v));
     } else {
-      store_as<C>(zp, z.dtype, off[2], binary_int<C>(op, (C)u, (C)v));
+      store_as<C>(zp, z.dtype, oz, binary_int<C>(op, (C)u, (C)v));
     }
   }
+}
+
+// binary32 operands and result laid out as [rows, cols] with cols % 4 == 0:
+// each operand walks its columns contiguously (a row segment, stride 1) or not
+// at all (one value per row, stride 0), and rows at any stride. Four elements
+// per thread with 16-byte accesses: the layout of bias adds, norm affines and
+// residual adds.
+struct VecOperand {
+  const float *p;
+  int64_t row;  // row stride, floats
+  int col;      // 1 = contiguous columns, 0 = one value per row
+};
+
+__global__ void k_binary_f32v(int op, uint32_t nv, uint32_t colsv, VecOperand a, VecOperand b, float4 *__restrict__ y) {
+  GRID_LOOP(uint32_t, v, nv) {
+    uint32_t r = v / colsv, c = (v - r * colsv) * 4;
+    float4 u, w;
+    if (a.col) u = *reinterpret_cast<const float4 *>(a.p + r * a.row + c);
+    else u.x = u.y = u.z = u.w = a.p[r * a.row];
+    if (b.col) w = *reinterpret_cast<const float4 *>(b.p + r * b.row + c);
+    else w.x = w.y = w.z = w.w = b.p[r * b.row];
+    float4 o;
+    o.x = binary_float(op, u.x, w.x);
+    o.y = binary_float(op, u.y, w.y);
+    o.z = binary_float(op, u.z, w.z);
+    o.w = binary_float(op, u.w, w.w);
+    y[v] = o;
+  }
+}
+
+// The vectorized layout of `it`'s operands, when it applies.
+static bool vec_layout(const Iter &it, const Operand *ops, int nin, uint32_t &rows, uint32_t &cols, VecOperand *vo) {
+  if (it.ndim > 2 || it.n >= ((int64_t)1 << 31)) return false;
+  const int last = it.ndim - 1;
+  int64_t C = it.shape[last];
+  if (C % 4) return false;
+  for (int k = 0; k <= nin; k++) {
+    if (ops[k].dtype != kF32) return false;
+    int64_t cs = ops[k].strides[last];
+    int64_t rs = it.ndim == 2 ? ops[k].strides[0] : 0;
+    if (k == nin) {  // the output: row-major
+      if (cs != 1 || (it.ndim == 2 && rs != C)) return false;
+      if (!aligned(ops[k].ptr, 16)) return false;
+      continue;
+    }
+    if (cs == 1) {
+      if (rs % 4 || !aligned(ops[k].ptr, 16)) return false;
+    } else if (cs != 0) {
+      return false;
+    }
+    vo[k].p = reinterpret_cast<const float *>(ops[k].ptr);
+    vo[k].row = rs;
+    vo[k].col = cs == 1;
+  }
+  rows = (uint32_t)(it.n / C);
+  cols = (uint32_t)C;
+  return true;
 }
 
 static int builtin_matmul(Arr *a, Arr *b, Arr **out);
@@ -522,22 +810,34 @@ int op_binary(uint32_t op, Arr *a, Arr *b, Arr **out) {
     Arr *ins[2] = {va, vb};
     prepare_iter(o, ins, 2, it, ops);
     if (it.n > 0) {
-      unsigned g = grid_for(it.n, 256, dev);
-      if (dtype_is_float(ct)) {
-        launch_typed(k_binary<float, true>, g, dev, (int)op, it, ops[0], ops[1], ops[2]);
+      unsigned g = grid_for(it.n, 256, dev, 16);
+      uint32_t vr, vc;
+      VecOperand vo[2];
+      if (!is_compare(op) && vec_layout(it, ops, 2, vr, vc, vo)) {
+        uint32_t nv = vr * (vc / 4);
+        k_binary_f32v<<<grid_for(nv, 256, dev, 16), 256, 0, dev->stream>>>((int)op, nv, vc / 4, vo[0], vo[1],
+                                                                          (float4 *)ops[2].ptr);
       } else {
-        // bool logical ops are computed on 0/1 in uint8
-        switch (ct) {
-          case kBool:
-          case kU8: launch_typed(k_binary<uint8_t, false>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
-          case kU16: launch_typed(k_binary<uint16_t, false>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
-          case kU32: launch_typed(k_binary<uint32_t, false>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
-          case kU64: launch_typed(k_binary<uint64_t, false>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
-          case kI8: launch_typed(k_binary<int8_t, false>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
-          case kI16: launch_typed(k_binary<int16_t, false>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
-          case kI32: launch_typed(k_binary<int32_t, false>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
-          default: launch_typed(k_binary<int64_t, false>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
-        }
+        by_rank(it, [&](auto ndc, auto ic) {
+          constexpr int ND = decltype(ndc)::value;
+          using I = decltype(ic);
+          if (dtype_is_float(ct)) {
+            launch_typed(k_binary<float, true, ND, I>, g, dev, (int)op, it, ops[0], ops[1], ops[2]);
+            return;
+          }
+          // bool logical ops are computed on 0/1 in uint8
+          switch (ct) {
+            case kBool:
+            case kU8: launch_typed(k_binary<uint8_t, false, ND, I>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
+            case kU16: launch_typed(k_binary<uint16_t, false, ND, I>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
+            case kU32: launch_typed(k_binary<uint32_t, false, ND, I>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
+            case kU64: launch_typed(k_binary<uint64_t, false, ND, I>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
+            case kI8: launch_typed(k_binary<int8_t, false, ND, I>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
+            case kI16: launch_typed(k_binary<int16_t, false, ND, I>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
+            case kI32: launch_typed(k_binary<int32_t, false, ND, I>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
+            default: launch_typed(k_binary<int64_t, false, ND, I>, g, dev, (int)op, it, ops[0], ops[1], ops[2]); break;
+          }
+        });
       }
       rc = launch_check("binary");
       if (rc) shlo_release(o);
@@ -551,19 +851,14 @@ int op_binary(uint32_t op, Arr *a, Arr *b, Arr **out) {
 
 // ------------------------------------------------------------ where ----
 
-template <typename C>
+template <typename C, int ND, typename I>
 __global__ void k_where(Iter it, Operand c, Operand x, Operand y, Operand z) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < it.n; i += stride) {
-    Operand ops[3] = {c, x, z};
-    int64_t off[3];
-    offsets<3>(it, ops, i, off);
-    Operand ops2[1] = {y};
-    int64_t offy[1];
-    offsets<1>(it, ops2, i, offy);
-    bool s = load_as<uint8_t>(c.ptr, c.dtype, off[0]) != 0;
-    C v = s ? load_as<C>(x.ptr, x.dtype, off[1]) : load_as<C>(y.ptr, y.dtype, offy[0]);
-    store_as<C>(const_cast<char *>(z.ptr), z.dtype, off[2], v);
+  GRID_LOOP(I, i, it.n) {
+    int64_t oc, ox, oy, oz;
+    offs4<ND, I>(it, c, x, y, z, i, oc, ox, oy, oz);
+    bool s = load_as<uint8_t>(c.ptr, c.dtype, oc) != 0;
+    C v = s ? load_as<C>(x.ptr, x.dtype, ox) : load_as<C>(y.ptr, y.dtype, oy);
+    store_as<C>(const_cast<char *>(z.ptr), z.dtype, oz, v);
   }
 }
 
@@ -579,7 +874,6 @@ int op_where(Arr *c, Arr *a, Arr *b, Arr **out) {
   int rc = broadcast_view(c, s2, n2, &vc) || broadcast_view(a, s2, n2, &va) || broadcast_view(b, s2, n2, &vb) ||
            new_array(dev, (uint8_t)ct, s2, n2, &o);
   if (!rc) {
-    // Iterate with the y operand kept separately (offsets<3> covers c, x, z).
     Iter it;
     Operand ops[4];
     Arr *ins[3] = {vc, va, vb};
@@ -601,10 +895,14 @@ int op_where(Arr *c, Arr *a, Arr *b, Arr **out) {
       for (int k = 0; k < 4; k++) ops[k].strides[0] = 1;
     }
     if (it.n > 0) {
-      unsigned g = grid_for(it.n, 256, dev);
-      if (dtype_is_float(ct)) launch_typed(k_where<float>, g, dev, it, ops[0], ops[1], ops[2], ops[3]);
-      else if (dtype_is_signed_int(ct)) launch_typed(k_where<int64_t>, g, dev, it, ops[0], ops[1], ops[2], ops[3]);
-      else launch_typed(k_where<uint64_t>, g, dev, it, ops[0], ops[1], ops[2], ops[3]);
+      unsigned g = grid_for(it.n, 256, dev, 16);
+      by_rank(it, [&](auto ndc, auto ic) {
+        constexpr int ND = decltype(ndc)::value;
+        using I = decltype(ic);
+        if (dtype_is_float(ct)) launch_typed(k_where<float, ND, I>, g, dev, it, ops[0], ops[1], ops[2], ops[3]);
+        else if (dtype_is_signed_int(ct)) launch_typed(k_where<int64_t, ND, I>, g, dev, it, ops[0], ops[1], ops[2], ops[3]);
+        else launch_typed(k_where<uint64_t, ND, I>, g, dev, it, ops[0], ops[1], ops[2], ops[3]);
+      });
       rc = launch_check("where");
     }
   }

@@ -717,6 +717,60 @@ __global__ void g_norm(const float *__restrict__ x, float *__restrict__ y, int n
   }
 }
 
+// The same computation with the warp's 32 rows resident in shared memory
+// (ncols <= 1024): all loads are issued at once as 16-byte vectors, the serial
+// chains then read shared memory (row pitch ncols + 1: conflict-free), and
+// the output is written with 16-byte stores.
+__global__ void __launch_bounds__(32) g_norm_smem(const float *__restrict__ x, float *__restrict__ y, int ncols,
+                                                  int64_t rows, float eps) {
+  extern __shared__ float tile[];  // [32][ncols + 1]
+  const int lane = threadIdx.x;
+  const int pitch = ncols + 1;
+  const int64_t r0 = (int64_t)blockIdx.x * 32;
+  const int nr = rows - r0 < 32 ? (int)(rows - r0) : 32;
+  const float *xb = x + r0 * ncols;
+  const int nv = nr * ncols / 4;  // float4 elements of the block (ncols % 4 == 0)
+  for (int v = lane; v < nv; v += 32) {
+    float4 t = reinterpret_cast<const float4 *>(xb)[v];
+    int e = v * 4, r = e / ncols, c = e - r * ncols;
+    float *d = tile + r * pitch + c;
+    d[0] = t.x; d[1] = t.y; d[2] = t.z; d[3] = t.w;
+  }
+  __syncwarp();
+  float mean = 0.0f, scl = 0.0f;
+  if (lane < nr) {
+    const float *row = tile + lane * pitch;
+    double sum = 0.0;
+    for (int c = 0; c < ncols; c++) sum = __dadd_rn(sum, (double)row[c]);
+    mean = __fdiv_rn(__double2float_rn(sum), (float)ncols);
+    double s2 = 0.0;
+    for (int c = 0; c < ncols; c += 4) {  // ncols % 4 == 0: no tail
+      float d0 = __fsub_rn(row[c], mean), d1 = __fsub_rn(row[c + 1], mean);
+      float d2 = __fsub_rn(row[c + 2], mean), d3 = __fsub_rn(row[c + 3], mean);
+      s2 = __dadd_rn(s2, (double)__fadd_rn(__fadd_rn(__fmul_rn(d0, d0), __fmul_rn(d1, d1)),
+                                           __fadd_rn(__fmul_rn(d2, d2), __fmul_rn(d3, d3))));
+    }
+    float var = __double2float_rn(__ddiv_rn(s2, (double)ncols));
+    scl = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+  }
+  __shared__ float ms[32], ss[32];
+  ms[lane] = mean;
+  ss[lane] = scl;
+  __syncwarp();
+  float *yb = y + r0 * ncols;
+  for (int v = lane; v < nv; v += 32) {
+    int e = v * 4, r = e / ncols, c = e - r * ncols;
+    const float *s = tile + r * pitch + c;
+    float m = ms[r], k = ss[r];
+    float4 o;
+    o.x = arm_nan(__fmul_rn(__fsub_rn(s[0], m), k));
+    o.y = arm_nan(__fmul_rn(__fsub_rn(s[1], m), k));
+    o.z = arm_nan(__fmul_rn(__fsub_rn(s[2], m), k));
+    o.w = arm_nan(__fmul_rn(__fsub_rn(s[3], m), k));
+    reinterpret_cast<float4 *>(yb)[v] = o;
+  }
+}
+
 int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
   const int64_t ncols = p[0], rows = p[1];
   const float eps = bitsf_host(p[2]);
@@ -725,7 +779,24 @@ int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
   int64_t shape[1] = {ncols * rows};
   Arr *o;
   SHLO_TRY(new_array(dev, kF32, shape, 1, &o));
-  if (ncols * rows > 0) {
+  const size_t smem = (size_t)32 * (ncols + 1) * sizeof(float);
+  if (ncols * rows > 0 && p[3] == 0 && ncols % 4 == 0 && ncols <= 1024) {
+    static bool attr_done[64] = {false};
+    if (!attr_done[dev->id]) {
+      if (cuda_check(cudaFuncSetAttribute(g_norm_smem, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          32 * 1025 * (int)sizeof(float)), "norm attribute")) {
+        shlo_release(o);
+        return 1;
+      }
+      attr_done[dev->id] = true;
+    }
+    g_norm_smem<<<(unsigned)((rows + 31) / 32), 32, smem, dev->stream>>>((const float *)data_ptr(x),
+                                                                          (float *)o->buf->ptr, (int)ncols, rows, eps);
+    if (launch_check("norm")) {
+      shlo_release(o);
+      return 1;
+    }
+  } else if (ncols * rows > 0) {
     int64_t nblk = (rows + 31) / 32;
     int64_t blocks = (nblk + 7) / 8;
     if (blocks > (int64_t)dev->sm_count * 8) blocks = (int64_t)dev->sm_count * 8;
