@@ -227,8 +227,12 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mul_mat_fast(MMArgs a) {
   using namespace mm;
   extern __shared__ __align__(16) float smem[];
   const int tid = threadIdx.x;
-  const int tm = tid & 31;   // m group: m = m0 + 4*tm + [0,4)
-  const int tn = tid >> 5;   // r group: r = r0 + 8*tn + [0,8)
+  // Warps tile the CTA 4 (m) x 2 (r); lanes tile a warp 8 (m) x 4 (r), so a
+  // warp's operand reads per k-step are one 128-byte w row and two 128-byte x
+  // rows (broadcast within the lane groups).
+  const int warp = tid >> 5, lane = tid & 31;
+  const int tm = (warp & 3) * 8 + (lane & 7);   // m group: m = m0 + 4*tm + [0,4)
+  const int tn = (warp >> 2) * 4 + (lane >> 3); // r group: r = r0 + 8*tn + [0,8)
   const int m0 = blockIdx.x * BM;
   const int bx = blockIdx.y / a.r_tiles;          // batch
   const int rt = blockIdx.y % a.r_tiles;
