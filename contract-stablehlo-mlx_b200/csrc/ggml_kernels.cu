@@ -1094,3 +1094,114 @@ int k_f32_of_f64(Device *dev, Arr *a, const uint32_t *p, Arr **out) {
 }
 
 }  // namespace shlo
+
+// ================================================= mul_mat without allocation ====
+// Some callers cannot let this library allocate device memory: a host runtime
+// whose device memory is all owned by its own allocator (a framework's caching
+// pool, a fixed arena), or one that must not allocate while it records work.
+// shlo_mul_mat_noalloc serves them: the caller passes the operands and the
+// output as device pointers, and the two packed operands of the fast path go to
+// the fixed scratch array below instead of to allocated storage. The array is
+// part of the library image: every GPU that loads the library holds it until
+// the process exits.
+
+namespace shlo {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)16 << 20;  // 16 MiB
+static __device__ __align__(256) float g_mm_noalloc_scratch[kNoAllocScratchBytes / sizeof(float)];
+
+// The scratch array's device address, looked up once per device with that device
+// current (in host code the array's name is only a host-side stand-in).
+static std::mutex g_noalloc_mu;
+static float *g_noalloc_ptr[64];
+
+static int noalloc_scratch(int dev, float **out) {
+  if (dev < 0 || dev >= 64) return fail("mul_mat_noalloc: device %d out of range", dev);
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void *p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_mm_noalloc_scratch);
+    if (e != cudaSuccess) return cuda_check(e, "mul_mat_noalloc: scratch address");
+    g_noalloc_ptr[dev] = (float *)p;
+  }
+  *out = g_noalloc_ptr[dev];
+  return 0;
+}
+
+}  // namespace shlo
+
+extern "C" int shlo_mul_mat_noalloc(const float *w, const float *x, float *y, int64_t K, int64_t M, int64_t R,
+                                    int64_t N, int64_t w_batch_stride, void *stream) {
+  using namespace shlo;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (!w || !x || !y) return fail("mul_mat_noalloc: null pointer");
+  if (K <= 0 || M <= 0 || R < 0 || N <= 0 || R % N)
+    return fail("mul_mat_noalloc: K=%lld M=%lld R=%lld N=%lld not carried", (long long)K, (long long)M, (long long)R,
+                (long long)N);
+  const int64_t wbs = w_batch_stride;
+  if (wbs && wbs < M * K) return fail("mul_mat_noalloc: w batch stride %lld below M*K", (long long)wbs);
+  if (K > INT32_MAX || M > INT32_MAX) return fail("mul_mat_noalloc: K or M too large");
+  if (R * M == 0) return 0;
+  int devid = 0;
+  SHLO_CUDA(cudaGetDevice(&devid));
+  const int flavor = current_flavor();
+  const int64_t np = K & ~(int64_t)15;
+  if (np < 16) {  // all tail: the one-output-per-thread kernel needs no scratch
+    int sms = 0;
+    SHLO_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, devid));
+    int64_t blocks = (R * M + 255) / 256;
+    if (blocks > (int64_t)sms * 8) blocks = (int64_t)sms * 8;
+    k_mul_mat_naive<<<(unsigned)blocks, 256, 0, s>>>(w, x, y, (int)K, (int)M, R, N, wbs, 0, flavor);
+    return launch_check("mul_mat_noalloc");
+  }
+  const int64_t nb = R / N;
+  const int seg = (int)(np / 16);
+  const int segp = (seg + 3) & ~3;
+  const int Mp = (int)((M + mm::BM - 1) / mm::BM * mm::BM);
+  const int64_t Bx = wbs ? nb : 1;
+  const int64_t Nx = wbs ? N : R;
+  const int Np = (int)((Nx + mm::BN - 1) / mm::BN * mm::BN);
+  const int64_t Wb = wbs ? nb : 1;
+  const int64_t w_floats = Wb * 16 * segp * (int64_t)Mp;
+  const int64_t x_floats = Bx * 16 * segp * (int64_t)Np;
+  const int64_t need = (w_floats + x_floats) * (int64_t)sizeof(float);
+  if (need > (int64_t)kNoAllocScratchBytes)
+    return fail("mul_mat_noalloc: the packed operands need %lld bytes of scratch, above the %zu-byte maximum of this "
+                "entry point (use the allocating kernel for larger shapes)", (long long)need, kNoAllocScratchBytes);
+  float *scratch;
+  SHLO_TRY(noalloc_scratch(devid, &scratch));
+  // Both packed regions are written in full by the pack kernels (padding
+  // included), so nothing in the scratch array has to start at zero.
+  float *wp = scratch, *xp = scratch + w_floats;
+  {
+    dim3 grid((Mp + 31) / 32, (segp + 7) / 8, (unsigned)Wb);
+    k_mm_pack<<<grid, 256, 0, s>>>(w, (int)M, (int)K, wbs, seg, segp, Mp, -0.0f, wp);
+    SHLO_TRY(launch_check("mul_mat_noalloc pack"));
+  }
+  {
+    dim3 grid((Np + 31) / 32, (segp + 7) / 8, (unsigned)Bx);
+    k_mm_pack<<<grid, 256, 0, s>>>(x, (int)Nx, (int)K, Nx * K, seg, segp, Np, 0.0f, xp);
+    SHLO_TRY(launch_check("mul_mat_noalloc pack"));
+  }
+  MMArgs a;
+  a.wp = wp;
+  a.xp = xp;
+  a.w = w;
+  a.x = x;
+  a.y = y;
+  a.K = (int)K;
+  a.M = (int)M;
+  a.np = (int)np;
+  a.segp = segp;
+  a.Mp = Mp;
+  a.Np = Np;
+  a.Nx = Nx;
+  a.wbs = wbs;
+  a.r_tiles = Np / mm::BN;
+  a.flavor = flavor;
+  const size_t smem = (size_t)mm::NS * mm::STAGE_FLOATS * sizeof(float);
+  SHLO_CUDA(cudaFuncSetAttribute(k_mul_mat_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  dim3 grid(Mp / mm::BM, (unsigned)(Bx * a.r_tiles));
+  k_mul_mat_fast<<<grid, mm::THREADS, smem, s>>>(a);
+  return launch_check("mul_mat_noalloc");
+}

@@ -162,6 +162,24 @@ int shlo_current_stream(void **stream);
 /* How many kernels this library has launched since it was loaded, all devices. */
 int shlo_launch_count(uint64_t *count);
 
+/* ---- mul_mat for callers that cannot allocate (no counterpart in the reference) ----
+   The same product as the "smlx_mul_mat" kernel (ggml_vec_dot_f32 order, the
+   current ggml build; parameters as Run.lean's mulMat: y[r*M+m] = dot of w row
+   (r/N)*w_batch_stride + m*K and x row r), for callers whose device memory is
+   not this library's to allocate -- a runtime whose GPU memory is all held by
+   its own pool or arena, or one that must not allocate while it records work.
+   w, x and y are device pointers on the current device (float32, row-major,
+   caller-owned); the work is queued on `stream` (a cudaStream_t; NULL is the
+   default stream). The packed operands go to one fixed 16 MiB scratch array
+   that every GPU loading this library holds until exit; shapes whose packed
+   operands need more are rejected with an error. The first call on a device
+   looks up the array's address (make it before any stream capture). All calls
+   on a device share the array, so calls that overlap on the GPU race: queue
+   them on one stream. Nothing is allocated: no cudaMalloc, cudaFree or
+   allocating library call. */
+int shlo_mul_mat_noalloc(const float *w, const float *x, float *y, int64_t K, int64_t M, int64_t R, int64_t N,
+                         int64_t w_batch_stride, void *stream);
+
 /* ---- test-driver helpers (Mlx.lean:69-73) ---- */
 
 /* smlx_libm_erff_range: this platform's binary32 erff over `count`
