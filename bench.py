@@ -50,6 +50,10 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--impl", default="shlo", choices=["shlo", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    # Short runs to wrap in a profiler (no JSON line): one warm denoiser step, or
+    # mul_mat alone at --mm-shape K,M,R.
+    ap.add_argument("--profile-run", choices=["step", "mul_mat"])
+    ap.add_argument("--mm-shape", default="512,1536,16384")
     return ap.parse_args()
 
 
@@ -386,8 +390,43 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def profile_run(args):
+    """A short, fixed piece of work for `ncu` to capture (see profiles/)."""
+    import shlo  # noqa: F401
+    from shlo import denoiser as D
+    from shlo import exec as E
+    from shlo import mlx as M
+    from shlo import run as Run
+
+    M.set_flavor("pinned")
+    if args.profile_run == "step":
+        cfg = D.Config(layers=args.layers)
+        B = args.batch_per_gpu
+        w = D.init_weights(cfg, seed=1)
+        W = [M.of_numpy(w[n]) for n, _ in D.weight_specs(cfg)]
+        X = [M.of_numpy(a) for a in D.inputs(cfg, B, seed=1)]
+        fn = E.prepare(E.load(D.module_text(cfg, B)), None, True)
+        c0 = M.launch_count()
+        M.eval_([M.apply(fn, X + W)[0]])  # warm-up step
+        c1 = M.launch_count()
+        M.eval_([M.apply(fn, X + W)[0]])  # the captured step
+        print("launches: warm-up %d, step %d" % (c1 - c0, M.launch_count() - c1))
+    else:
+        K, Mm, R = (int(v) for v in args.mm_shape.split(","))
+        rng = np.random.default_rng(0)
+        wa = M.of_numpy(rng.standard_normal((Mm, K)).astype(np.float32))
+        xa = M.of_numpy(rng.standard_normal((R, K)).astype(np.float32))
+        for _ in range(3):
+            y = Run.mul_mat(wa, xa, K, Mm, R, R, 0)
+        M.eval_([y])
+        print("mul_mat %s: 3 launches" % args.mm_shape)
+
+
 def main():
     args = parse_args()
+    if args.profile_run:
+        profile_run(args)
+        return
     if args.impl == "reference":
         run_reference(args)
     else:
