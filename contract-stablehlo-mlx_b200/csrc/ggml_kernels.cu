@@ -343,6 +343,214 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mul_mat_fast(MMArgs a) {
   }
 }
 
+// ------------------------------------------------ the TMEM-stack mul_mat ----
+// The same packed-segment algorithm with an 8 x 8 tile per thread (CTA tile
+// 128 m x 128 r): the four stack levels of the reduction tree (64 values each per
+// thread) live in Tensor Memory instead of registers. Warp w reaches TMEM lanes
+// [32 (w % 4), +32); warps w and w + 4 share those lanes and split the 512
+// columns: columns 256 (w / 4) + 64 L + [0, 64) hold level L. The stack is
+// touched only at segment boundaries.
+namespace mt {
+constexpr int BM = 128, BN = 128, BK = 16, NS = 6, THREADS = 256;
+constexpr int STAGE_FLOATS = BK * (BM + BN);
+constexpr int TMEM_COLS = 512;
+// More dynamic shared memory than half an SM's: one CTA per SM, since each CTA
+// holds all 512 TMEM columns.
+constexpr size_t SMEM_BYTES = 120 * 1024;
+static_assert((size_t)NS * STAGE_FLOATS * sizeof(float) <= SMEM_BYTES, "stages fit");
+}  // namespace mt
+
+// 16 consecutive 32-bit TMEM columns of this thread's lane, stored / loaded
+// (32x32b shape: lane = the thread's lane in the warp's quarter). Each waits for
+// its own completion inside the same asm statement, so the registers are never
+// used before they are valid.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float *v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n"
+               "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+               "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+               "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+               "r"(__float_as_uint(v[15]))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
+  uint32_t r[16];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n"
+               "tcgen05.wait::ld.sync.aligned;\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+               : "r"(taddr)
+               : "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Fold the finished chain of leaf S into the TMEM stack: pop and add the levels
+// below the first zero bit of S (the left operand is the older value, as in the
+// tree), then push at that level; at S = 15 the result stays in acc (sumf).
+template <int S>
+__device__ __forceinline__ void tfold(float (&acc)[64], uint32_t tcol) {
+  constexpr int depth = (S & 1) == 0 ? 0 : (S & 3) != 3 ? 1 : (S & 7) != 7 ? 2 : (S & 15) != 15 ? 3 : 4;
+#pragma unroll
+  for (int c = 0; c < 4; c++) {
+#pragma unroll
+    for (int L = 0; L < depth; L++) {
+      float t[16];
+      tmem_ld16(tcol + 64 * L + 16 * c, t);
+#pragma unroll
+      for (int i = 0; i < 16; i++) acc[16 * c + i] = __fadd_rn(t[i], acc[16 * c + i]);
+    }
+    if (depth < 4) tmem_st16(tcol + 64 * depth + 16 * c, acc + 16 * c);
+  }
+}
+
+__global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
+  using namespace mt;
+  extern __shared__ __align__(16) float smem[];
+  __shared__ uint32_t tmem_base;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // Warps 2 (m) x 4 (r), lanes 8 (m) x 4 (r); a thread's m are mo + [0,4) and
+  // mo + 32 + [0,4), its r are ro + [0,4) and ro + 16 + [0,4).
+  const int mo = (warp & 1) * 64 + (lane & 7) * 4;
+  const int ro = (warp >> 1) * 32 + (lane >> 3) * 4;
+  const int m0 = blockIdx.x * BM;
+  const int bx = blockIdx.y / a.r_tiles;
+  const int rt = blockIdx.y % a.r_tiles;
+  const int64_t rl0 = (int64_t)rt * BN;
+  const int Kq = 16 * a.segp;
+  const float *wp = a.wp + (a.wbs ? (int64_t)bx * Kq * a.Mp : 0) + m0;
+  const float *xp = a.xp + (int64_t)bx * Kq * a.Np + rl0;
+  const int nstages = Kq / BK;
+
+  if (warp == 0) {
+    uint32_t slot = (uint32_t)__cvta_generic_to_shared(&tmem_base);
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(slot),
+                 "n"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+  }
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  const uint32_t tcol = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(256 * (warp >> 2));
+
+  auto issue = [&](int st) {
+    float *ws = smem + (st % NS) * STAGE_FLOATS;
+    float *xs = ws + BK * BM;
+    const int k0 = st * BK;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      int q = tid + i * THREADS;
+      if (q < BK * BM / 4) {
+        int row = q >> 5, col = (q & 31) * 4;
+        cp_async16(ws + row * BM + col, wp + (int64_t)(k0 + row) * a.Mp + col);
+      } else {
+        q -= BK * BM / 4;
+        int row = q >> 5, col = (q & 31) * 4;
+        cp_async16(xs + row * BN + col, xp + (int64_t)(k0 + row) * a.Np + col);
+      }
+    }
+  };
+
+#pragma unroll
+  for (int s = 0; s < NS - 1; s++) {
+    if (s < nstages) issue(s);
+    cp_async_commit();
+  }
+
+  float acc[64];
+  const int groups_per_seg = a.segp / 4;
+  int g = 0;
+#pragma unroll
+  for (int S = 0; S < 16; S++) {
+#pragma unroll
+    for (int i = 0; i < 64; i++) acc[i] = 0.0f;
+    for (int gi = 0; gi < groups_per_seg; gi++, g++) {
+      const int stg = g >> 2;
+      if ((g & 3) == 0) {
+        cp_async_wait<NS - 2>();
+        __syncthreads();
+        if (stg + NS - 1 < nstages) issue(stg + NS - 1);
+        cp_async_commit();
+      }
+      const float *ws = smem + (stg % NS) * STAGE_FLOATS + (g & 3) * 4 * BM;
+      const float *xs = smem + (stg % NS) * STAGE_FLOATS + BK * BM + (g & 3) * 4 * BN;
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        const float4 w0 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo);
+        const float4 w1 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo + 32);
+        const float4 x0 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro);
+        const float4 x1 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro + 16);
+        const float wr[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+        const float xr[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int j = 0; j < 8; j++)
+#pragma unroll
+          for (int i = 0; i < 8; i++) acc[j * 8 + i] = __fmaf_rn(wr[i], xr[j], acc[j * 8 + i]);
+      }
+    }
+    switch (S) {
+      case 0: tfold<0>(acc, tcol); break;
+      case 1: tfold<1>(acc, tcol); break;
+      case 2: tfold<2>(acc, tcol); break;
+      case 3: tfold<3>(acc, tcol); break;
+      case 4: tfold<4>(acc, tcol); break;
+      case 5: tfold<5>(acc, tcol); break;
+      case 6: tfold<6>(acc, tcol); break;
+      case 7: tfold<7>(acc, tcol); break;
+      case 8: tfold<8>(acc, tcol); break;
+      case 9: tfold<9>(acc, tcol); break;
+      case 10: tfold<10>(acc, tcol); break;
+      case 11: tfold<11>(acc, tcol); break;
+      case 12: tfold<12>(acc, tcol); break;
+      case 13: tfold<13>(acc, tcol); break;
+      case 14: tfold<14>(acc, tcol); break;
+      default: tfold<15>(acc, tcol); break;
+    }
+  }
+  cp_async_wait<0>();
+
+  // Every TMEM access of this CTA is complete (each waited): free the columns.
+  asm volatile("tcgen05.fence::before_thread_sync;\n");
+  __syncthreads();
+  asm volatile("tcgen05.fence::after_thread_sync;\n");
+  if (warp == 0)
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_base), "n"(TMEM_COLS));
+
+  // Epilogue: the tail (K mod 16 elements, in order) and the store.
+  const int64_t rbase = (int64_t)bx * a.Nx;
+  const bool vec = (a.M & 3) == 0;
+#pragma unroll
+  for (int j = 0; j < 8; j++) {
+    const int64_t rl = rl0 + ro + (j & 3) + (j >> 2) * 16;
+    if (rl >= a.Nx) continue;
+    const int64_t r = rbase + rl;
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int mb = m0 + mo + 32 * h;
+      float v[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        v[i] = acc[j * 8 + 4 * h + i];
+        const int m = mb + i;
+        if (a.np < a.K && m < a.M) {
+          const float *wr = a.w + (a.wbs ? (int64_t)bx * a.wbs : 0) + (int64_t)m * a.K;
+          v[i] = dot_tail(wr, a.x + r * a.K, a.np, a.K, v[i], a.flavor);
+        }
+        v[i] = arm_nan(v[i]);
+      }
+      if (vec && mb + 3 < a.M) {
+        *reinterpret_cast<float4 *>(a.y + r * a.M + mb) = make_float4(v[0], v[1], v[2], v[3]);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          if (mb + i < a.M) a.y[r * a.M + mb + i] = v[i];
+      }
+    }
+  }
+}
+
 // $SHLO_MUL_MAT_PATH = naive | fast forces one of the two exact paths (both give
 // the same bits; the tests run each); unset, the size decides.
 static int mm_path() {
@@ -398,10 +606,10 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
   }
   const int seg = (int)(np / 16);
   const int segp = (seg + 3) & ~3;
-  const int Mp = (int)((M + mm::BM - 1) / mm::BM * mm::BM);
+  const int Mp = (int)((M + mt::BM - 1) / mt::BM * mt::BM);
   const int64_t Bx = wbs ? nb : 1;
   const int64_t Nx = wbs ? N : R;
-  const int Np = (int)((Nx + mm::BN - 1) / mm::BN * mm::BN);
+  const int Np = (int)((Nx + mt::BN - 1) / mt::BN * mt::BN);
   const int Wb = wbs ? (int)nb : 1;
   // The packed w is derived from w's storage, which never changes: keep it.
   Buffer *wpk = nullptr;
@@ -445,12 +653,12 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
   a.Np = Np;
   a.Nx = Nx;
   a.wbs = wbs;
-  a.r_tiles = Np / mm::BN;
+  a.r_tiles = Np / mt::BN;
   a.flavor = flavor;
-  const size_t smem = (size_t)mm::NS * mm::STAGE_FLOATS * sizeof(float);
+  const size_t smem = mt::SMEM_BYTES;
   static bool attr_done[64] = {false};
   if (!attr_done[dev->id]) {
-    if (cuda_check(cudaFuncSetAttribute(k_mul_mat_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+    if (cuda_check(cudaFuncSetAttribute(k_mul_mat_tm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                    "mul_mat attribute")) {
       buffer_release(wpk);
       buffer_release(xpk);
@@ -459,8 +667,8 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
     }
     attr_done[dev->id] = true;
   }
-  dim3 grid(Mp / mm::BM, (unsigned)(Bx * a.r_tiles));
-  k_mul_mat_fast<<<grid, mm::THREADS, smem, dev->stream>>>(a);
+  dim3 grid(Mp / mt::BM, (unsigned)(Bx * a.r_tiles));
+  k_mul_mat_tm<<<grid, mt::THREADS, smem, dev->stream>>>(a);
   int rc = launch_check("mul_mat");
   buffer_release(wpk);
   buffer_release(xpk);
