@@ -390,12 +390,10 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
 // Fold the finished chain of leaf S into the TMEM stack: pop and add the levels
 // below the first zero bit of S (the left operand is the older value, as in the
 // tree), then push at that level; at S = 15 the result stays in acc (sumf).
-template <int S>
-__device__ __forceinline__ void tfold(float (&acc)[64], uint32_t tcol) {
-  constexpr int depth = (S & 1) == 0 ? 0 : (S & 3) != 3 ? 1 : (S & 7) != 7 ? 2 : (S & 15) != 15 ? 3 : 4;
+__device__ __forceinline__ void tfold_rt(float (&acc)[64], uint32_t tcol, int S) {
+  const int depth = __ffs(~S) - 1;  // trailing one bits: 0..4
 #pragma unroll
   for (int c = 0; c < 4; c++) {
-#pragma unroll
     for (int L = 0; L < depth; L++) {
       float t[16];
       tmem_ld16(tcol + 64 * L + 16 * c, t);
@@ -459,54 +457,45 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
     cp_async_commit();
   }
 
+  // One flat loop over all groups of 4 packed k-steps; the chain of segment S
+  // ends every segp/4 groups and folds into the TMEM stack (a runtime depth:
+  // the number of trailing one bits of S), so the hot body exists once.
   float acc[64];
+#pragma unroll
+  for (int i = 0; i < 64; i++) acc[i] = 0.0f;
   const int groups_per_seg = a.segp / 4;
-  int g = 0;
-#pragma unroll
-  for (int S = 0; S < 16; S++) {
-#pragma unroll
-    for (int i = 0; i < 64; i++) acc[i] = 0.0f;
-    for (int gi = 0; gi < groups_per_seg; gi++, g++) {
-      const int stg = g >> 2;
-      if ((g & 3) == 0) {
-        cp_async_wait<NS - 2>();
-        __syncthreads();
-        if (stg + NS - 1 < nstages) issue(stg + NS - 1);
-        cp_async_commit();
-      }
-      const float *ws = smem + (stg % NS) * STAGE_FLOATS + (g & 3) * 4 * BM;
-      const float *xs = smem + (stg % NS) * STAGE_FLOATS + BK * BM + (g & 3) * 4 * BN;
-#pragma unroll
-      for (int kk = 0; kk < 4; kk++) {
-        const float4 w0 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo);
-        const float4 w1 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo + 32);
-        const float4 x0 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro);
-        const float4 x1 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro + 16);
-        const float wr[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        const float xr[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-        for (int j = 0; j < 8; j++)
-#pragma unroll
-          for (int i = 0; i < 8; i++) acc[j * 8 + i] = __fmaf_rn(wr[i], xr[j], acc[j * 8 + i]);
-      }
+  const int ngroups = 16 * groups_per_seg;
+  int S = 0, gi = 0;
+  for (int g = 0; g < ngroups; g++) {
+    const int stg = g >> 2;
+    if ((g & 3) == 0) {
+      cp_async_wait<NS - 2>();
+      __syncthreads();
+      if (stg + NS - 1 < nstages) issue(stg + NS - 1);
+      cp_async_commit();
     }
-    switch (S) {
-      case 0: tfold<0>(acc, tcol); break;
-      case 1: tfold<1>(acc, tcol); break;
-      case 2: tfold<2>(acc, tcol); break;
-      case 3: tfold<3>(acc, tcol); break;
-      case 4: tfold<4>(acc, tcol); break;
-      case 5: tfold<5>(acc, tcol); break;
-      case 6: tfold<6>(acc, tcol); break;
-      case 7: tfold<7>(acc, tcol); break;
-      case 8: tfold<8>(acc, tcol); break;
-      case 9: tfold<9>(acc, tcol); break;
-      case 10: tfold<10>(acc, tcol); break;
-      case 11: tfold<11>(acc, tcol); break;
-      case 12: tfold<12>(acc, tcol); break;
-      case 13: tfold<13>(acc, tcol); break;
-      case 14: tfold<14>(acc, tcol); break;
-      default: tfold<15>(acc, tcol); break;
+    const float *ws = smem + (stg % NS) * STAGE_FLOATS + (g & 3) * 4 * BM;
+    const float *xs = smem + (stg % NS) * STAGE_FLOATS + BK * BM + (g & 3) * 4 * BN;
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+      const float4 w0 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo);
+      const float4 w1 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo + 32);
+      const float4 x0 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro);
+      const float4 x1 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro + 16);
+      const float wr[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      const float xr[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+      for (int j = 0; j < 8; j++)
+#pragma unroll
+        for (int i = 0; i < 8; i++) acc[j * 8 + i] = __fmaf_rn(wr[i], xr[j], acc[j * 8 + i]);
+    }
+    if (++gi == groups_per_seg) {
+      tfold_rt(acc, tcol, S);
+      gi = 0;
+      if (++S < 16) {
+#pragma unroll
+        for (int i = 0; i < 64; i++) acc[i] = 0.0f;
+      }
     }
   }
   cp_async_wait<0>();
