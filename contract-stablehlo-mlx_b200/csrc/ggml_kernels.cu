@@ -390,17 +390,25 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
 // Fold the finished chain of leaf S into the TMEM stack: pop and add the levels
 // below the first zero bit of S (the left operand is the older value, as in the
 // tree), then push at that level; at S = 15 the result stays in acc (sumf).
-__device__ __forceinline__ void tfold_rt(float (&acc)[64], uint32_t tcol, int S) {
+__device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, int S) {
   const int depth = __ffs(~S) - 1;  // trailing one bits: 0..4
 #pragma unroll
   for (int c = 0; c < 4; c++) {
+    float v[16];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      v[2 * q] = acc2[8 * c + q].x;
+      v[2 * q + 1] = acc2[8 * c + q].y;
+    }
     for (int L = 0; L < depth; L++) {
       float t[16];
       tmem_ld16(tcol + 64 * L + 16 * c, t);
 #pragma unroll
-      for (int i = 0; i < 16; i++) acc[16 * c + i] = __fadd_rn(t[i], acc[16 * c + i]);
+      for (int i = 0; i < 16; i++) v[i] = __fadd_rn(t[i], v[i]);
     }
-    if (depth < 4) tmem_st16(tcol + 64 * depth + 16 * c, acc + 16 * c);
+    if (depth < 4) tmem_st16(tcol + 64 * depth + 16 * c, v);
+#pragma unroll
+    for (int q = 0; q < 8; q++) acc2[8 * c + q] = make_float2(v[2 * q], v[2 * q + 1]);
   }
 }
 
@@ -460,9 +468,10 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
   // One flat loop over all groups of 4 packed k-steps; the chain of segment S
   // ends every segp/4 groups and folds into the TMEM stack (a runtime depth:
   // the number of trailing one bits of S), so the hot body exists once.
-  float acc[64];
+  // acc[j][i] (r index j, m index i) lives in pairs along m: acc2[4 j + i / 2].
+  float2 acc2[32];
 #pragma unroll
-  for (int i = 0; i < 64; i++) acc[i] = 0.0f;
+  for (int i = 0; i < 32; i++) acc2[i] = make_float2(0.0f, 0.0f);
   const int groups_per_seg = a.segp / 4;
   const int ngroups = 16 * groups_per_seg;
   int S = 0, gi = 0;
@@ -482,19 +491,23 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
       const float4 w1 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo + 32);
       const float4 x0 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro);
       const float4 x1 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro + 16);
-      const float wr[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+      // Paired FP32 FMAs: each component rounds exactly as __fmaf_rn.
+      const float2 wp2[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                             make_float2(w1.z, w1.w)};
       const float xr[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
-      for (int j = 0; j < 8; j++)
+      for (int j = 0; j < 8; j++) {
+        const float2 xj = make_float2(xr[j], xr[j]);
 #pragma unroll
-        for (int i = 0; i < 8; i++) acc[j * 8 + i] = __fmaf_rn(wr[i], xr[j], acc[j * 8 + i]);
+        for (int i = 0; i < 4; i++) acc2[j * 4 + i] = __ffma2_rn(wp2[i], xj, acc2[j * 4 + i]);
+      }
     }
     if (++gi == groups_per_seg) {
-      tfold_rt(acc, tcol, S);
+      tfold_rt(acc2, tcol, S);
       gi = 0;
       if (++S < 16) {
 #pragma unroll
-        for (int i = 0; i < 64; i++) acc[i] = 0.0f;
+        for (int i = 0; i < 32; i++) acc2[i] = make_float2(0.0f, 0.0f);
       }
     }
   }
@@ -521,7 +534,8 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
       float v[4];
 #pragma unroll
       for (int i = 0; i < 4; i++) {
-        v[i] = acc[j * 8 + 4 * h + i];
+        const float2 pr = acc2[j * 4 + 2 * h + (i >> 1)];
+        v[i] = (i & 1) ? pr.y : pr.x;
         const int m = mb + i;
         if (a.np < a.K && m < a.M) {
           const float *wr = a.w + (a.wbs ? (int64_t)bx * a.wbs : 0) + (int64_t)m * a.K;
