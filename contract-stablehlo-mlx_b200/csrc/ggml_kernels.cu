@@ -169,37 +169,6 @@ __global__ void k_mm_pack(const float *__restrict__ src, int rows, int K, int64_
   }
 }
 
-// The same packing with every value written twice, as a pair (v, v): the
-// TMEM-stack kernel multiplies pairs of w by such a pair with one paired FMA, so
-// the pair comes ready-made from shared memory. dst is [batch][Kq][rows_p] float2.
-__global__ void k_mm_pack_pairs(const float *__restrict__ src, int rows, int K, int64_t src_batch, int seg, int segp,
-                                int rows_p, float2 *__restrict__ dst) {
-  __shared__ float tile[32][129];
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const int r0 = blockIdx.x * 32;
-  const int c0 = blockIdx.y * 8;
-  const int b = blockIdx.z;
-  const int Kq = 16 * segp;
-  const float *s = src + (int64_t)b * src_batch;
-  for (int rr = ty; rr < 32; rr += 8) {
-    int r = r0 + rr;
-    for (int kk = tx; kk < 128; kk += 32) {
-      float v = 0.0f;
-      if (r < rows && (c0 + kk / 16) < seg) v = s[(int64_t)r * K + (c0 * 16) + kk];
-      tile[rr][kk] = v;
-    }
-  }
-  __syncthreads();
-  float2 *d = dst + (int64_t)b * Kq * rows_p;
-  for (int o = ty; o < 128; o += 8) {
-    int j = o >> 3, c = o & 7;
-    int cg = c0 + c;
-    if (cg >= segp) continue;
-    float v = cg < seg ? tile[tx][16 * c + j] : 0.0f;
-    d[(int64_t)(leaf_of_class(j) * segp + cg) * rows_p + r0 + tx] = make_float2(v, v);
-  }
-}
-
 namespace mm {
 constexpr int BM = 128;  // w rows (m) per CTA
 constexpr int BN = 64;   // x rows (r) per CTA
@@ -382,8 +351,8 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mul_mat_fast(MMArgs a) {
 // columns: columns 256 (w / 4) + 64 L + [0, 64) hold level L. The stack is
 // touched only at segment boundaries.
 namespace mt {
-constexpr int BM = 128, BN = 128, BK = 16, NS = 5, THREADS = 256;
-constexpr int STAGE_FLOATS = BK * (BM + 2 * BN);  // w, and x as (v, v) pairs
+constexpr int BM = 128, BN = 128, BK = 16, NS = 6, THREADS = 256;
+constexpr int STAGE_FLOATS = BK * (BM + BN);
 constexpr int TMEM_COLS = 512;
 // More dynamic shared memory than half an SM's: one CTA per SM, since each CTA
 // holds all 512 TMEM columns.
@@ -458,8 +427,7 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
   const int64_t rl0 = (int64_t)rt * BN;
   const int Kq = 16 * a.segp;
   const float *wp = a.wp + (a.wbs ? (int64_t)bx * Kq * a.Mp : 0) + m0;
-  // x is packed as pairs (v, v): a.xp points at float2 [Bx][Kq][Np].
-  const float2 *xp = reinterpret_cast<const float2 *>(a.xp) + (int64_t)bx * Kq * a.Np + rl0;
+  const float *xp = a.xp + (int64_t)bx * Kq * a.Np + rl0;
   const int nstages = Kq / BK;
 
   if (warp == 0) {
@@ -475,18 +443,17 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
 
   auto issue = [&](int st) {
     float *ws = smem + (st % NS) * STAGE_FLOATS;
-    float2 *xs = reinterpret_cast<float2 *>(ws + BK * BM);
+    float *xs = ws + BK * BM;
     const int k0 = st * BK;
-    // 16 x 128 floats of w and 16 x 128 pairs of x: 1536 16-byte copies, six per thread.
 #pragma unroll
-    for (int i = 0; i < 6; i++) {
+    for (int i = 0; i < 4; i++) {
       int q = tid + i * THREADS;
       if (q < BK * BM / 4) {
         int row = q >> 5, col = (q & 31) * 4;
         cp_async16(ws + row * BM + col, wp + (int64_t)(k0 + row) * a.Mp + col);
       } else {
         q -= BK * BM / 4;
-        int row = q >> 6, col = (q & 63) * 2;
+        int row = q >> 5, col = (q & 31) * 4;
         cp_async16(xs + row * BN + col, xp + (int64_t)(k0 + row) * a.Np + col);
       }
     }
@@ -511,11 +478,11 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
   // Operands of the current k-step in registers; the next k-step's are loaded
   // before the current one's FMAs (software pipelining), except across a stage
   // boundary, where the loads follow the barrier.
-  float4 cw0, cw1, cx[4], nw0, nw1, nx[4];
+  float4 cw0, cw1, cx0, cx1;
   for (int g = 0; g < ngroups; g++) {
     const int stg = g >> 2;
     const float *wst = smem + (stg % NS) * STAGE_FLOATS;
-    const float2 *xst = reinterpret_cast<const float2 *>(wst + BK * BM);
+    const float *xst = wst + BK * BM;
     if ((g & 3) == 0) {
       cp_async_wait<NS - 2>();
       __syncthreads();
@@ -523,41 +490,36 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
       cp_async_commit();
       cw0 = *reinterpret_cast<const float4 *>(wst + mo);
       cw1 = *reinterpret_cast<const float4 *>(wst + mo + 32);
-#pragma unroll
-      for (int q = 0; q < 4; q++)
-        cx[q] = *reinterpret_cast<const float4 *>(xst + ro + (q >> 1) * 16 + (q & 1) * 2);
+      cx0 = *reinterpret_cast<const float4 *>(xst + ro);
+      cx1 = *reinterpret_cast<const float4 *>(xst + ro + 16);
     }
     const int row0 = (g & 3) * 4;
 #pragma unroll
     for (int kk = 0; kk < 4; kk++) {
+      float4 nw0, nw1, nx0, nx1;
       const bool pre = kk < 3 || (g & 3) != 3;
       if (pre) {
         const int rn = row0 + kk + 1;  // next k-step row within this stage
         nw0 = *reinterpret_cast<const float4 *>(wst + rn * BM + mo);
         nw1 = *reinterpret_cast<const float4 *>(wst + rn * BM + mo + 32);
-#pragma unroll
-        for (int q = 0; q < 4; q++)
-          nx[q] = *reinterpret_cast<const float4 *>(xst + rn * BN + ro + (q >> 1) * 16 + (q & 1) * 2);
+        nx0 = *reinterpret_cast<const float4 *>(xst + rn * BN + ro);
+        nx1 = *reinterpret_cast<const float4 *>(xst + rn * BN + ro + 16);
       }
-      // Paired FP32 FMAs: each component rounds exactly as __fmaf_rn. r index
-      // j = 4 (q >> 1) + 2 (q & 1) + half: x pair (x_j, x_j) is cx[q].xy or .zw.
+      // Paired FP32 FMAs: each component rounds exactly as __fmaf_rn.
       const float2 wp2[4] = {make_float2(cw0.x, cw0.y), make_float2(cw0.z, cw0.w), make_float2(cw1.x, cw1.y),
                              make_float2(cw1.z, cw1.w)};
+      const float xr[8] = {cx0.x, cx0.y, cx0.z, cx0.w, cx1.x, cx1.y, cx1.z, cx1.w};
 #pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const float2 xa = make_float2(cx[q].x, cx[q].y), xb = make_float2(cx[q].z, cx[q].w);
-        const int ja = 4 * (q >> 1) + 2 * (q & 1), jb = ja + 1;
+      for (int j = 0; j < 8; j++) {
+        const float2 xj = make_float2(xr[j], xr[j]);
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-          acc2[ja * 4 + i] = __ffma2_rn(wp2[i], xa, acc2[ja * 4 + i]);
-          acc2[jb * 4 + i] = __ffma2_rn(wp2[i], xb, acc2[jb * 4 + i]);
-        }
+        for (int i = 0; i < 4; i++) acc2[j * 4 + i] = __ffma2_rn(wp2[i], xj, acc2[j * 4 + i]);
       }
       if (pre) {
         cw0 = nw0;
         cw1 = nw1;
-#pragma unroll
-        for (int q = 0; q < 4; q++) cx[q] = nx[q];
+        cx0 = nx0;
+        cx1 = nx1;
       }
     }
     if (++gi == groups_per_seg) {
@@ -695,22 +657,10 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
     }
   }
   Buffer *xpk;
-  // x as (v, v) pairs for the paired FMAs of the TMEM-stack kernel.
-  if (buffer_alloc(dev, (size_t)Bx * 16 * segp * Np * sizeof(float2), &xpk)) {
+  if (pack_operand(dev, (const float *)data_ptr(x), (int)Nx, (int)K, Nx * K, (int)Bx, seg, segp, Np, 0.0f, &xpk)) {
     buffer_release(wpk);
     shlo_release(o);
     return 1;
-  }
-  {
-    dim3 pg((Np + 31) / 32, (segp + 7) / 8, (unsigned)Bx);
-    k_mm_pack_pairs<<<pg, 256, 0, dev->stream>>>((const float *)data_ptr(x), (int)Nx, (int)K, Nx * K, seg, segp, Np,
-                                                 (float2 *)xpk->ptr);
-    if (launch_check("mul_mat pack")) {
-      buffer_release(wpk);
-      buffer_release(xpk);
-      shlo_release(o);
-      return 1;
-    }
   }
   MMArgs a;
   a.wp = (const float *)wpk->ptr;
