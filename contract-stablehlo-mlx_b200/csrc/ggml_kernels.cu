@@ -475,51 +475,31 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
   const int groups_per_seg = a.segp / 4;
   const int ngroups = 16 * groups_per_seg;
   int S = 0, gi = 0;
-  // Operands of the current k-step in registers; the next k-step's are loaded
-  // before the current one's FMAs (software pipelining), except across a stage
-  // boundary, where the loads follow the barrier.
-  float4 cw0, cw1, cx0, cx1;
   for (int g = 0; g < ngroups; g++) {
     const int stg = g >> 2;
-    const float *wst = smem + (stg % NS) * STAGE_FLOATS;
-    const float *xst = wst + BK * BM;
     if ((g & 3) == 0) {
       cp_async_wait<NS - 2>();
       __syncthreads();
       if (stg + NS - 1 < nstages) issue(stg + NS - 1);
       cp_async_commit();
-      cw0 = *reinterpret_cast<const float4 *>(wst + mo);
-      cw1 = *reinterpret_cast<const float4 *>(wst + mo + 32);
-      cx0 = *reinterpret_cast<const float4 *>(xst + ro);
-      cx1 = *reinterpret_cast<const float4 *>(xst + ro + 16);
     }
-    const int row0 = (g & 3) * 4;
+    const float *ws = smem + (stg % NS) * STAGE_FLOATS + (g & 3) * 4 * BM;
+    const float *xs = smem + (stg % NS) * STAGE_FLOATS + BK * BM + (g & 3) * 4 * BN;
 #pragma unroll
     for (int kk = 0; kk < 4; kk++) {
-      float4 nw0, nw1, nx0, nx1;
-      const bool pre = kk < 3 || (g & 3) != 3;
-      if (pre) {
-        const int rn = row0 + kk + 1;  // next k-step row within this stage
-        nw0 = *reinterpret_cast<const float4 *>(wst + rn * BM + mo);
-        nw1 = *reinterpret_cast<const float4 *>(wst + rn * BM + mo + 32);
-        nx0 = *reinterpret_cast<const float4 *>(xst + rn * BN + ro);
-        nx1 = *reinterpret_cast<const float4 *>(xst + rn * BN + ro + 16);
-      }
+      const float4 w0 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo);
+      const float4 w1 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo + 32);
+      const float4 x0 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro);
+      const float4 x1 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro + 16);
       // Paired FP32 FMAs: each component rounds exactly as __fmaf_rn.
-      const float2 wp2[4] = {make_float2(cw0.x, cw0.y), make_float2(cw0.z, cw0.w), make_float2(cw1.x, cw1.y),
-                             make_float2(cw1.z, cw1.w)};
-      const float xr[8] = {cx0.x, cx0.y, cx0.z, cx0.w, cx1.x, cx1.y, cx1.z, cx1.w};
+      const float2 wp2[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                             make_float2(w1.z, w1.w)};
+      const float xr[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
 #pragma unroll
       for (int j = 0; j < 8; j++) {
         const float2 xj = make_float2(xr[j], xr[j]);
 #pragma unroll
         for (int i = 0; i < 4; i++) acc2[j * 4 + i] = __ffma2_rn(wp2[i], xj, acc2[j * 4 + i]);
-      }
-      if (pre) {
-        cw0 = nw0;
-        cw1 = nw1;
-        cx0 = nx0;
-        cx1 = nx1;
       }
     }
     if (++gi == groups_per_seg) {
