@@ -348,8 +348,8 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mul_mat_fast(MMArgs a) {
 // 128 m x 128 r): the four stack levels of the reduction tree (64 values each per
 // thread) live in Tensor Memory instead of registers. Warp w reaches TMEM lanes
 // [32 (w % 4), +32); warps w and w + 4 share those lanes and split the 512
-// columns: columns 256 (w / 4) + 64 (L - 1) + [0, 64) hold level L = 1..3 (level
-// 0 stays in registers). The stack is touched only at segment boundaries.
+// columns: columns 256 (w / 4) + 64 L + [0, 64) hold level L. The stack is
+// touched only at segment boundaries.
 namespace mt {
 constexpr int BM = 128, BN = 128, BK = 16, NS = 6, THREADS = 256;
 constexpr int STAGE_FLOATS = BK * (BM + BN);
@@ -387,54 +387,28 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
   for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// 32 consecutive 32-bit TMEM columns of this thread's lane in one access (16
-// register pairs), with the completion wait in the same asm statement.
-__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float2 *v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n"
-               "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr), "r"(__float_as_uint(v[0].x)), "r"(__float_as_uint(v[0].y)), "r"(__float_as_uint(v[1].x)), "r"(__float_as_uint(v[1].y)), "r"(__float_as_uint(v[2].x)), "r"(__float_as_uint(v[2].y)), "r"(__float_as_uint(v[3].x)), "r"(__float_as_uint(v[3].y)), "r"(__float_as_uint(v[4].x)), "r"(__float_as_uint(v[4].y)), "r"(__float_as_uint(v[5].x)), "r"(__float_as_uint(v[5].y)), "r"(__float_as_uint(v[6].x)), "r"(__float_as_uint(v[6].y)), "r"(__float_as_uint(v[7].x)), "r"(__float_as_uint(v[7].y)), "r"(__float_as_uint(v[8].x)), "r"(__float_as_uint(v[8].y)), "r"(__float_as_uint(v[9].x)), "r"(__float_as_uint(v[9].y)), "r"(__float_as_uint(v[10].x)), "r"(__float_as_uint(v[10].y)), "r"(__float_as_uint(v[11].x)), "r"(__float_as_uint(v[11].y)), "r"(__float_as_uint(v[12].x)), "r"(__float_as_uint(v[12].y)), "r"(__float_as_uint(v[13].x)), "r"(__float_as_uint(v[13].y)), "r"(__float_as_uint(v[14].x)), "r"(__float_as_uint(v[14].y)), "r"(__float_as_uint(v[15].x)), "r"(__float_as_uint(v[15].y))
-               : "memory");
-}
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float2 *v) {
-  uint32_t r[32];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
-               "tcgen05.wait::ld.sync.aligned;\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-               : "r"(taddr)
-               : "memory");
-#pragma unroll
-  for (int i = 0; i < 16; i++) v[i] = make_float2(__uint_as_float(r[2 * i]), __uint_as_float(r[2 * i + 1]));
-}
-
-// Fold the finished chain of leaf S into the stack: pop and add the levels
+// Fold the finished chain of leaf S into the TMEM stack: pop and add the levels
 // below the first zero bit of S (the left operand is the older value, as in the
 // tree), then push at that level; at S = 15 the result stays in acc (sumf).
-// Level 0, used at every segment, is kept in registers (lv0); levels 1-3 live in
-// TMEM, 64 columns each, moved as two 32-column halves.
-__device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], float2 (&lv0)[32], uint32_t tcol, int S) {
+__device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, int S) {
   const int depth = __ffs(~S) - 1;  // trailing one bits: 0..4
-  if (depth == 0) {
 #pragma unroll
-    for (int i = 0; i < 32; i++) lv0[i] = acc2[i];
-    return;
-  }
+  for (int c = 0; c < 4; c++) {
+    float v[16];
 #pragma unroll
-  for (int i = 0; i < 32; i++)
-    acc2[i] = make_float2(__fadd_rn(lv0[i].x, acc2[i].x), __fadd_rn(lv0[i].y, acc2[i].y));
-  for (int L = 1; L < depth; L++) {
-#pragma unroll
-    for (int h = 0; h < 2; h++) {
-      float2 t[16];
-      tmem_ld32(tcol + 64 * (L - 1) + 32 * h, t);
-#pragma unroll
-      for (int i = 0; i < 16; i++) {
-        float2 &a = acc2[16 * h + i];
-        a = make_float2(__fadd_rn(t[i].x, a.x), __fadd_rn(t[i].y, a.y));
-      }
+    for (int q = 0; q < 8; q++) {
+      v[2 * q] = acc2[8 * c + q].x;
+      v[2 * q + 1] = acc2[8 * c + q].y;
     }
-  }
-  if (depth < 4) {
-    tmem_st32(tcol + 64 * (depth - 1), acc2);
-    tmem_st32(tcol + 64 * (depth - 1) + 32, acc2 + 16);
+    for (int L = 0; L < depth; L++) {
+      float t[16];
+      tmem_ld16(tcol + 64 * L + 16 * c, t);
+#pragma unroll
+      for (int i = 0; i < 16; i++) v[i] = __fadd_rn(t[i], v[i]);
+    }
+    if (depth < 4) tmem_st16(tcol + 64 * depth + 16 * c, v);
+#pragma unroll
+    for (int q = 0; q < 8; q++) acc2[8 * c + q] = make_float2(v[2 * q], v[2 * q + 1]);
   }
 }
 
@@ -495,7 +469,7 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
   // ends every segp/4 groups and folds into the TMEM stack (a runtime depth:
   // the number of trailing one bits of S), so the hot body exists once.
   // acc[j][i] (r index j, m index i) lives in pairs along m: acc2[4 j + i / 2].
-  float2 acc2[32], lv0[32];
+  float2 acc2[32];
 #pragma unroll
   for (int i = 0; i < 32; i++) acc2[i] = make_float2(0.0f, 0.0f);
   const int groups_per_seg = a.segp / 4;
@@ -529,7 +503,7 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
       }
     }
     if (++gi == groups_per_seg) {
-      tfold_rt(acc2, lv0, tcol, S);
+      tfold_rt(acc2, tcol, S);
       gi = 0;
       if (++S < 16) {
 #pragma unroll
