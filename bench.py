@@ -333,13 +333,14 @@ def run_shlo(args):
                    "l2": "no flush: per-step working set (100 MB weights + >1 GB activations at batch 64) exceeds the 126 MB L2",
                    "ggml_build": "pinned"},
         "model_tflops": round(flops_step * args.steps * ws / dt_max / 1e12, 2),
-        "roofline": {"bound": "fp32-cuda-core", "kernel": "mul_mat (pack + k_mul_mat_fast)",
+        "roofline": {"bound": "fp32-cuda-core", "kernel": "mul_mat (k_mm_pack of x + k_mul_mat_tm)",
                      "achieved": round(mm_tflops, 2), "peak": round(peak_sgemm, 2), "unit": "TFLOP/s",
                      "frac": round(mm_tflops / peak_sgemm, 3),
                      "peak_source": "measured cuBLAS SGEMM (TF32 off), 8192^3, this GPU, this run",
                      "peak_nominal": round(nominal, 1), "frac_of_nominal": round(mm_tflops / nominal, 3),
                      "per_shape": per_shape,
-                     "traffic": profile_traffic("mul_mat_denoiser_ffn1.txt")},
+                     "traffic": profile_traffic("mul_mat_denoiser_qkv.md"),
+                     "traffic_launch": "k_mul_mat_tm at 16384x1536x512 (ncu capture)"},
         "dot_general": {"config1_64x256x128_tflops": round(cfg1_tflops, 4),
                         "config1_us_per_call": round(t1 / n1 * 1e6, 2),
                         "denoiser_shapes_tflops": round(mm_tflops, 2)},
