@@ -50,9 +50,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--impl", default="shlo", choices=["shlo", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    # Short runs to wrap in a profiler (no JSON line): one warm denoiser step, or
-    # mul_mat alone at --mm-shape K,M,R.
-    ap.add_argument("--profile-run", choices=["step", "mul_mat"])
+    # Short runs to wrap in a profiler (no JSON line): one warm denoiser step,
+    # mul_mat alone at --mm-shape K,M,R, or every exact kernel once (batch 16).
+    ap.add_argument("--profile-run", choices=["step", "mul_mat", "kernels"])
     ap.add_argument("--mm-shape", default="512,1536,16384")
     return ap.parse_args()
 
@@ -207,6 +207,90 @@ class EventTimer:
         return s.elapsed_time(e) / 1e3  # seconds
 
 
+def kernel_suite(B: int, cfg, small: bool = False):
+    """Every exact kernel at the shape it runs at in this workload (or its BASELINE
+    config), as (name, algorithmic bytes, flop, launcher) with the inputs already
+    on the device. Bytes: one read of each input + one write of each output."""
+    from shlo import mlx as M
+    from shlo import run as Run
+
+    rng = np.random.default_rng(7)
+    f32 = lambda *s: M.of_numpy((2.0 * rng.standard_normal(s)).astype(np.float32))  # noqa: E731
+    out = []
+    # BASELINE config 2: [512,1024], N(0, sd 2), 5% -inf, row 0 near 88 (fits in L2)
+    x2 = (2.0 * rng.standard_normal((512, 1024))).astype(np.float32)
+    x2[rng.random((512, 1024)) < 0.05] = -np.inf
+    x2[0] = np.float32(88.0) + rng.uniform(-0.5, 0.5, 1024).astype(np.float32)
+    x2[:, 0] = np.where(np.all(np.isinf(x2), axis=1), np.float32(0.0), x2[:, 0])
+    a2 = M.of_numpy(x2)
+    out.append(("soft_max [512x1024] (config 2)", 2 * 4 * 512 * 1024, 0,
+                lambda: Run.soft_max(a2, 1024, 512, 0x3F800000)))
+    rows_sm = (B if not small else 16) * cfg.heads * cfg.seq
+    asm = f32(rows_sm, cfg.seq)
+    out.append(("soft_max [%dx%d] (attention scores)" % (rows_sm, cfg.seq), 2 * 4 * rows_sm * cfg.seq, 0,
+                lambda: Run.soft_max(asm, cfg.seq, rows_sm, 0x3F800000)))
+    R = (B if not small else 16) * cfg.seq
+    an = f32(R, cfg.d)
+    out.append(("norm [%dx%d] (layer norm)" % (R, cfg.d), 2 * 4 * R * cfg.d, 0,
+                lambda: Run.norm(an, cfg.d, R, 0x3727C5AC)))
+    at = f32(B, cfg.d)
+    out.append(("silu [%dx%d] (timestep MLP)" % (B, cfg.d), 2 * 4 * B * cfg.d, 0,
+                lambda: Run.silu(at, B * cfg.d)))
+    ag = f32(R, cfg.ffn)
+    out.append(("gelu_erf [%dx%d] (FFN)" % (R, cfg.ffn), 2 * 4 * R * cfg.ffn, 0,
+                lambda: Run.gelu_erf(ag, R * cfg.ffn)))
+    ne = 1 << (26 if small else 28)
+    out.append(("erff_map 2^%d patterns (sweep, config 3)" % (ne.bit_length() - 1), 4 * ne, 0,
+                lambda: Run.erff_map(0x3F000000, ne)))
+    n32 = 1 << 25
+    da, db = f32(n32), f32(n32)
+    out.append(("divide 2^25", 3 * 4 * n32, 0, lambda: Run.divide(da, db, n32)))
+    out.append(("sqrt 2^25", 2 * 4 * n32, 0, lambda: Run.sqrt(da, n32)))
+    n64 = 1 << 24
+    fa = M.of_numpy((rng.standard_normal(n64) * 3.0).view(np.uint64), M.dtU64)
+    fb = M.of_numpy((rng.standard_normal(n64) * 3.0).view(np.uint64), M.dtU64)
+    for op, nm in ((Run.F64_ADD, "add"), (Run.F64_MUL, "mul"), (Run.F64_DIV, "div")):
+        out.append(("f64_ew %s 2^24" % nm, 3 * 8 * n64, 0, (lambda o: lambda: Run.f64_ew(o, fa, fb, n64))(op)))
+    out.append(("f64_of_f32 2^25", 12 * n32, 0, lambda: Run.f64_of_f32(da, n32)))
+    out.append(("f32_of_f64 2^24", 12 * n64, 0, lambda: Run.f32_of_f64(fa, n64)))
+    w1, x1 = f32(128, 256), f32(64, 256)
+    out.append(("mul_mat [64x256]x[256x128] (config 1)", 4 * (64 * 256 + 256 * 128 + 64 * 128),
+                2 * 64 * 128 * 256, lambda: Run.mul_mat(w1, x1, 256, 128, 64, 64, 0)))
+    return out
+
+
+def time_kernels(timer, suite, n: int, hbm_gbs: float) -> dict:
+    """Per-launch CUDA-event durations on the library's stream, with L2 flushed
+    (a 256 MiB fill on the same stream) before every launch."""
+    torch = timer.torch
+    flush = torch.empty(64 << 20, dtype=torch.float32, device=timer.stream.device)
+    res = {}
+    for name, nbytes, flop, fn in suite:
+        for _ in range(2):
+            fn()
+        total = 0.0
+        evs = []
+        with torch.cuda.stream(timer.stream):
+            for i in range(n):
+                flush.fill_(float(i))
+                s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                s.record(timer.stream)
+                fn()
+                e.record(timer.stream)
+                evs.append((s, e))
+        timer.stream.synchronize()
+        total = sum(s.elapsed_time(e) for s, e in evs) / 1e3
+        us = total / n * 1e6
+        row = {"us": round(us, 2), "gbs": round(nbytes / (total / n) / 1e9, 1)}
+        if hbm_gbs:
+            row["frac_hbm"] = round(row["gbs"] / hbm_gbs, 3)
+        if flop:
+            row["tflops"] = round(flop / (total / n) / 1e12, 4)
+        res[name] = row
+    del flush
+    return res
+
+
 def run_shlo(args):
     rank, local_rank, ws, dist = dist_init()
     import torch
@@ -296,6 +380,8 @@ def run_shlo(args):
     t1 = timer.time(lambda: Run.mul_mat(w1, x1, 256, 128, 64, 64, 0), n1)
     cfg1_tflops = 2.0 * 64 * 128 * 256 / (t1 / n1) / 1e12
 
+    kernels = time_kernels(timer, kernel_suite(B, cfg), 10, measured_peaks().get("hbm_gbs"))
+
     peak_sgemm = fp32_peak_tflops(local_rank)
     sm_count = torch.cuda.get_device_properties(local_rank).multi_processor_count
     clocks = clk.summary()
@@ -341,6 +427,7 @@ def run_shlo(args):
                      "per_shape": per_shape,
                      "traffic": profile_traffic("mul_mat_denoiser_qkv.md"),
                      "traffic_launch": "k_mul_mat_tm at 16384x1536x512 (ncu capture)"},
+        "kernels": kernels,
         "dot_general": {"config1_64x256x128_tflops": round(cfg1_tflops, 4),
                         "config1_us_per_call": round(t1 / n1 * 1e6, 2),
                         "denoiser_shapes_tflops": round(mm_tflops, 2)},
@@ -412,6 +499,11 @@ def profile_run(args):
         c1 = M.launch_count()
         M.eval_([M.apply(fn, X + W)[0]])  # the captured step
         print("launches: warm-up %d, step %d" % (c1 - c0, M.launch_count() - c1))
+    elif args.profile_run == "kernels":
+        suite = kernel_suite(args.batch_per_gpu, D.Config(layers=args.layers), small=True)
+        outs = [fn() for _, _, _, fn in suite]
+        M.eval_(outs)
+        print("kernels: %d launches: %s" % (len(suite), "; ".join(n for n, _, _, _ in suite)))
     else:
         K, Mm, R = (int(v) for v in args.mm_shape.split(","))
         rng = np.random.default_rng(0)

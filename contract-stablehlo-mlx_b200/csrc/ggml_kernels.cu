@@ -138,35 +138,67 @@ __global__ void k_mul_mat_naive(const float *__restrict__ w, const float *__rest
 
 // Pack `rows` rows of K floats (per batch) into dst[batch][Kq][rows_p], K reordered
 // class-major (leaf order) over the first np = 16*seg elements, each segment
-// padded to segp with `pad`. Grid: (ceil(rows/32), ceil(segp/8), batches).
-__global__ void k_mm_pack(const float *__restrict__ src, int rows, int K, int64_t src_batch, int seg, int segp,
-                          int rows_p, float pad, float *__restrict__ dst) {
-  __shared__ float tile[32][129];
-  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;
-  const int r0 = blockIdx.x * 32;
-  const int c0 = blockIdx.y * 8;  // chunk (of 16 k) index base
-  const int b = blockIdx.z;
-  const int Kq = 16 * segp;
-  const float *s = src + (int64_t)b * src_batch;
-  for (int rr = ty; rr < 32; rr += 8) {
-    int r = r0 + rr;
-    for (int kk = tx; kk < 128; kk += 32) {
-      int k = (c0 * 16) + kk;
-      float v = 0.0f;
-      if (r < rows && (c0 + kk / 16) < seg) v = s[(int64_t)r * K + k];
-      tile[rr][kk] = v;
+// padded to segp with `pad`; rows in [rows, rows_p) hold 0 (pad in the padding
+// chunks). rows_p is a multiple of 64.
+//
+// One warp packs one 16-k chunk c of 64 rows. Lane (q = lane & 3, g = lane >> 2)
+// loads, for each of two 32-row groups, rows 4g..4g+3 at k = 16c + 4q .. 16c + 4q + 3
+// (16-byte loads when VEC), transposes the 4x4 block in registers and stores, for
+// each of its classes j = 4q + e, the four rows as one 16-byte vector at packed
+// row leaf(j)*segp + c: the 8 lanes of one q write 128 contiguous bytes. No
+// shared memory; 8 loads per lane are in flight before the first store.
+// Grid: (rows_p / 64, ceil(segp / 8), batches), 256 threads.
+template <bool VEC>
+__global__ void __launch_bounds__(256) k_mm_pack(const float *__restrict__ src, int rows, int K, int64_t src_batch,
+                                                 int seg, int segp, int rows_p, float pad, float *__restrict__ dst) {
+  const int lane = threadIdx.x & 31, q = lane & 3, g = lane >> 2;
+  const int c = blockIdx.y * 8 + (threadIdx.x >> 5);
+  if (c >= segp) return;
+  const float *s = src + (int64_t)blockIdx.z * src_batch;
+  float *d = dst + (int64_t)blockIdx.z * (16 * (int64_t)segp) * rows_p;
+  float v[2][4][4];  // [group][row i][class e]
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int r = blockIdx.x * 64 + 32 * h + 4 * g + i;
+      if (c < seg && r < rows) {
+        const float *p = s + (int64_t)r * K + 16 * c + 4 * q;
+        if (VEC) {
+          const float4 t = __ldg(reinterpret_cast<const float4 *>(p));
+          v[h][i][0] = t.x; v[h][i][1] = t.y; v[h][i][2] = t.z; v[h][i][3] = t.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; e++) v[h][i][e] = __ldg(p + e);
+        }
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; e++) v[h][i][e] = c < seg ? 0.0f : pad;
+      }
     }
   }
-  __syncthreads();
-  float *d = dst + (int64_t)b * Kq * rows_p;
-  for (int o = ty; o < 128; o += 8) {
-    int j = o >> 3, c = o & 7;
-    int cg = c0 + c;
-    if (cg >= segp) continue;
-    int kq = leaf_of_class(j) * segp + cg;
-    float v = cg < seg ? tile[tx][16 * c + j] : pad;
-    d[(int64_t)kq * rows_p + r0 + tx] = v;
+#pragma unroll
+  for (int h = 0; h < 2; h++) {
+    const int r = blockIdx.x * 64 + 32 * h + 4 * g;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+      const int kq = leaf_of_class(4 * q + e) * segp + c;
+      *reinterpret_cast<float4 *>(d + (int64_t)kq * rows_p + r) =
+          make_float4(v[h][0][e], v[h][1][e], v[h][2][e], v[h][3][e]);
+    }
   }
+}
+
+// Launch the pack of `batches` operands of `rows` x K (batch stride src_batch).
+static cudaError_t launch_pack(const float *src, int rows, int K, int64_t src_batch, int batches, int seg, int segp,
+                               int rows_p, float pad, float *dst, cudaStream_t stream) {
+  dim3 grid(rows_p / 64, (segp + 7) / 8, batches);
+  const bool vec = K % 4 == 0 && src_batch % 4 == 0 && ((uintptr_t)src & 15) == 0;
+  if (vec)
+    k_mm_pack<true><<<grid, 256, 0, stream>>>(src, rows, K, src_batch, seg, segp, rows_p, pad, dst);
+  else
+    k_mm_pack<false><<<grid, 256, 0, stream>>>(src, rows, K, src_batch, seg, segp, rows_p, pad, dst);
+  return cudaGetLastError();
 }
 
 namespace mm {
@@ -567,8 +599,7 @@ static int pack_operand(Device *dev, const float *src, int rows, int K, int64_t 
                         int segp, int rows_p, float pad, Buffer **out) {
   size_t bytes = (size_t)batches * 16 * segp * rows_p * sizeof(float);
   SHLO_TRY(buffer_alloc(dev, bytes, out));
-  dim3 grid((rows_p + 31) / 32, (segp + 7) / 8, batches);
-  k_mm_pack<<<grid, 256, 0, dev->stream>>>(src, rows, K, src_batch, seg, segp, rows_p, pad, (float *)(*out)->ptr);
+  launch_pack(src, rows, K, src_batch, batches, seg, segp, rows_p, pad, (float *)(*out)->ptr, dev->stream);
   if (launch_check("mul_mat pack")) {
     buffer_release(*out);
     return 1;
@@ -699,12 +730,12 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
 template <int G>  // float4 groups per lane kept in registers (0 = stream through memory)
 __global__ void g_soft_max(const float *__restrict__ x, float *__restrict__ y, int ncols, int64_t rows, float sc,
                            int float_sum) {
-  extern __shared__ float parts_all[];
+  extern __shared__ double parts_all[];
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
   const int wpb = blockDim.x >> 5;
   const int ng = ncols / 4;
-  float *parts = parts_all + wib * (G > 0 ? G * 32 : 256);
+  double *parts = parts_all + wib * (G > 0 ? G * 32 : 256);
   for (int64_t row = (int64_t)blockIdx.x * wpb + wib; row < rows; row += (int64_t)gridDim.x * wpb) {
     const float4 *xr = reinterpret_cast<const float4 *>(x + row * ncols);
     float4 *yr = reinterpret_cast<float4 *>(y + row * ncols);
@@ -767,16 +798,17 @@ __global__ void g_soft_max(const float *__restrict__ x, float *__restrict__ y, i
           e.w = ggml_v_expf(__fsub_rn(t.w, mx));
           if (G > 0) v[i] = e;
           else yr[gi] = e;
-          parts[lane + 32 * i] = __fadd_rn(__fadd_rn(e.x, e.y), __fadd_rn(e.z, e.w));
+          // widened here, by every lane, so lane 0's chain is adds alone
+          parts[lane + 32 * i] = (double)__fadd_rn(__fadd_rn(e.x, e.y), __fadd_rn(e.z, e.w));
         }
       }
       __syncwarp();
       if (lane == 0) {
         int n = ng - c0 < chunk ? ng - c0 : chunk;
-        for (int k = 0; k < n; k++) {
-          float pv = parts[k];
-          sum = __dadd_rn(sum, (double)pv);
-          fs = __fadd_rn(fs, pv);
+        if (float_sum) {
+          for (int k = 0; k < n; k++) fs = __fadd_rn(fs, (float)parts[k]);
+        } else {
+          for (int k = 0; k < n; k++) sum = __dadd_rn(sum, parts[k]);
         }
       }
       __syncwarp();
@@ -827,11 +859,11 @@ int k_soft_max(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
     float *yp = (float *)o->buf->ptr;
     int ng = (int)(ncols / 4);
     if (ng <= 32 * 2)
-      g_soft_max<2><<<(unsigned)blocks, wpb * 32, wpb * 64 * sizeof(float), dev->stream>>>(xp, yp, (int)ncols, rows, sc, float_sum);
+      g_soft_max<2><<<(unsigned)blocks, wpb * 32, wpb * 64 * sizeof(double), dev->stream>>>(xp, yp, (int)ncols, rows, sc, float_sum);
     else if (ng <= 32 * 8)
-      g_soft_max<8><<<(unsigned)blocks, wpb * 32, wpb * 256 * sizeof(float), dev->stream>>>(xp, yp, (int)ncols, rows, sc, float_sum);
+      g_soft_max<8><<<(unsigned)blocks, wpb * 32, wpb * 256 * sizeof(double), dev->stream>>>(xp, yp, (int)ncols, rows, sc, float_sum);
     else
-      g_soft_max<0><<<(unsigned)blocks, wpb * 32, wpb * 256 * sizeof(float), dev->stream>>>(xp, yp, (int)ncols, rows, sc, float_sum);
+      g_soft_max<0><<<(unsigned)blocks, wpb * 32, wpb * 256 * sizeof(double), dev->stream>>>(xp, yp, (int)ncols, rows, sc, float_sum);
     if (launch_check("soft_max")) {
       shlo_release(o);
       return 1;
@@ -932,32 +964,48 @@ __global__ void g_norm(const float *__restrict__ x, float *__restrict__ y, int n
   }
 }
 
-// The same computation with the warp's 32 rows resident in shared memory
-// (ncols <= 1024): all loads are issued at once as 16-byte vectors, the serial
-// chains then read shared memory (row pitch ncols + 1: conflict-free), and
-// the output is written with 16-byte stores.
-__global__ void __launch_bounds__(32) g_norm_smem(const float *__restrict__ x, float *__restrict__ y, int ncols,
-                                                  int64_t rows, float eps) {
-  extern __shared__ float tile[];  // [32][ncols + 1]
-  const int lane = threadIdx.x;
+// The same computation with a block's rows resident in shared memory (ncols <=
+// 1024, ncols % 4 == 0): NORM_ROWS rows per block of NORM_THREADS threads. All
+// threads load the rows with 16-byte loads (NORM_UNROLL in flight per thread),
+// lanes 0..NORM_ROWS-1 of warp 0 run the rows' serial chains from shared memory
+// (row pitch ncols + 1: conflict-free), and all threads write the output with
+// 16-byte stores.
+constexpr int NORM_ROWS = 16, NORM_THREADS = 128, NORM_UNROLL = 4;
+
+__global__ void __launch_bounds__(NORM_THREADS) g_norm_rows(const float *__restrict__ x, float *__restrict__ y,
+                                                            int ncols, int64_t rows, float eps) {
+  extern __shared__ float tile[];  // [NORM_ROWS][ncols + 1]
+  __shared__ float ms[NORM_ROWS], ss[NORM_ROWS];
+  const int tid = threadIdx.x;
   const int pitch = ncols + 1;
-  const int64_t r0 = (int64_t)blockIdx.x * 32;
-  const int nr = rows - r0 < 32 ? (int)(rows - r0) : 32;
-  const float *xb = x + r0 * ncols;
-  const int nv = nr * ncols / 4;  // float4 elements of the block (ncols % 4 == 0)
-  for (int v = lane; v < nv; v += 32) {
-    float4 t = reinterpret_cast<const float4 *>(xb)[v];
-    int e = v * 4, r = e / ncols, c = e - r * ncols;
-    float *d = tile + r * pitch + c;
-    d[0] = t.x; d[1] = t.y; d[2] = t.z; d[3] = t.w;
+  const int64_t r0 = (int64_t)blockIdx.x * NORM_ROWS;
+  const int nr = rows - r0 < NORM_ROWS ? (int)(rows - r0) : NORM_ROWS;
+  const int cv = ncols / 4;  // float4 per row
+  const int nv = nr * cv;
+  const float4 *xb = reinterpret_cast<const float4 *>(x + r0 * ncols);
+  for (int v0 = tid; v0 < nv; v0 += NORM_THREADS * NORM_UNROLL) {
+    float4 t[NORM_UNROLL];
+#pragma unroll
+    for (int u = 0; u < NORM_UNROLL; u++) {
+      const int v = v0 + u * NORM_THREADS;
+      if (v < nv) t[u] = __ldg(xb + v);
+    }
+#pragma unroll
+    for (int u = 0; u < NORM_UNROLL; u++) {
+      const int v = v0 + u * NORM_THREADS;
+      if (v < nv) {
+        const int r = v / cv, c = 4 * (v - r * cv);
+        float *d = tile + r * pitch + c;
+        d[0] = t[u].x; d[1] = t[u].y; d[2] = t[u].z; d[3] = t[u].w;
+      }
+    }
   }
-  __syncwarp();
-  float mean = 0.0f, scl = 0.0f;
-  if (lane < nr) {
-    const float *row = tile + lane * pitch;
+  __syncthreads();
+  if (tid < nr) {
+    const float *row = tile + tid * pitch;
     double sum = 0.0;
     for (int c = 0; c < ncols; c++) sum = __dadd_rn(sum, (double)row[c]);
-    mean = __fdiv_rn(__double2float_rn(sum), (float)ncols);
+    const float mean = __fdiv_rn(__double2float_rn(sum), (float)ncols);
     double s2 = 0.0;
     for (int c = 0; c < ncols; c += 4) {  // ncols % 4 == 0: no tail
       float d0 = __fsub_rn(row[c], mean), d1 = __fsub_rn(row[c + 1], mean);
@@ -965,24 +1013,22 @@ __global__ void __launch_bounds__(32) g_norm_smem(const float *__restrict__ x, f
       s2 = __dadd_rn(s2, (double)__fadd_rn(__fadd_rn(__fmul_rn(d0, d0), __fmul_rn(d1, d1)),
                                            __fadd_rn(__fmul_rn(d2, d2), __fmul_rn(d3, d3))));
     }
-    float var = __double2float_rn(__ddiv_rn(s2, (double)ncols));
-    scl = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    const float var = __double2float_rn(__ddiv_rn(s2, (double)ncols));
+    ms[tid] = mean;
+    ss[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
   }
-  __shared__ float ms[32], ss[32];
-  ms[lane] = mean;
-  ss[lane] = scl;
-  __syncwarp();
-  float *yb = y + r0 * ncols;
-  for (int v = lane; v < nv; v += 32) {
-    int e = v * 4, r = e / ncols, c = e - r * ncols;
+  __syncthreads();
+  float4 *yb = reinterpret_cast<float4 *>(y + r0 * ncols);
+  for (int v = tid; v < nv; v += NORM_THREADS) {
+    const int r = v / cv, c = 4 * (v - r * cv);
     const float *s = tile + r * pitch + c;
-    float m = ms[r], k = ss[r];
+    const float m = ms[r], k = ss[r];
     float4 o;
     o.x = arm_nan(__fmul_rn(__fsub_rn(s[0], m), k));
     o.y = arm_nan(__fmul_rn(__fsub_rn(s[1], m), k));
     o.z = arm_nan(__fmul_rn(__fsub_rn(s[2], m), k));
     o.w = arm_nan(__fmul_rn(__fsub_rn(s[3], m), k));
-    reinterpret_cast<float4 *>(yb)[v] = o;
+    yb[v] = o;
   }
 }
 
@@ -994,19 +1040,20 @@ int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
   int64_t shape[1] = {ncols * rows};
   Arr *o;
   SHLO_TRY(new_array(dev, kF32, shape, 1, &o));
-  const size_t smem = (size_t)32 * (ncols + 1) * sizeof(float);
-  if (ncols * rows > 0 && p[3] == 0 && ncols % 4 == 0 && ncols <= 1024) {
+  const size_t smem = (size_t)NORM_ROWS * (ncols + 1) * sizeof(float);
+  const bool aligned = (((uintptr_t)data_ptr(x)) & 15) == 0;
+  if (ncols * rows > 0 && p[3] == 0 && ncols % 4 == 0 && ncols <= 1024 && aligned) {
     static bool attr_done[64] = {false};
     if (!attr_done[dev->id]) {
-      if (cuda_check(cudaFuncSetAttribute(g_norm_smem, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                          32 * 1025 * (int)sizeof(float)), "norm attribute")) {
+      if (cuda_check(cudaFuncSetAttribute(g_norm_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                          NORM_ROWS * 1025 * (int)sizeof(float)), "norm attribute")) {
         shlo_release(o);
         return 1;
       }
       attr_done[dev->id] = true;
     }
-    g_norm_smem<<<(unsigned)((rows + 31) / 32), 32, smem, dev->stream>>>((const float *)data_ptr(x),
-                                                                          (float *)o->buf->ptr, (int)ncols, rows, eps);
+    g_norm_rows<<<(unsigned)((rows + NORM_ROWS - 1) / NORM_ROWS), NORM_THREADS, smem, dev->stream>>>(
+        (const float *)data_ptr(x), (float *)o->buf->ptr, (int)ncols, rows, eps);
     if (launch_check("norm")) {
       shlo_release(o);
       return 1;
@@ -1384,16 +1431,10 @@ extern "C" int shlo_mul_mat_noalloc(const float *w, const float *x, float *y, in
   // Both packed regions are written in full by the pack kernels (padding
   // included), so nothing in the scratch array has to start at zero.
   float *wp = scratch, *xp = scratch + w_floats;
-  {
-    dim3 grid((Mp + 31) / 32, (segp + 7) / 8, (unsigned)Wb);
-    k_mm_pack<<<grid, 256, 0, s>>>(w, (int)M, (int)K, wbs, seg, segp, Mp, -0.0f, wp);
-    SHLO_TRY(launch_check("mul_mat_noalloc pack"));
-  }
-  {
-    dim3 grid((Np + 31) / 32, (segp + 7) / 8, (unsigned)Bx);
-    k_mm_pack<<<grid, 256, 0, s>>>(x, (int)Nx, (int)K, Nx * K, seg, segp, Np, 0.0f, xp);
-    SHLO_TRY(launch_check("mul_mat_noalloc pack"));
-  }
+  launch_pack(w, (int)M, (int)K, wbs, (int)Wb, seg, segp, Mp, -0.0f, wp, s);
+  SHLO_TRY(launch_check("mul_mat_noalloc pack"));
+  launch_pack(x, (int)Nx, (int)K, Nx * K, (int)Bx, seg, segp, Np, 0.0f, xp, s);
+  SHLO_TRY(launch_check("mul_mat_noalloc pack"));
   MMArgs a;
   a.wp = wp;
   a.xp = xp;
