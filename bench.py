@@ -352,24 +352,31 @@ def run_shlo(args):
     e2e_dt = all_max(dist, time.perf_counter() - t0)
     barrier(dist)
 
-    # ---- the dominant kernel: mul_mat at the layer's four weight shapes
+    # ---- the dominant kernel: mul_mat at a layer's six shapes (four weight
+    # products, then attention's scores and value products, batched per head)
     R = B * cfg.seq
+    BH = B * cfg.heads
     rng = np.random.default_rng(0)
-    shapes = [(cfg.d, 3 * cfg.d), (cfg.d, cfg.d), (cfg.d, cfg.ffn), (cfg.ffn, cfg.d)]
+    shapes = [(cfg.d, 3 * cfg.d, R, R, 1), (cfg.d, cfg.d, R, R, 1), (cfg.d, cfg.ffn, R, R, 1),
+              (cfg.ffn, cfg.d, R, R, 1), (cfg.dh, cfg.seq, BH * cfg.seq, cfg.seq, BH),
+              (cfg.seq, cfg.dh, BH * cfg.seq, cfg.seq, BH)]
     mm_flops, mm_time, mm_launches = 0.0, 0.0, 0
     per_shape = {}
-    for K, Mm in shapes:
-        wa = M.of_numpy(rng.standard_normal((Mm, K)).astype(np.float32))
-        xa = M.of_numpy(rng.standard_normal((R, K)).astype(np.float32))
+    for K, Mm, Rr, Nn, Wb in shapes:
+        wa = M.of_numpy(rng.standard_normal((Wb * Mm, K)).astype(np.float32))
+        xa = M.of_numpy(rng.standard_normal((Rr, K)).astype(np.float32))
+        wbs = Mm * K if Wb > 1 else 0
         for _ in range(3):
-            y = Run.mul_mat(wa, xa, K, Mm, R, R, 0)
+            y = Run.mul_mat(wa, xa, K, Mm, Rr, Nn, wbs)
         M.eval_([y])
         n = 20
-        t = timer.time(lambda: Run.mul_mat(wa, xa, K, Mm, R, R, 0), n)
-        mm_flops += 2.0 * K * Mm * R * n
+        t = timer.time(lambda: Run.mul_mat(wa, xa, K, Mm, Rr, Nn, wbs), n)
+        mm_flops += 2.0 * K * Mm * Rr * n
         mm_time += t
         mm_launches += n
-        per_shape["%dx%dx%d" % (R, Mm, K)] = round(2.0 * K * Mm * R / (t / n) / 1e12, 2)
+        per_shape["%s%dx%dx%d" % ("%dx" % Wb if Wb > 1 else "", Rr // Wb, Mm, K)] = round(
+            2.0 * K * Mm * Rr / (t / n) / 1e12, 2)
+        del wa, xa, y
     mm_tflops = mm_flops / mm_time / 1e12
     # dot_general config 1: [64,256] x [256,128]
     w1 = M.of_numpy(rng.standard_normal((128, 256)).astype(np.float32))

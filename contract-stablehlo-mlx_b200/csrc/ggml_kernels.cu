@@ -383,76 +383,71 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mul_mat_fast(MMArgs a) {
 // columns: columns 256 (w / 4) + 64 L + [0, 64) hold level L. The stack is
 // touched only at segment boundaries.
 namespace mt {
-constexpr int BM = 128, BN = 128, BK = 16, NS = 6, THREADS = 256;
-constexpr int STAGE_FLOATS = BK * (BM + BN);
+// Two CTA shapes: WM = 2 warps along m gives a 128 m x 128 r tile, WM = 1 a
+// 64 m x 256 r tile (for M <= 64, e.g. attention's value product).
+template <int WM>
+struct Tile {
+  static constexpr int BM = 64 * WM, BN = 256 / WM;
+  static constexpr int STAGE_FLOATS = 16 * (BM + BN);
+};
+constexpr int BK = 16, NS = 6, THREADS = 256;
 constexpr int TMEM_COLS = 512;
 // More dynamic shared memory than half an SM's: one CTA per SM, since each CTA
 // holds all 512 TMEM columns.
 constexpr size_t SMEM_BYTES = 120 * 1024;
-static_assert((size_t)NS * STAGE_FLOATS * sizeof(float) <= SMEM_BYTES, "stages fit");
+static_assert((size_t)NS * Tile<1>::STAGE_FLOATS * sizeof(float) <= SMEM_BYTES, "stages fit");
+static_assert((size_t)NS * Tile<2>::STAGE_FLOATS * sizeof(float) <= SMEM_BYTES, "stages fit");
 }  // namespace mt
 
-// 16 consecutive 32-bit TMEM columns of this thread's lane, stored / loaded
-// (32x32b shape: lane = the thread's lane in the warp's quarter). Each waits for
-// its own completion inside the same asm statement, so the registers are never
-// used before they are valid.
-__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float *v) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n"
-               "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr),
-               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
-               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
-               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
-               "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
-               "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
-               "r"(__float_as_uint(v[15]))
-               : "memory");
-}
-__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
-  uint32_t r[16];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n"
+// One stack level of this thread's lane: 64 consecutive 32-bit TMEM columns
+// (32x32b shape, lane = the thread's lane in the warp's quarter), moved by one
+// instruction whose completion is waited for inside the same asm statement, so
+// the registers are never used before they are valid. Column 2q holds
+// acc2[q].x and column 2q + 1 holds acc2[q].y.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&t)[64]) {
+  uint32_t r[64];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n"
                "tcgen05.wait::ld.sync.aligned;\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
                : "r"(taddr)
                : "memory");
 #pragma unroll
-  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+  for (int i = 0; i < 64; i++) t[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tmem_st64(uint32_t taddr, const float2 (&v)[32]) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64};\n"
+               "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr),
+               "r"(__float_as_uint(v[0].x)), "r"(__float_as_uint(v[0].y)), "r"(__float_as_uint(v[1].x)), "r"(__float_as_uint(v[1].y)), "r"(__float_as_uint(v[2].x)), "r"(__float_as_uint(v[2].y)), "r"(__float_as_uint(v[3].x)), "r"(__float_as_uint(v[3].y)), "r"(__float_as_uint(v[4].x)), "r"(__float_as_uint(v[4].y)), "r"(__float_as_uint(v[5].x)), "r"(__float_as_uint(v[5].y)), "r"(__float_as_uint(v[6].x)), "r"(__float_as_uint(v[6].y)), "r"(__float_as_uint(v[7].x)), "r"(__float_as_uint(v[7].y)), "r"(__float_as_uint(v[8].x)), "r"(__float_as_uint(v[8].y)), "r"(__float_as_uint(v[9].x)), "r"(__float_as_uint(v[9].y)), "r"(__float_as_uint(v[10].x)), "r"(__float_as_uint(v[10].y)), "r"(__float_as_uint(v[11].x)), "r"(__float_as_uint(v[11].y)), "r"(__float_as_uint(v[12].x)), "r"(__float_as_uint(v[12].y)), "r"(__float_as_uint(v[13].x)), "r"(__float_as_uint(v[13].y)), "r"(__float_as_uint(v[14].x)), "r"(__float_as_uint(v[14].y)), "r"(__float_as_uint(v[15].x)), "r"(__float_as_uint(v[15].y)), "r"(__float_as_uint(v[16].x)), "r"(__float_as_uint(v[16].y)), "r"(__float_as_uint(v[17].x)), "r"(__float_as_uint(v[17].y)), "r"(__float_as_uint(v[18].x)), "r"(__float_as_uint(v[18].y)), "r"(__float_as_uint(v[19].x)), "r"(__float_as_uint(v[19].y)), "r"(__float_as_uint(v[20].x)), "r"(__float_as_uint(v[20].y)), "r"(__float_as_uint(v[21].x)), "r"(__float_as_uint(v[21].y)), "r"(__float_as_uint(v[22].x)), "r"(__float_as_uint(v[22].y)), "r"(__float_as_uint(v[23].x)), "r"(__float_as_uint(v[23].y)), "r"(__float_as_uint(v[24].x)), "r"(__float_as_uint(v[24].y)), "r"(__float_as_uint(v[25].x)), "r"(__float_as_uint(v[25].y)), "r"(__float_as_uint(v[26].x)), "r"(__float_as_uint(v[26].y)), "r"(__float_as_uint(v[27].x)), "r"(__float_as_uint(v[27].y)), "r"(__float_as_uint(v[28].x)), "r"(__float_as_uint(v[28].y)), "r"(__float_as_uint(v[29].x)), "r"(__float_as_uint(v[29].y)), "r"(__float_as_uint(v[30].x)), "r"(__float_as_uint(v[30].y)), "r"(__float_as_uint(v[31].x)), "r"(__float_as_uint(v[31].y))
+               : "memory");
 }
 
 // Fold the finished chain of leaf S into the TMEM stack: pop and add the levels
 // below the first zero bit of S (the left operand is the older value, as in the
 // tree), then push at that level; at S = 15 the result stays in acc (sumf).
+// A level moves as one 64-column transfer, so a fold waits once per level.
 __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, int S) {
   const int depth = __ffs(~S) - 1;  // trailing one bits: 0..4
+  for (int L = 0; L < depth; L++) {
+    float t[64];
+    tmem_ld64(tcol + 64 * L, t);
 #pragma unroll
-  for (int c = 0; c < 4; c++) {
-    float v[16];
-#pragma unroll
-    for (int q = 0; q < 8; q++) {
-      v[2 * q] = acc2[8 * c + q].x;
-      v[2 * q + 1] = acc2[8 * c + q].y;
-    }
-    for (int L = 0; L < depth; L++) {
-      float t[16];
-      tmem_ld16(tcol + 64 * L + 16 * c, t);
-#pragma unroll
-      for (int i = 0; i < 16; i++) v[i] = __fadd_rn(t[i], v[i]);
-    }
-    if (depth < 4) tmem_st16(tcol + 64 * depth + 16 * c, v);
-#pragma unroll
-    for (int q = 0; q < 8; q++) acc2[8 * c + q] = make_float2(v[2 * q], v[2 * q + 1]);
+    for (int q = 0; q < 32; q++)
+      acc2[q] = make_float2(__fadd_rn(t[2 * q], acc2[q].x), __fadd_rn(t[2 * q + 1], acc2[q].y));
   }
+  if (depth < 4) tmem_st64(tcol + 64 * depth, acc2);
 }
 
+template <int WM>
 __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
   using namespace mt;
+  constexpr int BM = Tile<WM>::BM, BN = Tile<WM>::BN, STAGE_FLOATS = Tile<WM>::STAGE_FLOATS;
   extern __shared__ __align__(16) float smem[];
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  // Warps 2 (m) x 4 (r), lanes 8 (m) x 4 (r); a thread's m are mo + [0,4) and
-  // mo + 32 + [0,4), its r are ro + [0,4) and ro + 16 + [0,4).
-  const int mo = (warp & 1) * 64 + (lane & 7) * 4;
-  const int ro = (warp >> 1) * 32 + (lane >> 3) * 4;
+  // Warps WM (m) x 8/WM (r), lanes 8 (m) x 4 (r); a thread's m are mo + [0,4)
+  // and mo + 32 + [0,4), its r are ro + [0,4) and ro + 16 + [0,4).
+  const int mo = (warp % WM) * 64 + (lane & 7) * 4;
+  const int ro = (warp / WM) * 32 + (lane >> 3) * 4;
   const int m0 = blockIdx.x * BM;
   const int bx = blockIdx.y / a.r_tiles;
   const int rt = blockIdx.y % a.r_tiles;
@@ -478,14 +473,14 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
     float *xs = ws + BK * BM;
     const int k0 = st * BK;
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
+    for (int i = 0; i < STAGE_FLOATS / 4 / THREADS; i++) {
       int q = tid + i * THREADS;
       if (q < BK * BM / 4) {
-        int row = q >> 5, col = (q & 31) * 4;
+        int row = q / (BM / 4), col = (q % (BM / 4)) * 4;
         cp_async16(ws + row * BM + col, wp + (int64_t)(k0 + row) * a.Mp + col);
       } else {
         q -= BK * BM / 4;
-        int row = q >> 5, col = (q & 31) * 4;
+        int row = q / (BN / 4), col = (q % (BN / 4)) * 4;
         cp_async16(xs + row * BN + col, xp + (int64_t)(k0 + row) * a.Np + col);
       }
     }
@@ -640,17 +635,20 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
   }
   const int seg = (int)(np / 16);
   const int segp = (seg + 3) & ~3;
-  const int Mp = (int)((M + mt::BM - 1) / mt::BM * mt::BM);
+  const int WM = M <= 64 ? 1 : 2;
+  const int BM = WM == 1 ? mt::Tile<1>::BM : mt::Tile<2>::BM;
+  const int BN = WM == 1 ? mt::Tile<1>::BN : mt::Tile<2>::BN;
+  const int Mp = (int)((M + BM - 1) / BM * BM);
   const int64_t Bx = wbs ? nb : 1;
   const int64_t Nx = wbs ? N : R;
-  const int Np = (int)((Nx + mt::BN - 1) / mt::BN * mt::BN);
+  const int Np = (int)((Nx + BN - 1) / BN * BN);
   const int Wb = wbs ? (int)nb : 1;
   // The packed w is derived from w's storage, which never changes: keep it.
   Buffer *wpk = nullptr;
   {
     char key[160];
-    snprintf(key, sizeof key, "mm:%lld:%lld:%lld:%d:%lld", (long long)w->offset, (long long)K, (long long)M, Wb,
-             (long long)wbs);
+    snprintf(key, sizeof key, "mm:%lld:%lld:%lld:%d:%lld:%d", (long long)w->offset, (long long)K, (long long)M, Wb,
+             (long long)wbs, Mp);
     std::lock_guard<std::mutex> lk(w->buf->derived_mu);
     auto it = w->buf->derived.find(key);
     if (it != w->buf->derived.end()) {
@@ -687,22 +685,26 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
   a.Np = Np;
   a.Nx = Nx;
   a.wbs = wbs;
-  a.r_tiles = Np / mt::BN;
+  a.r_tiles = Np / BN;
   a.flavor = flavor;
   const size_t smem = mt::SMEM_BYTES;
-  static bool attr_done[64] = {false};
-  if (!attr_done[dev->id]) {
-    if (cuda_check(cudaFuncSetAttribute(k_mul_mat_tm, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+  static bool attr_done[2][64] = {{false}};
+  if (!attr_done[WM - 1][dev->id]) {
+    if (cuda_check(cudaFuncSetAttribute(WM == 1 ? k_mul_mat_tm<1> : k_mul_mat_tm<2>,
+                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
                    "mul_mat attribute")) {
       buffer_release(wpk);
       buffer_release(xpk);
       shlo_release(o);
       return 1;
     }
-    attr_done[dev->id] = true;
+    attr_done[WM - 1][dev->id] = true;
   }
-  dim3 grid(Mp / mt::BM, (unsigned)(Bx * a.r_tiles));
-  k_mul_mat_tm<<<grid, mt::THREADS, smem, dev->stream>>>(a);
+  dim3 grid(Mp / BM, (unsigned)(Bx * a.r_tiles));
+  if (WM == 1)
+    k_mul_mat_tm<1><<<grid, mt::THREADS, smem, dev->stream>>>(a);
+  else
+    k_mul_mat_tm<2><<<grid, mt::THREADS, smem, dev->stream>>>(a);
   int rc = launch_check("mul_mat");
   buffer_release(wpk);
   buffer_release(xpk);
@@ -1075,88 +1077,121 @@ int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
 
 // =========================================================== elementwise ====
 
+// Elementwise maps: each thread moves 16-byte vectors (two per trip for the
+// one-input maps) in a grid-stride loop; the n mod 4 tail is done element by
+// element. Every pointer is 16-byte aligned (fresh allocations, and kernel
+// inputs are realigned by the API before the launch).
+template <typename F>
+__device__ __forceinline__ void map_f32(const float *__restrict__ x, float *__restrict__ y, int64_t n, F f) {
+  const int64_t nv = n >> 2;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  const float4 *xv = reinterpret_cast<const float4 *>(x);
+  float4 *yv = reinterpret_cast<float4 *>(y);
+  int64_t i = t0;
+  for (; i + stride < nv; i += 2 * stride) {
+    const float4 a = __ldg(xv + i), b = __ldg(xv + i + stride);
+    yv[i] = make_float4(f(a.x), f(a.y), f(a.z), f(a.w));
+    yv[i + stride] = make_float4(f(b.x), f(b.y), f(b.z), f(b.w));
+  }
+  if (i < nv) {
+    const float4 a = __ldg(xv + i);
+    yv[i] = make_float4(f(a.x), f(a.y), f(a.z), f(a.w));
+  }
+  for (int64_t j = 4 * nv + t0; j < n; j += stride) y[j] = f(x[j]);
+}
+
+template <typename F>
+__device__ __forceinline__ void map2_f32(const float *__restrict__ a, const float *__restrict__ b,
+                                         float *__restrict__ y, int64_t n, F f) {
+  const int64_t nv = n >> 2;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = t0; i < nv; i += stride) {
+    const float4 u = __ldg(reinterpret_cast<const float4 *>(a) + i), v = __ldg(reinterpret_cast<const float4 *>(b) + i);
+    reinterpret_cast<float4 *>(y)[i] = make_float4(f(u.x, v.x), f(u.y, v.y), f(u.z, v.z), f(u.w, v.w));
+  }
+  for (int64_t j = 4 * nv + t0; j < n; j += stride) y[j] = f(a[j], b[j]);
+}
+
 // silu: Shaders.lean:172-179 (ggml_vec_silu_f32's four-lane body):
 // y = x / (1 + ggml_v_expf(0 - x)), a correctly rounded division.
+__device__ __forceinline__ float silu_one(float v, int gpu_ops) {
+  if (gpu_ops) return __fdividef(v, __fadd_rn(1.0f, __expf(-v)));
+  float r = __fdiv_rn(v, __fadd_rn(1.0f, ggml_v_expf(__fsub_rn(0.0f, v))));
+  // arm64: a NaN input comes back quieted (every step passes it through); an
+  // invalid division (-inf / inf) gives the default NaN.
+  const uint32_t b = fbits(v);
+  if ((b & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(b | 0x00400000u);
+  else if (r != r) r = bitsf(0x7FC00000u);
+  return r;
+}
+
 __global__ void g_silu(const float *__restrict__ x, float *__restrict__ y, int64_t n, int gpu_ops) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    float v = x[i];
-    if (gpu_ops) {
-      y[i] = __fdividef(v, __fadd_rn(1.0f, __expf(-v)));
-      continue;
-    }
-    float r = __fdiv_rn(v, __fadd_rn(1.0f, ggml_v_expf(__fsub_rn(0.0f, v))));
-    // arm64: a NaN input comes back quieted (every step passes it through); an
-    // invalid division (-inf / inf) gives the default NaN.
-    uint32_t b = fbits(v);
-    if ((b & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(b | 0x00400000u);
-    else if (r != r) r = bitsf(0x7FC00000u);
-    y[i] = r;
-  }
+  map_f32(x, y, n, [gpu_ops](float v) { return silu_one(v, gpu_ops); });
 }
 
 // gelu_erf: Shaders.lean:186-199 (ggml_vec_gelu_erf_f32):
 // y = (0.5f*x) * (1.0f + erff(x*SQRT_2_INV)) with the correctly rounded erff; a
 // NaN input returns itself quieted, as every arm64 step does.
-__global__ void g_gelu_erf(const float *__restrict__ x, float *__restrict__ y, int64_t n, int gpu_erf) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    float v = x[i];
-    float ev;
-    if (gpu_erf) {
-      // The planted fault: GELU's tanh form (SQRT_2_OVER_PI, GELU_COEF_A of vec.h).
-      ev = tanhf(__fmul_rn(__fmul_rn(bitsf(0x3F4C422Au), v),
-                           __fadd_rn(1.0f, __fmul_rn(__fmul_rn(bitsf(0x3D372713u), v), v))));
-    } else {
-      ev = shlo_erf::erff_cr(__fmul_rn(v, bitsf(0x3F3504F3u)));
-    }
-    float r = __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, ev));
-    uint32_t b = fbits(v);
-    if ((b & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(b | 0x00400000u);
-    else if (r != r) r = bitsf(0x7FC00000u);  // -inf * 0: arm64's default NaN
-    y[i] = r;
+__device__ __forceinline__ float gelu_one(float v, int gpu_erf) {
+  float ev;
+  if (gpu_erf) {
+    // The planted fault: GELU's tanh form (SQRT_2_OVER_PI, GELU_COEF_A of vec.h).
+    ev = tanhf(__fmul_rn(__fmul_rn(bitsf(0x3F4C422Au), v),
+                         __fadd_rn(1.0f, __fmul_rn(__fmul_rn(bitsf(0x3D372713u), v), v))));
+  } else {
+    ev = shlo_erf::erff_cr(__fmul_rn(v, bitsf(0x3F3504F3u)));
   }
+  float r = __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, ev));
+  const uint32_t b = fbits(v);
+  if ((b & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(b | 0x00400000u);
+  else if (r != r) r = bitsf(0x7FC00000u);  // -inf * 0: arm64's default NaN
+  return r;
 }
 
-// erff_map: Shaders.lean:204-208: y[t] = bits(erff(bits^-1(base + t))).
+__global__ void g_gelu_erf(const float *__restrict__ x, float *__restrict__ y, int64_t n, int gpu_erf) {
+  map_f32(x, y, n, [gpu_erf](float v) { return gelu_one(v, gpu_erf); });
+}
+
+// erff_map: Shaders.lean:204-208: y[t] = bits(erff(bits^-1(base + t))), four
+// consecutive patterns per thread and trip, stored as one 16-byte vector.
 __global__ void g_erff_map(uint32_t base, int64_t n, uint32_t *__restrict__ y) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride)
-    y[i] = fbits(shlo_erf::erff_cr(bitsf(base + (uint32_t)i)));
+  const int64_t nv = n >> 2;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = t0; i < nv; i += stride) {
+    const uint32_t p = base + (uint32_t)(4 * i);
+    reinterpret_cast<uint4 *>(y)[i] =
+        make_uint4(fbits(shlo_erf::erff_cr(bitsf(p))), fbits(shlo_erf::erff_cr(bitsf(p + 1u))),
+                   fbits(shlo_erf::erff_cr(bitsf(p + 2u))), fbits(shlo_erf::erff_cr(bitsf(p + 3u))));
+  }
+  for (int64_t j = 4 * nv + t0; j < n; j += stride) y[j] = fbits(shlo_erf::erff_cr(bitsf(base + (uint32_t)j)));
 }
 
 // divide and sqrt: SoftFloat.lean:262-305, correctly rounded binary32 with the
 // soft-float NaN rules: a NaN operand is returned quieted (the first one
 // first), an invalid operation gives 0x7FC00000; sqrt returns +inf, a positive
 // NaN (unquieted) and +-0 unchanged, and 0x7FC00000 for any negative input.
+__device__ __forceinline__ float divide_one(float u, float v) {
+  const uint32_t ub = fbits(u), vb = fbits(v);
+  if ((ub & 0x7FFFFFFFu) > 0x7F800000u) return bitsf(ub | 0x00400000u);
+  if ((vb & 0x7FFFFFFFu) > 0x7F800000u) return bitsf(vb | 0x00400000u);
+  const float r = __fdiv_rn(u, v);
+  return r != r ? bitsf(0x7FC00000u) : r;
+}
+
 __global__ void g_divide(const float *__restrict__ a, const float *__restrict__ b, float *__restrict__ y, int64_t n) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    float u = a[i], v = b[i];
-    uint32_t ub = fbits(u), vb = fbits(v);
-    float r;
-    if ((ub & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(ub | 0x00400000u);
-    else if ((vb & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(vb | 0x00400000u);
-    else {
-      r = __fdiv_rn(u, v);
-      if (r != r) r = bitsf(0x7FC00000u);
-    }
-    y[i] = r;
-  }
+  map2_f32(a, b, y, n, [](float u, float v) { return divide_one(u, v); });
+}
+
+__device__ __forceinline__ float sqrt_one(float u) {
+  const uint32_t b = fbits(u);
+  if ((b & 0x7FFFFFFFu) == 0) return u;
+  if (b >> 31) return bitsf(0x7FC00000u);
+  if (b >= 0x7F800000u) return u;
+  return __fsqrt_rn(u);
 }
 
 __global__ void g_sqrt(const float *__restrict__ a, float *__restrict__ y, int64_t n) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    float u = a[i];
-    uint32_t b = fbits(u);
-    float r;
-    if ((b & 0x7FFFFFFFu) == 0) r = u;
-    else if (b >> 31) r = bitsf(0x7FC00000u);
-    else if (b >= 0x7F800000u) r = u;
-    else r = __fsqrt_rn(u);
-    y[i] = r;
-  }
+  map_f32(a, y, n, [](float u) { return sqrt_one(u); });
 }
 
 // Binary64 on uint64 bit patterns (SoftFloat.lean:137-259, Shaders.lean:231-257):
@@ -1166,65 +1201,79 @@ __global__ void g_sqrt(const float *__restrict__ a, float *__restrict__ y, int64
 #define QNAN64 0x7FF8000000000000ull
 __device__ __forceinline__ bool nan64(uint64_t v) { return (v & 0x7FFFFFFFFFFFFFFFull) > 0x7FF0000000000000ull; }
 
+__device__ __forceinline__ uint64_t f64_one(int op, uint64_t u, uint64_t v) {
+  if (op == 4)  // floor
+    return nan64(u) ? (u | 0x8000000000000ull) : (uint64_t)__double_as_longlong(floor(__longlong_as_double((long long)u)));
+  if (op == 5) {  // to int64, toward zero, saturating
+    const double d = __longlong_as_double((long long)u);
+    if (nan64(u)) return 0;
+    if (d >= 9223372036854775808.0) return 0x7FFFFFFFFFFFFFFFull;
+    if (d <= -9223372036854775808.0) return 0x8000000000000000ull;
+    return (uint64_t)__double2ll_rz(d);
+  }
+  if (nan64(u)) return u | 0x8000000000000ull;
+  if (nan64(v)) return v | 0x8000000000000ull;
+  const double x = __longlong_as_double((long long)u), z = __longlong_as_double((long long)v);
+  double q;
+  switch (op) {
+    case 0: q = __dadd_rn(x, z); break;
+    case 1: q = __dsub_rn(x, z); break;
+    case 2: q = __dmul_rn(x, z); break;
+    default: q = __ddiv_rn(x, z); break;
+  }
+  return (q != q) ? QNAN64 : (uint64_t)__double_as_longlong(q);
+}
+
+// Two uint64 per 16-byte vector. b is read only by the binary ops (floor and
+// the int64 conversion ignore it).
 __global__ void g_f64_ew(const uint64_t *__restrict__ a, const uint64_t *__restrict__ b, uint64_t *__restrict__ y,
                          int64_t n, int op) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    uint64_t u = a[i];
-    uint64_t r;
-    if (op == 4) {  // floor
-      r = nan64(u) ? (u | 0x8000000000000ull) : (uint64_t)__double_as_longlong(floor(__longlong_as_double((long long)u)));
-    } else if (op == 5) {  // to int64, toward zero, saturating
-      double d = __longlong_as_double((long long)u);
-      if (nan64(u)) r = 0;
-      else if (d >= 9223372036854775808.0) r = 0x7FFFFFFFFFFFFFFFull;
-      else if (d <= -9223372036854775808.0) r = 0x8000000000000000ull;
-      else r = (uint64_t)__double2ll_rz(d);
-    } else {
-      uint64_t v = b[i];
-      if (nan64(u)) r = u | 0x8000000000000ull;
-      else if (nan64(v)) r = v | 0x8000000000000ull;
-      else {
-        double x = __longlong_as_double((long long)u), z = __longlong_as_double((long long)v), q;
-        switch (op) {
-          case 0: q = __dadd_rn(x, z); break;
-          case 1: q = __dsub_rn(x, z); break;
-          case 2: q = __dmul_rn(x, z); break;
-          default: q = __ddiv_rn(x, z); break;
-        }
-        r = (q != q) ? QNAN64 : (uint64_t)__double_as_longlong(q);
-      }
-    }
-    y[i] = r;
+  const int64_t nv = n >> 1;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  const bool binary = op < 4;
+  for (int64_t i = t0; i < nv; i += stride) {
+    const ulonglong2 u = __ldg(reinterpret_cast<const ulonglong2 *>(a) + i);
+    ulonglong2 v = make_ulonglong2(0, 0);
+    if (binary) v = __ldg(reinterpret_cast<const ulonglong2 *>(b) + i);
+    reinterpret_cast<ulonglong2 *>(y)[i] = make_ulonglong2(f64_one(op, u.x, v.x), f64_one(op, u.y, v.y));
   }
+  for (int64_t j = 2 * nv + t0; j < n; j += stride) y[j] = f64_one(op, a[j], binary ? b[j] : 0);
 }
 
 // Exact widening; a NaN keeps its payload and is not quieted (SoftFloat.lean:73-85).
+__device__ __forceinline__ uint64_t f64_of_f32_one(float x) {
+  const uint32_t b = fbits(x);
+  if ((b & 0x7FFFFFFFu) > 0x7F800000u)
+    return ((uint64_t)(b >> 31) << 63) | 0x7FF0000000000000ull | ((uint64_t)(b & 0x7FFFFFu) << 29);
+  return (uint64_t)__double_as_longlong((double)x);
+}
+
+// Two elements per thread and trip: 8 bytes in, 16 bytes out, both contiguous
+// across the warp.
 __global__ void g_f64_of_f32(const float *__restrict__ a, uint64_t *__restrict__ y, int64_t n) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    uint32_t b = fbits(a[i]);
-    uint64_t r;
-    if ((b & 0x7FFFFFFFu) > 0x7F800000u)
-      r = ((uint64_t)(b >> 31) << 63) | 0x7FF0000000000000ull | ((uint64_t)(b & 0x7FFFFFu) << 29);
-    else
-      r = (uint64_t)__double_as_longlong((double)a[i]);
-    y[i] = r;
+  const int64_t nv = n >> 1;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = t0; i < nv; i += stride) {
+    const float2 t = __ldg(reinterpret_cast<const float2 *>(a) + i);
+    reinterpret_cast<ulonglong2 *>(y)[i] = make_ulonglong2(f64_of_f32_one(t.x), f64_of_f32_one(t.y));
   }
+  for (int64_t j = 2 * nv + t0; j < n; j += stride) y[j] = f64_of_f32_one(a[j]);
 }
 
 // Round to nearest even with subnormals; a NaN is quieted, payload kept (SoftFloat.lean:95-120).
+__device__ __forceinline__ float f32_of_f64_one(uint64_t d) {
+  if (nan64(d)) return bitsf((uint32_t)((d >> 63) << 31) | 0x7FC00000u | (uint32_t)((d & 0xFFFFFFFFFFFFFull) >> 29));
+  return __double2float_rn(__longlong_as_double((long long)d));
+}
+
 __global__ void g_f32_of_f64(const uint64_t *__restrict__ a, float *__restrict__ y, int64_t n) {
-  int64_t stride = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += stride) {
-    uint64_t d = a[i];
-    float r;
-    if (nan64(d))
-      r = bitsf((uint32_t)((d >> 63) << 31) | 0x7FC00000u | (uint32_t)((d & 0xFFFFFFFFFFFFFull) >> 29));
-    else
-      r = __double2float_rn(__longlong_as_double((long long)d));
-    y[i] = r;
+  const int64_t nv = n >> 1;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t i = t0; i < nv; i += stride) {
+    const ulonglong2 u = __ldg(reinterpret_cast<const ulonglong2 *>(a) + i);
+    reinterpret_cast<float2 *>(y)[i] = make_float2(f32_of_f64_one(u.x), f32_of_f64_one(u.y));
   }
+  for (int64_t j = 2 * nv + t0; j < n; j += stride) y[j] = f32_of_f64_one(a[j]);
 }
 
 template <typename K, typename... Args>

@@ -34,7 +34,7 @@ MM_SHAPES = [  # K, M, R, N, batched
     (16, 1, 1, 1, False), (17, 3, 5, 5, False), (32, 128, 64, 64, False), (48, 130, 70, 70, False),
     (64, 256, 256, 256, True), (100, 64, 33, 11, True), (196, 196, 392, 196, True), (256, 64, 512, 256, True),
     (352, 128, 352, 352, False), (512, 1536, 300, 300, False), (737, 1024, 40, 40, False), (2048, 512, 129, 129, False),
-    (4096, 64, 16, 16, False), (80, 33, 200, 50, True),
+    (4096, 64, 16, 16, False), (80, 33, 200, 50, True), (64, 40, 700, 700, False), (192, 64, 1300, 650, True),
 ]
 
 
