@@ -338,6 +338,21 @@ def run_shlo(args):
     dt_max = all_max(dist, dt)
     deterministic = bool(np.array_equal(first.view(np.uint32), last.view(np.uint32)))
 
+    # ---- batch-1 step latency: the module recorded as a CUDA graph (compile
+    # enabled, as the executor prepares it) against plain eager calls
+    latency = {}
+    X1 = [M.of_numpy(a) for a in D.inputs(cfg, 1, seed=1)]
+    for name, comp in (("graph", True), ("eager", False)):
+        f1 = E.prepare(E.load(D.module_text(cfg, 1)), None, comp)
+        o1 = None
+        for _ in range(3):
+            o1 = M.apply(f1, X1 + W)[0]
+        M.eval_([o1])
+        o1 = None
+        latency[name] = round(timer.time(lambda: M.apply(f1, X1 + W), 20) / 20 * 1e3, 3)
+        del f1
+    del X1
+
     # ---- e2e: pinned host inputs copied in, output read back, every step
     pinned_in = [torch.from_numpy(a).pin_memory() for a in ins]
     pinned_out = torch.empty(first.shape, dtype=torch.float32).pin_memory()
@@ -442,6 +457,7 @@ def run_shlo(args):
         "e2e": {"value": round(ws * B * args.steps / e2e_dt, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h},
         "gpu_launches": int(launches),
+        "latency_b1_ms": latency,
         "clocks": clocks,
         "bit_exact": {"sample0_vs_oracle": exact0, "deterministic_across_steps": deterministic},
         "hbm_gbs_measured": measured_peaks().get("hbm_gbs"),

@@ -4,6 +4,9 @@
 #include <cstdio>
 #include <cstdlib>
 #include <functional>
+#include <map>
+#include <mutex>
+#include <string>
 #include <vector>
 
 #include "common.cuh"
@@ -47,12 +50,174 @@ struct shlo_kernel_s {
   const KernelInfo *info;
 };
 
+namespace {
+
+// One recorded signature of a compiled function (Mlx.lean:66-67; mx::compile in
+// c/smlx_shim.c:325-386). The graph reads private contiguous copies of the
+// inputs (`staging`); a replay first refreshes the copies whose source array
+// changed (arrays are immutable, so the same storage, offset and strides mean
+// the same data), relaunches the graph, and copies the outputs into fresh
+// arrays, so every result stays an independent immutable value.
+struct Captured {
+  bool eager = false;  // recording was refused for this signature: f runs every call
+  std::string why;
+  Device *dev = nullptr;
+  std::vector<Arr *> staging;
+  std::vector<Buffer *> src;        // source storage last copied into each slot (retained)
+  std::vector<std::string> layout;  // and its offset, strides, dtype
+  std::vector<Arr *> outs;          // the graph's results (its own storage)
+  std::vector<std::pair<void *, size_t>> allocs;  // every block the graph owns
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t exec = nullptr;
+  uint64_t launches = 0;  // kernel launches recorded in the graph
+};
+
+std::string signature(Device *dev, const shlo_arr *inputs, int n) {
+  std::string k = std::to_string(dev->id);
+  for (int i = 0; i < n; i++) {
+    k += "|";
+    k += std::to_string((int)inputs[i]->dtype);
+    for (int d = 0; d < inputs[i]->ndim; d++) k += "," + std::to_string((long long)inputs[i]->shape[d]);
+  }
+  return k;
+}
+
+std::string layout_of(const Arr *a) {
+  std::string k = std::to_string((long long)a->offset) + ":" + std::to_string((int)a->dtype);
+  for (int d = 0; d < a->ndim; d++) k += "," + std::to_string((long long)a->strides[d]);
+  return k;
+}
+
+}  // namespace
+
 struct shlo_fn_s {
   shlo_trace_fn f;
   void *payload;
   void (*payload_free)(void *);
   int enable;
+  std::mutex mu;
+  std::map<std::string, Captured *> graphs;
 };
+
+namespace {
+
+int call_traced(shlo_fn f, const shlo_arr *inputs, int n_inputs, shlo_arr *outputs, int *n_outputs, int max_outputs) {
+  char err[2048];
+  err[0] = 0;
+  int n = 0;
+  int rc = f->f(f->payload, inputs, n_inputs, outputs, &n, max_outputs, err, sizeof err);
+  if (rc) return fail("apply: traced function: %s", err[0] ? err : shlo_last_error());
+  *n_outputs = n;
+  return 0;
+}
+
+void release_all(shlo_arr *xs, int n) {
+  for (int i = 0; i < n; i++)
+    if (xs[i]) shlo_release(xs[i]);
+}
+
+void destroy_captured(Captured *c) {
+  if (!c) return;
+  if (c->dev) device_wait(c->dev, "compiled function free");
+  if (c->exec) cudaGraphExecDestroy(c->exec);
+  if (c->graph) cudaGraphDestroy(c->graph);
+  for (Arr *a : c->outs) shlo_release(a);
+  for (Arr *a : c->staging) shlo_release(a);
+  for (Buffer *b : c->src) buffer_release(b);
+  if (c->dev) {
+    std::lock_guard<std::mutex> lk(c->dev->mu);
+    for (auto &pb : c->allocs) {
+      c->dev->free_blocks.emplace(pb.second, pb.first);
+      c->dev->pooled_bytes += pb.second;
+    }
+  }
+  delete c;
+}
+
+// Copy input i into its private slot when its source changed since the last
+// call (and derive the slot's cached layouts again).
+int refresh_slot(Captured *c, int i, Arr *in) {
+  Arr *st = c->staging[i];
+  if (!st->buf) return 0;
+  const std::string lay = layout_of(in);
+  if (in->buf == c->src[i] && lay == c->layout[i]) return 0;
+  SHLO_TRY(launch_copy_strided(c->dev, in, st->buf->ptr));
+  SHLO_TRY(buffer_rederive(st->buf));
+  buffer_retain(in->buf);
+  buffer_release(c->src[i]);
+  c->src[i] = in->buf;
+  c->layout[i] = lay;
+  return 0;
+}
+
+// Record f over private copies of `inputs`. Returns nonzero only when f itself
+// fails; a refusal to record (an operation that cannot run inside a graph)
+// leaves c->eager set and f is then called eagerly for this signature.
+int record(shlo_fn f, Device *dev, const shlo_arr *inputs, int n_inputs, int max_outputs, Captured *c) {
+  c->dev = dev;
+  for (int i = 0; i < n_inputs; i++) {
+    Arr *in = inputs[i];
+    Arr *st;
+    SHLO_TRY(new_array(dev, in->dtype, in->shape, in->ndim, &st));
+    c->staging.push_back(st);
+    c->src.push_back(nullptr);
+    c->layout.push_back("");
+    SHLO_TRY(refresh_slot(c, i, in));
+  }
+  // One eager call first: it derives every cached layout of the inputs (the
+  // packed weights of mul_mat) outside the graph, and checks f.
+  {
+    std::vector<shlo_arr> tmp(max_outputs > 0 ? max_outputs : 1, nullptr);
+    int n = 0;
+    SHLO_TRY(call_traced(f, c->staging.data(), n_inputs, tmp.data(), &n, max_outputs));
+    release_all(tmp.data(), n);
+  }
+  // Nothing queued may still use a pooled block once the recording claims it.
+  SHLO_TRY(device_wait(dev, "compile"));
+  std::vector<shlo_arr> outs(max_outputs > 0 ? max_outputs : 1, nullptr);
+  int n_out = 0;
+  const uint64_t l0 = g_launches.load();
+  cudaError_t e = cudaStreamBeginCapture(dev->stream, cudaStreamCaptureModeRelaxed);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    c->eager = true;
+    c->why = std::string("begin capture: ") + cudaGetErrorString(e);
+    return 0;
+  }
+  {
+    std::lock_guard<std::mutex> lk(dev->mu);
+    dev->capturing = true;
+    dev->capture_owner = c;
+    dev->capture_allocs = &c->allocs;
+  }
+  int frc = call_traced(f, c->staging.data(), n_inputs, outs.data(), &n_out, max_outputs);
+  std::string ferr = frc ? shlo_last_error() : "";
+  cudaGraph_t g = nullptr;
+  e = cudaStreamEndCapture(dev->stream, &g);
+  c->launches = g_launches.load() - l0;
+  {
+    std::lock_guard<std::mutex> lk(dev->mu);
+    dev->capturing = false;
+    dev->capture_owner = nullptr;
+    dev->capture_allocs = nullptr;
+    dev->capture_free.clear();  // the graph keeps these blocks (in c->allocs)
+  }
+  if (e == cudaSuccess && !frc) e = cudaGraphInstantiate(&c->exec, g, 0);
+  if (frc || e != cudaSuccess) {
+    cudaGetLastError();
+    release_all(outs.data(), n_out);
+    if (g) cudaGraphDestroy(g);
+    c->exec = nullptr;
+    c->eager = true;
+    c->why = frc ? "traced function inside a capture: " + ferr : std::string("capture: ") + cudaGetErrorString(e);
+    return 0;
+  }
+  c->graph = g;
+  c->outs.assign(outs.begin(), outs.begin() + n_out);
+  return 0;
+}
+
+}  // namespace
 
 extern "C" {
 
@@ -155,17 +320,57 @@ int shlo_compile(shlo_trace_fn f, void *payload, void (*payload_free)(void *), i
 
 void shlo_fn_free(shlo_fn f) {
   if (!f) return;
+  for (auto &kv : f->graphs) destroy_captured(kv.second);
   if (f->payload_free) f->payload_free(f->payload);
   delete f;
 }
 
 int shlo_apply(shlo_fn f, const shlo_arr *inputs, int n_inputs, shlo_arr *outputs, int *n_outputs, int max_outputs) {
   if (!f) return fail("apply: null function");
-  char err[2048];
-  err[0] = 0;
+  for (int i = 0; i < n_inputs; i++)
+    if (!inputs[i]) return fail("apply: input %d is null", i);
+  if (!f->enable) return call_traced(f, inputs, n_inputs, outputs, n_outputs, max_outputs);
+  Device *dev;
+  // No device to record on: the function runs as called (its own ops report
+  // the error, if it has any).
+  if (current_device(&dev)) return call_traced(f, inputs, n_inputs, outputs, n_outputs, max_outputs);
+  if (dev->capturing) return call_traced(f, inputs, n_inputs, outputs, n_outputs, max_outputs);  // nested
+  std::lock_guard<std::mutex> lk(f->mu);
+  const std::string key = signature(dev, inputs, n_inputs);
+  Captured *c;
+  auto it = f->graphs.find(key);
+  if (it != f->graphs.end()) {
+    c = it->second;
+  } else {
+    c = new Captured();
+    if (record(f, dev, inputs, n_inputs, max_outputs, c)) {
+      std::string msg = shlo_last_error();
+      destroy_captured(c);
+      return fail("%s", msg.c_str());
+    }
+    f->graphs[key] = c;
+    if (c->eager && getenv("SHLO_GRAPH_VERBOSE")) fprintf(stderr, "shlo: compiled function runs eagerly: %s\n", c->why.c_str());
+  }
+  if (c->eager) return call_traced(f, inputs, n_inputs, outputs, n_outputs, max_outputs);
+  if ((int)c->outs.size() > max_outputs) return fail("apply: %d outputs, room for %d", (int)c->outs.size(), max_outputs);
+  for (int i = 0; i < n_inputs; i++) {
+    if (inputs[i]->buf && inputs[i]->buf->dev != dev) return fail("apply: input %d is on another device", i);
+    SHLO_TRY(refresh_slot(c, i, inputs[i]));
+  }
+  SHLO_CUDA(cudaGraphLaunch(c->exec, dev->stream));
+  g_launches.fetch_add(c->launches, std::memory_order_relaxed);
   int n = 0;
-  int rc = f->f(f->payload, inputs, n_inputs, outputs, &n, max_outputs, err, sizeof err);
-  if (rc) return fail("apply: traced function: %s", err[0] ? err : shlo_last_error());
+  for (Arr *o : c->outs) {
+    Arr *r;
+    int rc = new_array(dev, o->dtype, o->shape, o->ndim, &r);
+    if (!rc && r->buf) rc = launch_copy_strided(dev, o, r->buf->ptr);
+    if (rc) {
+      if (r) shlo_release(r);
+      release_all(outputs, n);
+      return 1;
+    }
+    outputs[n++] = r;
+  }
   *n_outputs = n;
   return 0;
 }

@@ -7,6 +7,7 @@
 #include <atomic>
 #include <cstdint>
 #include <cstring>
+#include <functional>
 #include <map>
 #include <memory>
 #include <mutex>
@@ -56,8 +57,15 @@ struct Device {
   std::mutex mu;                  // allocator
   std::multimap<size_t, void *> free_blocks;
   size_t pooled_bytes = 0;
-  bool capturing = false;         // a graph capture is in progress on `stream`
-  std::vector<void *> *capture_allocs = nullptr;  // blocks owned by the graph being captured
+  // A CUDA-graph capture in progress on `stream` (shlo_apply of a compiled
+  // function): blocks allocated meanwhile belong to `capture_owner` and are
+  // listed in `capture_allocs`; blocks the capture frees go to `capture_free`
+  // and are reused only by later allocations of the same capture (the graph is
+  // one linear chain of nodes, so stream order makes that reuse safe).
+  bool capturing = false;
+  void *capture_owner = nullptr;
+  std::vector<std::pair<void *, size_t>> *capture_allocs = nullptr;
+  std::multimap<size_t, void *> capture_free;
 };
 // The device current on this host thread, initialised on first use.
 int current_device(Device **out);
@@ -70,14 +78,23 @@ struct Buffer {
   Device *dev = nullptr;
   void *ptr = nullptr;
   size_t bytes = 0;
-  bool graph_owned = false;  // belongs to a captured graph; never pooled while the graph lives
+  // The captured graph this block belongs to (nullptr: the pool's). Such a
+  // block is never pooled while the graph lives.
+  void *graph_owner = nullptr;
+  bool no_recycle = false;  // written at capture time (a constant): never reused inside the capture
   // Derived layouts (e.g. the packed operand of mul_mat), keyed by how they
-  // were derived. Storage is immutable once written, so they stay valid for
-  // the buffer's lifetime.
+  // were derived, each with the launch that derives it again. Storage is
+  // immutable once written, so they stay valid for the buffer's lifetime; the
+  // one exception is the private input copy of a compiled function, which is
+  // rewritten between replays and then re-derives them (buffer_rederive).
   std::mutex derived_mu;
   std::map<std::string, Buffer *> derived;
+  std::map<std::string, std::function<int()>> rederive;
 };
 int buffer_alloc(Device *dev, size_t bytes, Buffer **out);
+// A block for data written by the host at capture time (see shlo_of_bytes).
+int buffer_alloc_constant(Device *dev, size_t bytes, Buffer **out);
+int buffer_rederive(Buffer *b);
 void buffer_retain(Buffer *b);
 void buffer_release(Buffer *b);
 
@@ -151,6 +168,10 @@ inline float bitsf_host(uint32_t u) {
 
 // Launch-error check after a kernel launch.
 int launch_check(const char *what);
+// Kernel launches made through launch_check since the library was loaded.
+extern std::atomic<uint64_t> g_launches;
+// Wait for all queued work of a device (bounded by SHLO_EVAL_TIMEOUT_S).
+int device_wait(Device *dev, const char *what);
 
 // ---- ggml kernels (ggml_kernels.cu) ----
 int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out);

@@ -659,9 +659,18 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
         shlo_release(o);
         return 1;
       }
-      if (!w->buf->graph_owned) {
+      // Not while a capture records (the pack is then a node of the graph), nor
+      // on a buffer a graph owns (it is rewritten by every replay).
+      if (!w->buf->graph_owner && !dev->capturing) {
         buffer_retain(wpk);
         w->buf->derived[key] = wpk;
+        const float *src = (const float *)data_ptr(w);
+        float *dst = (float *)wpk->ptr;
+        const int m = (int)M, k = (int)K;
+        w->buf->rederive[key] = [=]() {
+          launch_pack(src, m, k, wbs, Wb, seg, segp, Mp, -0.0f, dst, dev->stream);
+          return launch_check("mul_mat pack");
+        };
       }
     }
   }

@@ -33,7 +33,7 @@ int cuda_check(cudaError_t e, const char *what) {
   return fail("%s: CUDA error %d (%s)", what, (int)e, cudaGetErrorString(e));
 }
 
-static std::atomic<uint64_t> g_launches{0};
+std::atomic<uint64_t> g_launches{0};
 
 int launch_check(const char *what) {
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -141,25 +141,42 @@ static size_t round_bytes(size_t n) {
   return (n + 511) & ~(size_t)511;
 }
 
-int buffer_alloc(Device *dev, size_t bytes, Buffer **out) {
+static int take_block(Device *dev, size_t want, bool from_capture, void **p, size_t *got) {
+  *p = nullptr;
+  *got = want;
+  std::lock_guard<std::mutex> lk(dev->mu);
+  if (from_capture) {
+    auto it = dev->capture_free.lower_bound(want);
+    if (it != dev->capture_free.end() && it->first <= want * 2 + 65536) {
+      *got = it->first;
+      *p = it->second;
+      dev->capture_free.erase(it);
+      return 1;  // already the graph's
+    }
+  }
+  auto it = dev->free_blocks.lower_bound(want);
+  if (it != dev->free_blocks.end() && it->first <= want * 2 + 65536) {
+    *got = it->first;
+    *p = it->second;
+    dev->free_blocks.erase(it);
+    dev->pooled_bytes -= *got;
+  }
+  return 0;
+}
+
+static int alloc_block(Device *dev, size_t bytes, bool constant, Buffer **out) {
   size_t want = round_bytes(bytes);
   void *p = nullptr;
   size_t got = want;
-  {
-    std::lock_guard<std::mutex> lk(dev->mu);
-    auto it = dev->free_blocks.lower_bound(want);
-    if (it != dev->free_blocks.end() && it->first <= want * 2 + 65536) {
-      got = it->first;
-      p = it->second;
-      dev->free_blocks.erase(it);
-      dev->pooled_bytes -= got;
-    }
-  }
+  const bool cap = dev->capturing && dev->capture_allocs;
+  const int graphs = take_block(dev, want, cap && !constant, &p, &got);
   if (!p) {
     cudaError_t e = cudaMalloc(&p, want);
     if (e != cudaSuccess) {
       cudaGetLastError();
-      // Out of memory: give the pool back and try once more.
+      // Out of memory: give the pool back and try once more (not while a
+      // capture is recording: the stream cannot be waited on then).
+      if (cap) return cuda_check(e, "cudaMalloc");
       std::lock_guard<std::mutex> lk(dev->mu);
       SHLO_CUDA(cudaStreamSynchronize(dev->stream));
       for (auto &kv : dev->free_blocks) cudaFree(kv.second);
@@ -173,13 +190,17 @@ int buffer_alloc(Device *dev, size_t bytes, Buffer **out) {
   b->dev = dev;
   b->ptr = p;
   b->bytes = got;
-  if (dev->capturing && dev->capture_allocs) {
-    b->graph_owned = true;
-    dev->capture_allocs->push_back(p);
+  if (cap) {
+    b->graph_owner = dev->capture_owner;
+    b->no_recycle = constant;
+    if (!graphs) dev->capture_allocs->push_back({p, got});
   }
   *out = b;
   return 0;
 }
+
+int buffer_alloc(Device *dev, size_t bytes, Buffer **out) { return alloc_block(dev, bytes, false, out); }
+int buffer_alloc_constant(Device *dev, size_t bytes, Buffer **out) { return alloc_block(dev, bytes, true, out); }
 
 void buffer_retain(Buffer *b) {
   if (b) b->rc.fetch_add(1);
@@ -189,12 +210,24 @@ void buffer_release(Buffer *b) {
   if (!b) return;
   if (b->rc.fetch_sub(1) != 1) return;
   for (auto &kv : b->derived) buffer_release(kv.second);
-  if (!b->graph_owned) {
-    std::lock_guard<std::mutex> lk(b->dev->mu);
-    b->dev->free_blocks.emplace(b->bytes, b->ptr);
-    b->dev->pooled_bytes += b->bytes;
+  Device *dev = b->dev;
+  {
+    std::lock_guard<std::mutex> lk(dev->mu);
+    if (!b->graph_owner) {
+      dev->free_blocks.emplace(b->bytes, b->ptr);
+      dev->pooled_bytes += b->bytes;
+    } else if (dev->capturing && dev->capture_owner == b->graph_owner && !b->no_recycle) {
+      dev->capture_free.emplace(b->bytes, b->ptr);
+    }
   }
   delete b;
+}
+
+int buffer_rederive(Buffer *b) {
+  std::lock_guard<std::mutex> lk(b->derived_mu);
+  for (auto &kv : b->rederive)
+    if (kv.second()) return 1;
+  return 0;
 }
 
 // ---------------------------------------------------------------- arrays ----
@@ -306,6 +339,8 @@ static int wait_device(Device *dev, const char *what) {
     else std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
 }
+
+int device_wait(Device *dev, const char *what) { return wait_device(dev, what); }
 
 int read_words(Arr *a, uint32_t *words, int n) {
   if ((int64_t)numel(a) * (int64_t)dtype_size(a->dtype) < (int64_t)n * 4)
@@ -442,6 +477,31 @@ int shlo_of_bytes(const void *data, size_t nbytes, const int64_t *shape, int ndi
   Device *dev;
   SHLO_TRY(current_device(&dev));
   Arr *a;
+  if (dev->capturing) {
+    // Recording a compiled function: the data is a constant of the graph. It
+    // is written now, synchronously, into a block the capture never reuses
+    // (a copy on the recording stream would become a node reading this host
+    // memory at every replay).
+    a = new Arr();
+    a->dtype = dtype;
+    a->ndim = ndim;
+    for (int i = 0; i < ndim; i++) a->shape[i] = shape[i];
+    set_row_major(a);
+    if (buffer_alloc_constant(dev, nbytes, &a->buf)) {
+      delete a;
+      return 1;
+    }
+    if (nbytes && cuda_check(cudaMemcpy(a->buf->ptr, data, nbytes, cudaMemcpyHostToDevice), "ofBytes (capture)")) {
+      release_arr(a);
+      return 1;
+    }
+    if (nbytes <= 256) {
+      a->host.assign((const uint8_t *)data, (const uint8_t *)data + nbytes);
+      a->has_host = true;
+    }
+    *out = a;
+    return 0;
+  }
   SHLO_TRY(new_array(dev, dtype, shape, ndim, &a));
   if (nbytes) {
     cudaPointerAttributes at;
