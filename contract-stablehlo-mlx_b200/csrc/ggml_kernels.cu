@@ -252,7 +252,9 @@ struct MMArgs {
   int64_t Nx;       // x rows per batch
   int64_t wbs;      // w batch stride (elements of the original w), 0 = shared
   int r_tiles;      // r tiles per batch
+  int bx_count;     // x batches (1 when w is shared)
   int flavor;
+  float *park;      // k_mul_mat_tm: 64 floats a thread a CTA, T(0..7) between the halves
 };
 
 __global__ void __launch_bounds__(mm::THREADS, 1) k_mul_mat_fast(MMArgs a) {
@@ -385,62 +387,109 @@ __global__ void __launch_bounds__(mm::THREADS, 1) k_mul_mat_fast(MMArgs a) {
 namespace mt {
 // Two CTA shapes: WM = 2 warps along m gives a 128 m x 128 r tile, WM = 1 a
 // 64 m x 256 r tile (for M <= 64, e.g. attention's value product).
+constexpr int BK = 16, GPS = BK / 4, THREADS = 256;  // k per stage, groups of 4 k per stage
 template <int WM>
 struct Tile {
   static constexpr int BM = 64 * WM, BN = 256 / WM;
-  static constexpr int STAGE_FLOATS = 16 * (BM + BN);
+  static constexpr int STAGE_FLOATS = BK * (BM + BN);
 };
-constexpr int BK = 16, NS = 6, THREADS = 256;
-constexpr int TMEM_COLS = 512;
-// More dynamic shared memory than half an SM's: one CTA per SM, since each CTA
-// holds all 512 TMEM columns.
-constexpr size_t SMEM_BYTES = 120 * 1024;
-static_assert((size_t)NS * Tile<1>::STAGE_FLOATS * sizeof(float) <= SMEM_BYTES, "stages fit");
-static_assert((size_t)NS * Tile<2>::STAGE_FLOATS * sizeof(float) <= SMEM_BYTES, "stages fit");
+// Two CTAs per SM (16 warps, 128 registers a thread). Each CTA holds 256 TMEM
+// columns: stack levels 0 and 1 of its 8 warps (64 columns a level a warp).
+// Level 2 (touched at 4 of 16 folds) is a 64 KB shared-memory slab; level 3
+// (pushed once, at S = 7) is parked in a per-CTA global slice (it stays in L2)
+// and added back in the epilogue.
+constexpr int CTAS_PER_SM = 2;
+constexpr int TMEM_COLS = 256;
+constexpr int LEVEL_FLOATS = THREADS * 64;
+template <int WM>
+struct Pipe {
+  static constexpr int NS = WM == 2 ? 3 : 2;  // stages of BK k
+  static constexpr size_t SMEM = (size_t)NS * Tile<WM>::STAGE_FLOATS * 4 + (size_t)LEVEL_FLOATS * 4;
+};
+// Dynamic shared memory above a third of an SM's: at most two CTAs per SM, so
+// their TMEM columns (2 x 256) always fit the SM's 512.
+static_assert(Pipe<2>::SMEM <= 113 * 1024 && Pipe<1>::SMEM <= 113 * 1024, "two CTAs per SM");
+static_assert(3 * Pipe<2>::SMEM > 228 * 1024 && 3 * Pipe<1>::SMEM > 228 * 1024, "no third CTA on an SM");
 }  // namespace mt
 
-// One stack level of this thread's lane: 64 consecutive 32-bit TMEM columns
-// (32x32b shape, lane = the thread's lane in the warp's quarter), moved by one
-// instruction whose completion is waited for inside the same asm statement, so
-// the registers are never used before they are valid. Column 2q holds
-// acc2[q].x and column 2q + 1 holds acc2[q].y.
-__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&t)[64]) {
-  uint32_t r[64];
-  asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63}, [%64];\n"
+// 16 consecutive 32-bit TMEM columns of this thread's lane (32x32b shape: lane =
+// the thread's lane in the warp's quarter), stored / loaded. Each waits for its
+// own completion inside the same asm statement, so the registers are never used
+// before they are valid.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const float *v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16};\n"
+               "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr),
+               "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+               "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+               "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+               "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+               "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+               "r"(__float_as_uint(v[15]))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
+  uint32_t r[16];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, [%16];\n"
                "tcgen05.wait::ld.sync.aligned;\n"
-               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
                : "r"(taddr)
                : "memory");
 #pragma unroll
-  for (int i = 0; i < 64; i++) t[i] = __uint_as_float(r[i]);
-}
-__device__ __forceinline__ void tmem_st64(uint32_t taddr, const float2 (&v)[32]) {
-  asm volatile("tcgen05.st.sync.aligned.32x32b.x64.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32, %33, %34, %35, %36, %37, %38, %39, %40, %41, %42, %43, %44, %45, %46, %47, %48, %49, %50, %51, %52, %53, %54, %55, %56, %57, %58, %59, %60, %61, %62, %63, %64};\n"
-               "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr),
-               "r"(__float_as_uint(v[0].x)), "r"(__float_as_uint(v[0].y)), "r"(__float_as_uint(v[1].x)), "r"(__float_as_uint(v[1].y)), "r"(__float_as_uint(v[2].x)), "r"(__float_as_uint(v[2].y)), "r"(__float_as_uint(v[3].x)), "r"(__float_as_uint(v[3].y)), "r"(__float_as_uint(v[4].x)), "r"(__float_as_uint(v[4].y)), "r"(__float_as_uint(v[5].x)), "r"(__float_as_uint(v[5].y)), "r"(__float_as_uint(v[6].x)), "r"(__float_as_uint(v[6].y)), "r"(__float_as_uint(v[7].x)), "r"(__float_as_uint(v[7].y)), "r"(__float_as_uint(v[8].x)), "r"(__float_as_uint(v[8].y)), "r"(__float_as_uint(v[9].x)), "r"(__float_as_uint(v[9].y)), "r"(__float_as_uint(v[10].x)), "r"(__float_as_uint(v[10].y)), "r"(__float_as_uint(v[11].x)), "r"(__float_as_uint(v[11].y)), "r"(__float_as_uint(v[12].x)), "r"(__float_as_uint(v[12].y)), "r"(__float_as_uint(v[13].x)), "r"(__float_as_uint(v[13].y)), "r"(__float_as_uint(v[14].x)), "r"(__float_as_uint(v[14].y)), "r"(__float_as_uint(v[15].x)), "r"(__float_as_uint(v[15].y)), "r"(__float_as_uint(v[16].x)), "r"(__float_as_uint(v[16].y)), "r"(__float_as_uint(v[17].x)), "r"(__float_as_uint(v[17].y)), "r"(__float_as_uint(v[18].x)), "r"(__float_as_uint(v[18].y)), "r"(__float_as_uint(v[19].x)), "r"(__float_as_uint(v[19].y)), "r"(__float_as_uint(v[20].x)), "r"(__float_as_uint(v[20].y)), "r"(__float_as_uint(v[21].x)), "r"(__float_as_uint(v[21].y)), "r"(__float_as_uint(v[22].x)), "r"(__float_as_uint(v[22].y)), "r"(__float_as_uint(v[23].x)), "r"(__float_as_uint(v[23].y)), "r"(__float_as_uint(v[24].x)), "r"(__float_as_uint(v[24].y)), "r"(__float_as_uint(v[25].x)), "r"(__float_as_uint(v[25].y)), "r"(__float_as_uint(v[26].x)), "r"(__float_as_uint(v[26].y)), "r"(__float_as_uint(v[27].x)), "r"(__float_as_uint(v[27].y)), "r"(__float_as_uint(v[28].x)), "r"(__float_as_uint(v[28].y)), "r"(__float_as_uint(v[29].x)), "r"(__float_as_uint(v[29].y)), "r"(__float_as_uint(v[30].x)), "r"(__float_as_uint(v[30].y)), "r"(__float_as_uint(v[31].x)), "r"(__float_as_uint(v[31].y))
-               : "memory");
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
-// Fold the finished chain of leaf S into the TMEM stack: pop and add the levels
+// Fold the finished chain of leaf S into the stack: pop and add the levels
 // below the first zero bit of S (the left operand is the older value, as in the
-// tree), then push at that level; at S = 15 the result stays in acc (sumf).
-// A level moves as one 64-column transfer, so a fold waits once per level.
-__device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, int S) {
+// tree), then push at that level. Levels 0 and 1 are TMEM columns tcol + 64 L;
+// level 2 is this thread's float4 slots of the shared-memory slab lv2, float4 j
+// of chunk c at lv2[(c * 4 + j) * THREADS] (consecutive threads, consecutive
+// float4: no bank conflicts). Level 3 is pushed only at S = 7 (depth 3) and
+// popped only at S = 15 (depth 4); the caller parks it in global memory, so
+// here depth 3 leaves the value in acc and depth 4 stops after level 2.
+__device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, float4 *lv2, int S) {
   const int depth = __ffs(~S) - 1;  // trailing one bits: 0..4
-  for (int L = 0; L < depth; L++) {
-    float t[64];
-    tmem_ld64(tcol + 64 * L, t);
+  const int pops = depth < 3 ? depth : 3;
 #pragma unroll
-    for (int q = 0; q < 32; q++)
-      acc2[q] = make_float2(__fadd_rn(t[2 * q], acc2[q].x), __fadd_rn(t[2 * q + 1], acc2[q].y));
+  for (int c = 0; c < 4; c++) {
+    float v[16];
+#pragma unroll
+    for (int q = 0; q < 8; q++) {
+      v[2 * q] = acc2[8 * c + q].x;
+      v[2 * q + 1] = acc2[8 * c + q].y;
+    }
+    for (int L = 0; L < pops; L++) {
+      float t[16];
+      if (L < 2) {
+        tmem_ld16(tcol + 64 * L + 16 * c, t);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+          const float4 u = lv2[(c * 4 + j) * mt::THREADS];
+          t[4 * j] = u.x; t[4 * j + 1] = u.y; t[4 * j + 2] = u.z; t[4 * j + 3] = u.w;
+        }
+      }
+#pragma unroll
+      for (int i = 0; i < 16; i++) v[i] = __fadd_rn(t[i], v[i]);
+    }
+    if (depth < 2) {
+      tmem_st16(tcol + 64 * depth + 16 * c, v);
+    } else if (depth == 2) {
+#pragma unroll
+      for (int j = 0; j < 4; j++) lv2[(c * 4 + j) * mt::THREADS] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+    }
+#pragma unroll
+    for (int q = 0; q < 8; q++) acc2[8 * c + q] = make_float2(v[2 * q], v[2 * q + 1]);
   }
-  if (depth < 4) tmem_st64(tcol + 64 * depth, acc2);
 }
 
+// One CTA per tile, m-tile fastest (the CTAs running together share their x
+// tile in L2).
 template <int WM>
-__global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
+__global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMArgs a) {
   using namespace mt;
   constexpr int BM = Tile<WM>::BM, BN = Tile<WM>::BN, STAGE_FLOATS = Tile<WM>::STAGE_FLOATS;
+  constexpr int NS = Pipe<WM>::NS;
   extern __shared__ __align__(16) float smem[];
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -448,13 +497,23 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
   // and mo + 32 + [0,4), its r are ro + [0,4) and ro + 16 + [0,4).
   const int mo = (warp % WM) * 64 + (lane & 7) * 4;
   const int ro = (warp / WM) * 32 + (lane >> 3) * 4;
-  const int m0 = blockIdx.x * BM;
-  const int bx = blockIdx.y / a.r_tiles;
-  const int rt = blockIdx.y % a.r_tiles;
-  const int64_t rl0 = (int64_t)rt * BN;
+  // This CTA's tile: m0, batch bx, first row rl0 (recomputed where needed, so
+  // nothing but the operand pointers stays live through the k-loop).
+  auto pos = [&](int &m0, int &bx, int64_t &rl0) {
+    const int mtiles = a.Mp / BM, tile = blockIdx.x;
+    m0 = (tile % mtiles) * BM;
+    bx = (tile / mtiles) / a.r_tiles;
+    rl0 = (int64_t)((tile / mtiles) % a.r_tiles) * BN;
+  };
   const int Kq = 16 * a.segp;
-  const float *wp = a.wp + (a.wbs ? (int64_t)bx * Kq * a.Mp : 0) + m0;
-  const float *xp = a.xp + (int64_t)bx * Kq * a.Np + rl0;
+  const float *wp, *xp;
+  {
+    int m0, bx;
+    int64_t rl0;
+    pos(m0, bx, rl0);
+    wp = a.wp + (a.wbs ? (int64_t)bx * Kq * a.Mp : 0) + m0;
+    xp = a.xp + (int64_t)bx * Kq * a.Np + rl0;
+  }
   const int nstages = Kq / BK;
 
   if (warp == 0) {
@@ -466,15 +525,16 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
   asm volatile("tcgen05.fence::before_thread_sync;\n");
   __syncthreads();
   asm volatile("tcgen05.fence::after_thread_sync;\n");
-  const uint32_t tcol = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(256 * (warp >> 2));
+  const uint32_t tcol = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(128 * (warp >> 2));
 
   auto issue = [&](int st) {
     float *ws = smem + (st % NS) * STAGE_FLOATS;
     float *xs = ws + BK * BM;
     const int k0 = st * BK;
 #pragma unroll
-    for (int i = 0; i < STAGE_FLOATS / 4 / THREADS; i++) {
+    for (int i = 0; i < (STAGE_FLOATS / 4 + THREADS - 1) / THREADS; i++) {
       int q = tid + i * THREADS;
+      if (q >= STAGE_FLOATS / 4) break;
       if (q < BK * BM / 4) {
         int row = q / (BM / 4), col = (q % (BM / 4)) * 4;
         cp_async16(ws + row * BM + col, wp + (int64_t)(k0 + row) * a.Mp + col);
@@ -492,26 +552,44 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
     cp_async_commit();
   }
 
-  // One flat loop over all groups of 4 packed k-steps; the chain of segment S
-  // ends every segp/4 groups and folds into the TMEM stack (a runtime depth:
-  // the number of trailing one bits of S), so the hot body exists once.
   // acc[j][i] (r index j, m index i) lives in pairs along m: acc2[4 j + i / 2].
   float2 acc2[32];
 #pragma unroll
   for (int i = 0; i < 32; i++) acc2[i] = make_float2(0.0f, 0.0f);
+
+  // T(0..7), the left half of the tree, waits in this CTA's slice of a.park
+  // (float4 i of thread t at float4 index i * THREADS + t: coalesced).
+  auto park = [&](bool load) {
+    float4 *q = reinterpret_cast<float4 *>(a.park + (size_t)blockIdx.x * (THREADS * 64)) + tid;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      float2 &p0 = acc2[2 * i], &p1 = acc2[2 * i + 1];
+      if (load) {
+        const float4 l3 = q[i * THREADS];
+        p0 = make_float2(__fadd_rn(l3.x, p0.x), __fadd_rn(l3.y, p0.y));
+        p1 = make_float2(__fadd_rn(l3.z, p1.x), __fadd_rn(l3.w, p1.y));
+      } else {
+        q[i * THREADS] = make_float4(p0.x, p0.y, p1.x, p1.y);
+      }
+    }
+  };
+
+  // One flat loop over all groups of 4 packed k-steps; the chain of segment S
+  // ends every segp/4 groups and folds into the stack (a runtime depth: the
+  // number of trailing one bits of S), so the hot body exists once.
   const int groups_per_seg = a.segp / 4;
   const int ngroups = 16 * groups_per_seg;
   int S = 0, gi = 0;
   for (int g = 0; g < ngroups; g++) {
-    const int stg = g >> 2;
-    if ((g & 3) == 0) {
+    const int stg = g / GPS;
+    if (g % GPS == 0) {
       cp_async_wait<NS - 2>();
       __syncthreads();
       if (stg + NS - 1 < nstages) issue(stg + NS - 1);
       cp_async_commit();
     }
-    const float *ws = smem + (stg % NS) * STAGE_FLOATS + (g & 3) * 4 * BM;
-    const float *xs = smem + (stg % NS) * STAGE_FLOATS + BK * BM + (g & 3) * 4 * BN;
+    const float *ws = smem + (stg % NS) * STAGE_FLOATS + (g % GPS) * 4 * BM;
+    const float *xs = smem + (stg % NS) * STAGE_FLOATS + BK * BM + (g % GPS) * 4 * BN;
 #pragma unroll
     for (int kk = 0; kk < 4; kk++) {
       const float4 w0 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo);
@@ -530,8 +608,10 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
       }
     }
     if (++gi == groups_per_seg) {
-      tfold_rt(acc2, tcol, S);
+      tfold_rt(acc2, tcol, reinterpret_cast<float4 *>(smem + NS * STAGE_FLOATS) + tid, S);
       gi = 0;
+      // After S = 7 the fold left T(0..7) in acc (depth 3 pushes nothing).
+      if (S == 7) park(false);
       if (++S < 16) {
 #pragma unroll
         for (int i = 0; i < 32; i++) acc2[i] = make_float2(0.0f, 0.0f);
@@ -547,7 +627,12 @@ __global__ void __launch_bounds__(mt::THREADS, 1) k_mul_mat_tm(MMArgs a) {
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_base), "n"(TMEM_COLS));
 
-  // Epilogue: the tail (K mod 16 elements, in order) and the store.
+  // Epilogue: the root of the tree, T(0..7) + T(8..15); then the tail (K mod 16
+  // elements, in order) and the store.
+  park(true);
+  int m0, bx;
+  int64_t rl0;
+  pos(m0, bx, rl0);
   const int64_t rbase = (int64_t)bx * a.Nx;
   const bool vec = (a.M & 3) == 0;
 #pragma unroll
@@ -696,7 +781,8 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
   a.wbs = wbs;
   a.r_tiles = Np / BN;
   a.flavor = flavor;
-  const size_t smem = mt::SMEM_BYTES;
+  a.bx_count = (int)Bx;
+  const size_t smem = WM == 1 ? mt::Pipe<1>::SMEM : mt::Pipe<2>::SMEM;
   static bool attr_done[2][64] = {{false}};
   if (!attr_done[WM - 1][dev->id]) {
     if (cuda_check(cudaFuncSetAttribute(WM == 1 ? k_mul_mat_tm<1> : k_mul_mat_tm<2>,
@@ -709,12 +795,21 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
     }
     attr_done[WM - 1][dev->id] = true;
   }
-  dim3 grid(Mp / BM, (unsigned)(Bx * a.r_tiles));
+  const unsigned grid = (unsigned)((int64_t)(Mp / BM) * Bx * a.r_tiles);
+  Buffer *park;
+  if (buffer_alloc(dev, (size_t)grid * mt::THREADS * 64 * sizeof(float), &park)) {
+    buffer_release(wpk);
+    buffer_release(xpk);
+    shlo_release(o);
+    return 1;
+  }
+  a.park = (float *)park->ptr;
   if (WM == 1)
     k_mul_mat_tm<1><<<grid, mt::THREADS, smem, dev->stream>>>(a);
   else
     k_mul_mat_tm<2><<<grid, mt::THREADS, smem, dev->stream>>>(a);
   int rc = launch_check("mul_mat");
+  buffer_release(park);
   buffer_release(wpk);
   buffer_release(xpk);
   if (rc) {
