@@ -485,7 +485,9 @@ __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, floa
 
 // One CTA per tile, m-tile fastest (the CTAs running together share their x
 // tile in L2).
-template <int WM>
+// STAGE_FOLD: every segment spans whole stages (segp a multiple of 16), so the
+// fold check runs once per stage; otherwise after every group of 4 k.
+template <int WM, bool STAGE_FOLD>
 __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMArgs a) {
   using namespace mt;
   constexpr int BM = Tile<WM>::BM, BN = Tile<WM>::BN, STAGE_FLOATS = Tile<WM>::STAGE_FLOATS;
@@ -527,23 +529,23 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
   asm volatile("tcgen05.fence::after_thread_sync;\n");
   const uint32_t tcol = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(128 * (warp >> 2));
 
+  // Stage copies: this thread moves w rows tid / (BM/4) + j (1024/BM), x rows
+  // tid / (BN/4) + j (1024/BN), 16 bytes at column 4 (tid % (BM/4 or BN/4)).
+  // The addresses are rebuilt at every stage (once per 16 k) rather than kept
+  // live through the k-loop.
+  constexpr int WCP = BM / 64, XCP = BN / 64;  // 16-byte copies a thread a stage
   auto issue = [&](int st) {
-    float *ws = smem + (st % NS) * STAGE_FLOATS;
-    float *xs = ws + BK * BM;
-    const int k0 = st * BK;
+    const int t = threadIdx.x;
+    float *sb = smem + (st % NS) * STAGE_FLOATS;
+    const int64_t k0 = (int64_t)st * BK;
+    const float *gw = wp + (k0 + t / (BM / 4)) * a.Mp + (t % (BM / 4)) * 4;
+    const float *gx = xp + (k0 + t / (BN / 4)) * a.Np + (t % (BN / 4)) * 4;
+    float *dw = sb + (t / (BM / 4)) * BM + (t % (BM / 4)) * 4;
+    float *dx = sb + BK * BM + (t / (BN / 4)) * BN + (t % (BN / 4)) * 4;
 #pragma unroll
-    for (int i = 0; i < (STAGE_FLOATS / 4 + THREADS - 1) / THREADS; i++) {
-      int q = tid + i * THREADS;
-      if (q >= STAGE_FLOATS / 4) break;
-      if (q < BK * BM / 4) {
-        int row = q / (BM / 4), col = (q % (BM / 4)) * 4;
-        cp_async16(ws + row * BM + col, wp + (int64_t)(k0 + row) * a.Mp + col);
-      } else {
-        q -= BK * BM / 4;
-        int row = q / (BN / 4), col = (q % (BN / 4)) * 4;
-        cp_async16(xs + row * BN + col, xp + (int64_t)(k0 + row) * a.Np + col);
-      }
-    }
+    for (int j = 0; j < WCP; j++) cp_async16(dw + j * (1024 / BM) * BM, gw + (int64_t)j * (1024 / BM) * a.Mp);
+#pragma unroll
+    for (int j = 0; j < XCP; j++) cp_async16(dx + j * (1024 / BN) * BN, gx + (int64_t)j * (1024 / BN) * a.Np);
   };
 
 #pragma unroll
@@ -574,42 +576,15 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
     }
   };
 
-  // One flat loop over all groups of 4 packed k-steps; the chain of segment S
-  // ends every segp/4 groups and folds into the stack (a runtime depth: the
-  // number of trailing one bits of S), so the hot body exists once.
-  const int groups_per_seg = a.segp / 4;
-  const int ngroups = 16 * groups_per_seg;
-  int S = 0, gi = 0;
-  for (int g = 0; g < ngroups; g++) {
-    const int stg = g / GPS;
-    if (g % GPS == 0) {
-      cp_async_wait<NS - 2>();
-      __syncthreads();
-      if (stg + NS - 1 < nstages) issue(stg + NS - 1);
-      cp_async_commit();
-    }
-    const float *ws = smem + (stg % NS) * STAGE_FLOATS + (g % GPS) * 4 * BM;
-    const float *xs = smem + (stg % NS) * STAGE_FLOATS + BK * BM + (g % GPS) * 4 * BN;
-#pragma unroll
-    for (int kk = 0; kk < 4; kk++) {
-      const float4 w0 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo);
-      const float4 w1 = *reinterpret_cast<const float4 *>(ws + kk * BM + mo + 32);
-      const float4 x0 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro);
-      const float4 x1 = *reinterpret_cast<const float4 *>(xs + kk * BN + ro + 16);
-      // Paired FP32 FMAs: each component rounds exactly as __fmaf_rn.
-      const float2 wp2[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
-                             make_float2(w1.z, w1.w)};
-      const float xr[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
-#pragma unroll
-      for (int j = 0; j < 8; j++) {
-        const float2 xj = make_float2(xr[j], xr[j]);
-#pragma unroll
-        for (int i = 0; i < 4; i++) acc2[j * 4 + i] = __ffma2_rn(wp2[i], xj, acc2[j * 4 + i]);
-      }
-    }
-    if (++gi == groups_per_seg) {
-      tfold_rt(acc2, tcol, reinterpret_cast<float4 *>(smem + NS * STAGE_FLOATS) + tid, S);
-      gi = 0;
+  // Stage-major k-loop, the groups of 4 k of a stage unrolled; the chain of
+  // segment S ends every segp/4 groups and folds into the stack (a runtime
+  // depth: the number of trailing one bits of S).
+  float4 *lv2 = reinterpret_cast<float4 *>(smem + NS * STAGE_FLOATS) + tid;
+  int S = 0, gleft = a.segp / 4;
+  auto end_group = [&]() {
+    if (--gleft == 0) {
+      tfold_rt(acc2, tcol, lv2, S);
+      gleft = a.segp / 4;
       // After S = 7 the fold left T(0..7) in acc (depth 3 pushes nothing).
       if (S == 7) park(false);
       if (++S < 16) {
@@ -617,6 +592,41 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
         for (int i = 0; i < 32; i++) acc2[i] = make_float2(0.0f, 0.0f);
       }
     }
+  };
+  int so = 0;  // offset of stage st % NS
+  for (int st = 0; st < nstages; st++) {
+    cp_async_wait<NS - 2>();
+    __syncthreads();
+    if (st + NS - 1 < nstages) issue(st + NS - 1);
+    cp_async_commit();
+    const float *ws = smem + so + mo;
+    const float *xs = smem + so + BK * BM + ro;
+#pragma unroll
+    for (int q = 0; q < GPS; q++) {
+#pragma unroll
+      for (int kk = 0; kk < 4; kk++) {
+        const float4 w0 = *reinterpret_cast<const float4 *>(ws + (4 * q + kk) * BM);
+        const float4 w1 = *reinterpret_cast<const float4 *>(ws + (4 * q + kk) * BM + 32);
+        const float4 x0 = *reinterpret_cast<const float4 *>(xs + (4 * q + kk) * BN);
+        const float4 x1 = *reinterpret_cast<const float4 *>(xs + (4 * q + kk) * BN + 16);
+        // Paired FP32 FMAs: each component rounds exactly as __fmaf_rn.
+        const float2 wp2[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                               make_float2(w1.z, w1.w)};
+        const float xr[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const float2 xj = make_float2(xr[j], xr[j]);
+#pragma unroll
+          for (int i = 0; i < 4; i++) acc2[j * 4 + i] = __ffma2_rn(wp2[i], xj, acc2[j * 4 + i]);
+        }
+      }
+      if (!STAGE_FOLD) end_group();
+    }
+    if (STAGE_FOLD) {
+      gleft -= GPS - 1;
+      end_group();
+    }
+    so = so + STAGE_FLOATS == NS * STAGE_FLOATS ? 0 : so + STAGE_FLOATS;
   }
   cp_async_wait<0>();
 
@@ -783,17 +793,22 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
   a.flavor = flavor;
   a.bx_count = (int)Bx;
   const size_t smem = WM == 1 ? mt::Pipe<1>::SMEM : mt::Pipe<2>::SMEM;
-  static bool attr_done[2][64] = {{false}};
-  if (!attr_done[WM - 1][dev->id]) {
-    if (cuda_check(cudaFuncSetAttribute(WM == 1 ? k_mul_mat_tm<1> : k_mul_mat_tm<2>,
-                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
-                   "mul_mat attribute")) {
+  static bool attr_done[64] = {false};
+  if (!attr_done[dev->id]) {
+    if (cuda_check(cudaFuncSetAttribute(k_mul_mat_tm<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)mt::Pipe<1>::SMEM), "mul_mat attribute") ||
+        cuda_check(cudaFuncSetAttribute(k_mul_mat_tm<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)mt::Pipe<1>::SMEM), "mul_mat attribute") ||
+        cuda_check(cudaFuncSetAttribute(k_mul_mat_tm<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)mt::Pipe<2>::SMEM), "mul_mat attribute") ||
+        cuda_check(cudaFuncSetAttribute(k_mul_mat_tm<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        (int)mt::Pipe<2>::SMEM), "mul_mat attribute")) {
       buffer_release(wpk);
       buffer_release(xpk);
       shlo_release(o);
       return 1;
     }
-    attr_done[WM - 1][dev->id] = true;
+    attr_done[dev->id] = true;
   }
   const unsigned grid = (unsigned)((int64_t)(Mp / BM) * Bx * a.r_tiles);
   Buffer *park;
@@ -804,10 +819,15 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
     return 1;
   }
   a.park = (float *)park->ptr;
-  if (WM == 1)
-    k_mul_mat_tm<1><<<grid, mt::THREADS, smem, dev->stream>>>(a);
+  const bool stage_fold = segp % 16 == 0;
+  if (WM == 1 && stage_fold)
+    k_mul_mat_tm<1, true><<<grid, mt::THREADS, smem, dev->stream>>>(a);
+  else if (WM == 1)
+    k_mul_mat_tm<1, false><<<grid, mt::THREADS, smem, dev->stream>>>(a);
+  else if (stage_fold)
+    k_mul_mat_tm<2, true><<<grid, mt::THREADS, smem, dev->stream>>>(a);
   else
-    k_mul_mat_tm<2><<<grid, mt::THREADS, smem, dev->stream>>>(a);
+    k_mul_mat_tm<2, false><<<grid, mt::THREADS, smem, dev->stream>>>(a);
   int rc = launch_check("mul_mat");
   buffer_release(park);
   buffer_release(wpk);
