@@ -516,7 +516,8 @@ def profile_run(args):
         w = D.init_weights(cfg, seed=1)
         W = [M.of_numpy(w[n]) for n, _ in D.weight_specs(cfg)]
         X = [M.of_numpy(a) for a in D.inputs(cfg, B, seed=1)]
-        fn = E.prepare(E.load(D.module_text(cfg, B)), None, True)
+        # called eagerly, so every kernel is a launch of its own in the list
+        fn = E.prepare(E.load(D.module_text(cfg, B)), None, False)
         c0 = M.launch_count()
         M.eval_([M.apply(fn, X + W)[0]])  # warm-up step
         c1 = M.launch_count()

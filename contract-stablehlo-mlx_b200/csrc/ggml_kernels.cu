@@ -934,7 +934,16 @@ __global__ void g_soft_max(const float *__restrict__ x, float *__restrict__ y, i
         if (float_sum) {
           for (int k = 0; k < n; k++) fs = __fadd_rn(fs, (float)parts[k]);
         } else {
-          for (int k = 0; k < n; k++) sum = __dadd_rn(sum, parts[k]);
+          // eight parts loaded ahead of their serial adds
+          int k = 0;
+          for (; k + 8 <= n; k += 8) {
+            double v[8];
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = parts[k + i];
+#pragma unroll
+            for (int i = 0; i < 8; i++) sum = __dadd_rn(sum, v[i]);
+          }
+          for (; k < n; k++) sum = __dadd_rn(sum, parts[k]);
         }
       }
       __syncwarp();
@@ -1128,17 +1137,36 @@ __global__ void __launch_bounds__(NORM_THREADS) g_norm_rows(const float *__restr
   }
   __syncthreads();
   if (tid < nr) {
+    // The chains run several steps at a time with their operands loaded and
+    // widened first, so only the binary64 adds are serial.
     const float *row = tile + tid * pitch;
     double sum = 0.0;
-    for (int c = 0; c < ncols; c++) sum = __dadd_rn(sum, (double)row[c]);
-    const float mean = __fdiv_rn(__double2float_rn(sum), (float)ncols);
-    double s2 = 0.0;
-    for (int c = 0; c < ncols; c += 4) {  // ncols % 4 == 0: no tail
-      float d0 = __fsub_rn(row[c], mean), d1 = __fsub_rn(row[c + 1], mean);
-      float d2 = __fsub_rn(row[c + 2], mean), d3 = __fsub_rn(row[c + 3], mean);
-      s2 = __dadd_rn(s2, (double)__fadd_rn(__fadd_rn(__fmul_rn(d0, d0), __fmul_rn(d1, d1)),
-                                           __fadd_rn(__fmul_rn(d2, d2), __fmul_rn(d3, d3))));
+    int c = 0;
+    for (; c + 8 <= ncols; c += 8) {
+      double v[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) v[i] = (double)row[c + i];
+#pragma unroll
+      for (int i = 0; i < 8; i++) sum = __dadd_rn(sum, v[i]);
     }
+    for (; c < ncols; c++) sum = __dadd_rn(sum, (double)row[c]);
+    const float mean = __fdiv_rn(__double2float_rn(sum), (float)ncols);
+    auto group = [&](int g) {
+      float d0 = __fsub_rn(row[g], mean), d1 = __fsub_rn(row[g + 1], mean);
+      float d2 = __fsub_rn(row[g + 2], mean), d3 = __fsub_rn(row[g + 3], mean);
+      return (double)__fadd_rn(__fadd_rn(__fmul_rn(d0, d0), __fmul_rn(d1, d1)),
+                               __fadd_rn(__fmul_rn(d2, d2), __fmul_rn(d3, d3)));
+    };
+    double s2 = 0.0;
+    c = 0;
+    for (; c + 16 <= ncols; c += 16) {  // ncols % 4 == 0: no tail
+      double q[4];
+#pragma unroll
+      for (int i = 0; i < 4; i++) q[i] = group(c + 4 * i);
+#pragma unroll
+      for (int i = 0; i < 4; i++) s2 = __dadd_rn(s2, q[i]);
+    }
+    for (; c < ncols; c += 4) s2 = __dadd_rn(s2, group(c));
     const float var = __double2float_rn(__ddiv_rn(s2, (double)ncols));
     ms[tid] = mean;
     ss[tid] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
@@ -1256,14 +1284,14 @@ __global__ void g_silu(const float *__restrict__ x, float *__restrict__ y, int64
 // gelu_erf: Shaders.lean:186-199 (ggml_vec_gelu_erf_f32):
 // y = (0.5f*x) * (1.0f + erff(x*SQRT_2_INV)) with the correctly rounded erff; a
 // NaN input returns itself quieted, as every arm64 step does.
-__device__ __forceinline__ float gelu_one(float v, int gpu_erf) {
+__device__ __forceinline__ float gelu_one(float v, int gpu_erf, const shlo_erf::ErfSmem *t) {
   float ev;
   if (gpu_erf) {
     // The planted fault: GELU's tanh form (SQRT_2_OVER_PI, GELU_COEF_A of vec.h).
     ev = tanhf(__fmul_rn(__fmul_rn(bitsf(0x3F4C422Au), v),
                          __fadd_rn(1.0f, __fmul_rn(__fmul_rn(bitsf(0x3D372713u), v), v))));
   } else {
-    ev = shlo_erf::erff_cr(__fmul_rn(v, bitsf(0x3F3504F3u)));
+    ev = shlo_erf::erff_cr_smem(__fmul_rn(v, bitsf(0x3F3504F3u)), t);
   }
   float r = __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, ev));
   const uint32_t b = fbits(v);
@@ -1273,21 +1301,29 @@ __device__ __forceinline__ float gelu_one(float v, int gpu_erf) {
 }
 
 __global__ void g_gelu_erf(const float *__restrict__ x, float *__restrict__ y, int64_t n, int gpu_erf) {
-  map_f32(x, y, n, [gpu_erf](float v) { return gelu_one(v, gpu_erf); });
+  __shared__ shlo_erf::ErfSmem tab;
+  shlo_erf::erf_smem_load(&tab);
+  __syncthreads();
+  const shlo_erf::ErfSmem *t = &tab;
+  map_f32(x, y, n, [gpu_erf, t](float v) { return gelu_one(v, gpu_erf, t); });
 }
 
 // erff_map: Shaders.lean:204-208: y[t] = bits(erff(bits^-1(base + t))), four
 // consecutive patterns per thread and trip, stored as one 16-byte vector.
 __global__ void g_erff_map(uint32_t base, int64_t n, uint32_t *__restrict__ y) {
+  __shared__ shlo_erf::ErfSmem tab;
+  shlo_erf::erf_smem_load(&tab);
+  __syncthreads();
+  const shlo_erf::ErfSmem *t = &tab;
   const int64_t nv = n >> 2;
   const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = t0; i < nv; i += stride) {
     const uint32_t p = base + (uint32_t)(4 * i);
     reinterpret_cast<uint4 *>(y)[i] =
-        make_uint4(fbits(shlo_erf::erff_cr(bitsf(p))), fbits(shlo_erf::erff_cr(bitsf(p + 1u))),
-                   fbits(shlo_erf::erff_cr(bitsf(p + 2u))), fbits(shlo_erf::erff_cr(bitsf(p + 3u))));
+        make_uint4(fbits(shlo_erf::erff_cr_smem(bitsf(p), t)), fbits(shlo_erf::erff_cr_smem(bitsf(p + 1u), t)),
+                   fbits(shlo_erf::erff_cr_smem(bitsf(p + 2u), t)), fbits(shlo_erf::erff_cr_smem(bitsf(p + 3u), t)));
   }
-  for (int64_t j = 4 * nv + t0; j < n; j += stride) y[j] = fbits(shlo_erf::erff_cr(bitsf(base + (uint32_t)j)));
+  for (int64_t j = 4 * nv + t0; j < n; j += stride) y[j] = fbits(shlo_erf::erff_cr_smem(bitsf(base + (uint32_t)j), t));
 }
 
 // divide and sqrt: SoftFloat.lean:262-305, correctly rounded binary32 with the

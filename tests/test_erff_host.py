@@ -2,8 +2,9 @@
 the oracle (erfl with binary128 hard cases) -- no GPU needed.
 
 Both paths of contract-stablehlo-mlx_b200/csrc/erff_cr.cuh are checked: the
-fast path (binary64 erf + rounding test) and the double-double series alone,
-which the fast path falls back to near rounding midpoints.
+fast path (piecewise binary64 polynomials + rounding test), exhaustively below
+4, and the double-double series alone, which the fast path falls back to near
+rounding midpoints. The host build runs the same arithmetic as the device.
 """
 import ctypes
 import os
@@ -23,12 +24,13 @@ def host():
     src = os.path.join(HERE, "helpers", "erff_host.cpp")
     hdr = os.path.join(HERE, "..", "contract-stablehlo-mlx_b200", "csrc", "erff_cr.cuh")
     if not os.path.exists(SO) or os.path.getmtime(SO) < max(os.path.getmtime(src), os.path.getmtime(hdr)):
-        subprocess.run(["/usr/bin/g++", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared", src, "-o", SO],
-                       check=True)
+        subprocess.run(["/usr/bin/g++", "-O2", "-ffp-contract=off", "-fno-fast-math", "-fPIC", "-shared", "-pthread",
+                        src, "-o", SO], check=True)
     L = ctypes.CDLL(SO)
     p = np.ctypeslib.ndpointer(dtype=np.uint32, flags="C_CONTIGUOUS")
     for f in (L.erff_cr_bits, L.erff_slow_bits):
         f.argtypes = [p, p, ctypes.c_long]
+    L.erff_cr_range.argtypes = [ctypes.c_uint32, ctypes.c_long, p, ctypes.c_int]
     return L
 
 
@@ -79,3 +81,20 @@ def test_nan_inf_zero(host):
     got = np.empty_like(xb)
     host.erff_cr_bits(xb, got, xb.size)
     assert list(got) == [0x7FC00000, 0x7FC00001, 0xFFE00000, 0x3F800000, 0xBF800000, 0, 0x80000000]
+
+
+@pytest.mark.slow
+def test_exhaustive_below_4(host):
+    """Every non-negative binary32 input below 4 (the rest is +-1, NaN or a sign
+    flip), in chunks of 2^24: the polynomial fast path with its rounding test,
+    and the series behind it, against the oracle's erfl/binary128 rounding."""
+    n_threads = max(1, os.cpu_count() or 1)
+    chunk = 1 << 24
+    got = np.empty(chunk, dtype=np.uint32)
+    bad = 0
+    for base in range(0, 0x40800000, chunk):
+        n = min(chunk, 0x40800000 - base)
+        host.erff_cr_range(base, n, got, n_threads)
+        want = O.erff_range(base, n, n_threads)
+        bad += int(np.count_nonzero(got[:n] != want))
+    assert bad == 0

@@ -2,12 +2,11 @@
 all 2^32 binary32 inputs, NaN, infinities and subnormals included.
 
 Chunk by chunk (2^24 inputs), the GPU kernel erff_map is compared on the
-device with this platform's CPU erff (libm_erff_range, the correctly rounded
-erff computed on the host cores): `binary ne` then `count_nonzero`, as the
-reference does. The two sides evaluate binary64 erf with different libraries
-(CUDA's on the device, the C library's on the host) before the correctly
-rounded rounding step, so agreement on every input is a cross-check of both.
-Then the planted fault: the CPU side shifted by one input must differ.
+device with the oracle's correctly rounded erff computed on the host cores
+(erfl, with binary128 re-evaluation near rounding midpoints: a method
+independent of the kernel's piecewise binary64 polynomials): `binary ne` then
+`count_nonzero`, as the reference does. Then the planted fault: the CPU side
+shifted by one input must differ.
 """
 import concurrent.futures as cf
 import os
@@ -18,6 +17,7 @@ import pytest
 
 pytestmark = [pytest.mark.gpu, pytest.mark.slow]
 
+from oracle import oracle as O  # noqa: E402
 from shlo import mlx as M  # noqa: E402
 from shlo import run as Run  # noqa: E402
 
@@ -32,7 +32,7 @@ def test_erff_exhaustive():
     t0 = time.perf_counter()
     gpu_s = 0.0
     with cf.ThreadPoolExecutor(max_workers=workers) as ex:
-        futs = {ex.submit(M.libm_erff_range, c * chunk, chunk): c for c in range(chunks)}
+        futs = {ex.submit(O.erff_range, c * chunk, chunk, 1): c for c in range(chunks)}
         for fut in cf.as_completed(futs):
             c = futs[fut]
             base = c * chunk
@@ -40,7 +40,7 @@ def test_erff_exhaustive():
             gpu = Run.erff_map(base, chunk)
             M.eval_([gpu])
             gpu_s += time.perf_counter() - g0
-            cpu = M.of_bytes(fut.result(), [chunk], M.dtU32)
+            cpu = M.of_numpy(fut.result(), M.dtU32)
             k = M.count_nonzero(M.binary(M.opNe, gpu, cpu))
             if k:
                 bad += k
@@ -51,5 +51,5 @@ def test_erff_exhaustive():
     assert bad == 0, "first differing chunk at %08x" % first_bad
     # Planted: compare against the CPU routine one input late.
     gpu = Run.erff_map(0x3F000000, chunk)
-    cpu = M.of_bytes(M.libm_erff_range(0x3F000001, chunk), [chunk], M.dtU32)
+    cpu = M.of_numpy(O.erff_range(0x3F000001, chunk), M.dtU32)
     assert M.count_nonzero(M.binary(M.opNe, gpu, cpu)) != 0
