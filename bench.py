@@ -51,7 +51,7 @@ def parse_args():
     ap.add_argument("--impl", default="shlo", choices=["shlo", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     # Short runs to wrap in a profiler (no JSON line): one warm denoiser step,
-    # mul_mat alone at --mm-shape K,M,R, or every exact kernel once (batch 16).
+    # mul_mat alone at --mm-shape K,M,R[,N], or every exact kernel once (batch 16).
     ap.add_argument("--profile-run", choices=["step", "mul_mat", "kernels"])
     ap.add_argument("--mm-shape", default="512,1536,16384")
     return ap.parse_args()
@@ -529,12 +529,17 @@ def profile_run(args):
         M.eval_(outs)
         print("kernels: %d launches: %s" % (len(suite), "; ".join(n for n, _, _, _ in suite)))
     else:
-        K, Mm, R = (int(v) for v in args.mm_shape.split(","))
+        # K,M,R (one shared w) or K,M,R,N (R / N batches, each with its own w)
+        dims = [int(v) for v in args.mm_shape.split(",")]
+        K, Mm, R = dims[:3]
+        N = dims[3] if len(dims) > 3 else R
+        nb = R // N if len(dims) > 3 else 1
         rng = np.random.default_rng(0)
-        wa = M.of_numpy(rng.standard_normal((Mm, K)).astype(np.float32))
+        wa = M.of_numpy(rng.standard_normal((nb * Mm, K)).astype(np.float32))
         xa = M.of_numpy(rng.standard_normal((R, K)).astype(np.float32))
+        wbs = Mm * K if nb > 1 else 0
         for _ in range(3):
-            y = Run.mul_mat(wa, xa, K, Mm, R, R, 0)
+            y = Run.mul_mat(wa, xa, K, Mm, R, N, wbs)
         M.eval_([y])
         print("mul_mat %s: 3 launches" % args.mm_shape)
 

@@ -8,6 +8,8 @@
 #include <cmath>
 
 #include "common.cuh"
+#include <utility>
+
 #include "erff_cr.cuh"
 
 namespace shlo {
@@ -676,6 +678,111 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
   }
 }
 
+// Short K (segp == 4, K < 80: every segment is 4 packed k-steps, e.g.
+// attention's K = 64 head dimension). The whole packed K of a 64 m x 64 r tile
+// sits in shared memory (2 x 16 KB), each thread owns 4 m x 4 r outputs, and
+// the 16 segments are unrolled with their folds known at compile time, so the
+// 4-level stack lives in registers: no TMEM, and no fold waits. A thread's m
+// are mo + [0,4), its r are ro + [0,4) (warps 2 (m) x 4 (r), lanes 8 x 4).
+namespace ms {
+constexpr int BM = 64, BN = 64, KQ = 64, THREADS = 256;
+}
+
+template <int S>
+__device__ __forceinline__ void fold_regs(float2 (&acc)[8], float2 (&st)[4][8]) {
+  constexpr int depth = S == 15 ? 4 : (S & 1) == 0 ? 0 : (S & 3) == 1 ? 1 : (S & 7) == 3 ? 2 : 3;
+#pragma unroll
+  for (int L = 0; L < depth; L++)
+#pragma unroll
+    for (int i = 0; i < 8; i++) acc[i] = make_float2(__fadd_rn(st[L][i].x, acc[i].x), __fadd_rn(st[L][i].y, acc[i].y));
+  if (depth < 4) {
+#pragma unroll
+    for (int i = 0; i < 8; i++) st[depth][i] = acc[i];
+  }
+}
+
+template <int S>
+__device__ __forceinline__ void seg_regs(const float *ws, const float *xs, float2 (&acc)[8], float2 (&st)[4][8]) {
+#pragma unroll
+  for (int i = 0; i < 8; i++) acc[i] = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int kk = 0; kk < 4; kk++) {
+    const float4 w4 = *reinterpret_cast<const float4 *>(ws + (4 * S + kk) * ms::BM);
+    const float4 x4 = *reinterpret_cast<const float4 *>(xs + (4 * S + kk) * ms::BN);
+    const float2 w01 = make_float2(w4.x, w4.y), w23 = make_float2(w4.z, w4.w);
+    const float xr[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float2 xj = make_float2(xr[j], xr[j]);
+      acc[2 * j] = __ffma2_rn(w01, xj, acc[2 * j]);
+      acc[2 * j + 1] = __ffma2_rn(w23, xj, acc[2 * j + 1]);
+    }
+  }
+  fold_regs<S>(acc, st);
+}
+
+template <int... S>
+__device__ __forceinline__ void all_segs(const float *ws, const float *xs, float2 (&acc)[8], float2 (&st)[4][8],
+                                         std::integer_sequence<int, S...>) {
+  (seg_regs<S>(ws, xs, acc, st), ...);
+}
+
+__global__ void __launch_bounds__(ms::THREADS, 2) k_mul_mat_short(MMArgs a) {
+  using namespace ms;
+  __shared__ __align__(16) float ws[KQ * BM];
+  __shared__ __align__(16) float xs[KQ * BN];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int mo = (warp & 1) * 32 + (lane & 7) * 4;
+  const int ro = (warp >> 1) * 16 + (lane >> 3) * 4;
+  const int mtiles = a.Mp / BM;
+  const int m0 = (blockIdx.x % mtiles) * BM;
+  const int rb = blockIdx.x / mtiles;
+  const int bx = rb / a.r_tiles;
+  const int64_t rl0 = (int64_t)(rb % a.r_tiles) * BN;
+  const float *wp = a.wp + (a.wbs ? (int64_t)bx * KQ * a.Mp : 0) + m0;
+  const float *xp = a.xp + (int64_t)bx * KQ * a.Np + rl0;
+#pragma unroll
+  for (int i = 0; i < KQ * BM / 4 / THREADS; i++) {
+    const int q = tid + i * THREADS, row = q / (BM / 4), col = (q % (BM / 4)) * 4;
+    cp_async16(ws + row * BM + col, wp + (int64_t)row * a.Mp + col);
+    cp_async16(xs + row * BN + col, xp + (int64_t)row * a.Np + col);
+  }
+  cp_async_commit();
+  cp_async_wait<0>();
+  __syncthreads();
+
+  float2 acc[8], st[4][8];
+  all_segs(ws + mo, xs + ro, acc, st, std::make_integer_sequence<int, 16>{});
+
+  // Epilogue: the tail (K mod 16 elements, in order) and the store.
+  const int64_t rbase = (int64_t)bx * a.Nx;
+  const bool vec = (a.M & 3) == 0;
+  const int mb = m0 + mo;
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    const int64_t rl = rl0 + ro + j;
+    if (rl >= a.Nx) continue;
+    const int64_t r = rbase + rl;
+    float v[4] = {acc[2 * j].x, acc[2 * j].y, acc[2 * j + 1].x, acc[2 * j + 1].y};
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int m = mb + i;
+      if (a.np < a.K && m < a.M) {
+        const float *wr = a.w + (a.wbs ? (int64_t)bx * a.wbs : 0) + (int64_t)m * a.K;
+        v[i] = dot_tail(wr, a.x + r * a.K, a.np, a.K, v[i], a.flavor);
+      }
+      v[i] = arm_nan(v[i]);
+    }
+    if (vec && mb + 3 < a.M) {
+      *reinterpret_cast<float4 *>(a.y + r * a.M + mb) = make_float4(v[0], v[1], v[2], v[3]);
+    } else {
+#pragma unroll
+      for (int i = 0; i < 4; i++)
+        if (mb + i < a.M) a.y[r * a.M + mb + i] = v[i];
+    }
+  }
+}
+
 // $SHLO_MUL_MAT_PATH = naive | fast forces one of the two exact paths (both give
 // the same bits; the tests run each); unset, the size decides.
 static int mm_path() {
@@ -730,9 +837,10 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
   }
   const int seg = (int)(np / 16);
   const int segp = (seg + 3) & ~3;
+  const bool short_k = segp == 4;  // every segment 4 packed k: k_mul_mat_short
   const int WM = M <= 64 ? 1 : 2;
-  const int BM = WM == 1 ? mt::Tile<1>::BM : mt::Tile<2>::BM;
-  const int BN = WM == 1 ? mt::Tile<1>::BN : mt::Tile<2>::BN;
+  const int BM = short_k ? ms::BM : WM == 1 ? mt::Tile<1>::BM : mt::Tile<2>::BM;
+  const int BN = short_k ? ms::BN : WM == 1 ? mt::Tile<1>::BN : mt::Tile<2>::BN;
   const int Mp = (int)((M + BM - 1) / BM * BM);
   const int64_t Bx = wbs ? nb : 1;
   const int64_t Nx = wbs ? N : R;
@@ -792,6 +900,19 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
   a.r_tiles = Np / BN;
   a.flavor = flavor;
   a.bx_count = (int)Bx;
+  if (short_k) {
+    const unsigned grid = (unsigned)((int64_t)(Mp / BM) * Bx * a.r_tiles);
+    k_mul_mat_short<<<grid, ms::THREADS, 0, dev->stream>>>(a);
+    int rc = launch_check("mul_mat");
+    buffer_release(wpk);
+    buffer_release(xpk);
+    if (rc) {
+      shlo_release(o);
+      return 1;
+    }
+    *out = o;
+    return 0;
+  }
   const size_t smem = WM == 1 ? mt::Pipe<1>::SMEM : mt::Pipe<2>::SMEM;
   static bool attr_done[64] = {false};
   if (!attr_done[dev->id]) {
