@@ -18,7 +18,7 @@ namespace {
 
 enum KernelKind {
   KK_MUL_MAT, KK_SOFT_MAX, KK_NORM, KK_SILU, KK_GELU_ERF, KK_ERFF_MAP, KK_DIVIDE, KK_SQRT, KK_F64_EW,
-  KK_F64_OF_F32, KK_F32_OF_F64
+  KK_F64_OF_F32, KK_F32_OF_F64, KK_MUL_MAT_EP, KK_NORM_AFFINE
 };
 
 struct KernelInfo {
@@ -42,6 +42,11 @@ const KernelInfo kKernels[] = {
     {"smlx_f64_ew", KK_F64_EW, 3, 2, 2, kU64},         // a, b, p = [count, op]
     {"smlx_f64_of_f32", KK_F64_OF_F32, 2, 1, 1, kU64}, // a, p = [count]
     {"smlx_f32_of_f64", KK_F32_OF_F64, 2, 1, 1, kF32}, // a, p = [count]
+    // This backend's fused forms, which its executor uses in place of a kernel
+    // followed by built-in adds and multiplies (the reference has none; every
+    // rounding of the unfused sequence is kept):
+    {"shlo_mul_mat_bias", KK_MUL_MAT_EP, 5, 4, 7, kF32},  // w, x, bias, residual, p = [mul_mat's six, flags]
+    {"shlo_norm_affine", KK_NORM_AFFINE, 4, 3, 4, kF32},  // x, gamma, beta, p = [norm's four]
 };
 
 }  // namespace
@@ -258,7 +263,7 @@ int shlo_kernel_apply(shlo_kernel k, const shlo_arr *inputs, int n_inputs, const
   Device *dev;
   SHLO_TRY(arr_device(inputs[0], &dev));
   // The kernels index flat row-major buffers (c/smlx_shim.c:292-293).
-  Arr *in[3] = {nullptr, nullptr, nullptr};
+  Arr *in[5] = {nullptr, nullptr, nullptr, nullptr, nullptr};
   int rc = 0;
   for (int i = 0; i < n_inputs && !rc; i++) {
     if (i == ki.param_index) continue;
@@ -288,6 +293,8 @@ int shlo_kernel_apply(shlo_kernel k, const shlo_arr *inputs, int n_inputs, const
       case KK_F64_EW: rc = k_f64_ew(dev, in[0], in[1], p, &o); break;
       case KK_F64_OF_F32: rc = k_f64_of_f32(dev, in[0], p, &o); break;
       case KK_F32_OF_F64: rc = k_f32_of_f64(dev, in[0], p, &o); break;
+      case KK_MUL_MAT_EP: rc = k_mul_mat_ep(dev, in[0], in[1], p, in[2], in[3], (int)p[6], &o); break;
+      case KK_NORM_AFFINE: rc = k_norm_affine(dev, in[0], p, in[1], in[2], &o); break;
     }
   }
   for (Arr *a : in)

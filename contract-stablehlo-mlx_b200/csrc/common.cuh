@@ -175,8 +175,13 @@ int device_wait(Device *dev, const char *what);
 
 // ---- ggml kernels (ggml_kernels.cu) ----
 int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out);
+// mul_mat with the executor's fused epilogue: + bias[m] and/or + res[r][m]
+// (ep: 1 bias, 2 bias is the add's left operand, 4 residual, 8 residual left).
+int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr *res, int ep, Arr **out);
 int k_soft_max(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out);
+// norm with the executor's fused affine: (y * gamma[c]) + beta[c].
+int k_norm_affine(Device *dev, Arr *x, const uint32_t *p, Arr *gamma, Arr *beta, Arr **out);
 int k_silu(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 int k_gelu_erf(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 int k_erff_map(Device *dev, const uint32_t *p, Arr **out);

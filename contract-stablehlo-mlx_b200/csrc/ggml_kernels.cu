@@ -257,7 +257,35 @@ struct MMArgs {
   int bx_count;     // x batches (1 when w is shared)
   int flavor;
   float *park;      // k_mul_mat_tm: 64 floats a thread a CTA, T(0..7) between the halves
+  // Fused epilogue (the executor's bias and residual adds, each its own
+  // binary32 rounding, in the module's operand order): EP_* flags.
+  const float *bias;  // [M]
+  const float *res;   // [R][M]
+  int ep;
 };
+
+enum { EP_BIAS = 1, EP_BIAS_LHS = 2, EP_RES = 4, EP_RES_LHS = 8 };
+
+// y (the dot product, NaN already canonical) + bias[m], then + res[r][m]: the
+// same __fadd_rn the built-in add runs, in the same operand order.
+__device__ __forceinline__ float epilogue_adds(const MMArgs &a, float v, int64_t r, int m) {
+  if (a.ep & EP_BIAS) {
+    const float b = __ldg(a.bias + m);
+    v = (a.ep & EP_BIAS_LHS) ? __fadd_rn(b, v) : __fadd_rn(v, b);
+  }
+  if (a.ep & EP_RES) {
+    const float h = __ldg(a.res + r * a.M + m);
+    v = (a.ep & EP_RES_LHS) ? __fadd_rn(h, v) : __fadd_rn(v, h);
+  }
+  return v;
+}
+
+// The same adds over a finished y of R x M (the paths without a fused epilogue).
+__global__ void k_mm_epilogue(MMArgs a, int64_t R) {
+  const int64_t n = R * a.M;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    a.y[i] = epilogue_adds(a, a.y[i], i / a.M, (int)(i % a.M));
+}
 
 __global__ void __launch_bounds__(mm::THREADS, 1) k_mul_mat_fast(MMArgs a) {
   using namespace mm;
@@ -665,7 +693,7 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
           const float *wr = a.w + (a.wbs ? (int64_t)bx * a.wbs : 0) + (int64_t)m * a.K;
           v[i] = dot_tail(wr, a.x + r * a.K, a.np, a.K, v[i], a.flavor);
         }
-        v[i] = arm_nan(v[i]);
+        v[i] = epilogue_adds(a, arm_nan(v[i]), r, m);
       }
       if (vec && mb + 3 < a.M) {
         *reinterpret_cast<float4 *>(a.y + r * a.M + mb) = make_float4(v[0], v[1], v[2], v[3]);
@@ -771,7 +799,7 @@ __global__ void __launch_bounds__(ms::THREADS, 2) k_mul_mat_short(MMArgs a) {
         const float *wr = a.w + (a.wbs ? (int64_t)bx * a.wbs : 0) + (int64_t)m * a.K;
         v[i] = dot_tail(wr, a.x + r * a.K, a.np, a.K, v[i], a.flavor);
       }
-      v[i] = arm_nan(v[i]);
+      v[i] = epilogue_adds(a, arm_nan(v[i]), r, m);
     }
     if (vec && mb + 3 < a.M) {
       *reinterpret_cast<float4 *>(a.y + r * a.M + mb) = make_float4(v[0], v[1], v[2], v[3]);
@@ -805,8 +833,20 @@ static int pack_operand(Device *dev, const float *src, int rows, int K, int64_t 
 }
 
 int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
+  return k_mul_mat_ep(dev, w, x, p, nullptr, nullptr, 0, out);
+}
+
+int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr *res, int ep, Arr **out) {
   const int64_t K = p[0], M = p[1], R = p[2], wbs = p[3], N = p[4];
   const int plain = p[5] != 0;
+  if ((ep & EP_BIAS) && (!bias || require_dtype(bias, kF32, "mul_mat bias") || check_elems(bias, M, "mul_mat bias")))
+    return 1;
+  if ((ep & EP_RES) && (!res || require_dtype(res, kF32, "mul_mat residual") || check_elems(res, R * M, "mul_mat residual")))
+    return 1;
+  MMArgs ea{};
+  ea.bias = (ep & EP_BIAS) ? (const float *)data_ptr(bias) : nullptr;
+  ea.res = (ep & EP_RES) ? (const float *)data_ptr(res) : nullptr;
+  ea.ep = ep;
   SHLO_TRY(require_dtype(w, kF32, "mul_mat") || require_dtype(x, kF32, "mul_mat"));
   if (K <= 0 || N <= 0 || R % N) return fail("mul_mat: K=%lld R=%lld N=%lld not carried", (long long)K, (long long)R, (long long)N);
   const int64_t nb = R / N;
@@ -828,7 +868,14 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
     k_mul_mat_naive<<<grid_for(R * M, 256, dev), 256, 0, dev->stream>>>(
         (const float *)data_ptr(w), (const float *)data_ptr(x), (float *)o->buf->ptr, (int)K, (int)M, R, N, wbs, plain,
         flavor);
-    if (launch_check("mul_mat")) {
+    int rc = launch_check("mul_mat");
+    if (!rc && ep) {
+      ea.y = (float *)o->buf->ptr;
+      ea.M = (int)M;
+      k_mm_epilogue<<<grid_for(R * M, 256, dev), 256, 0, dev->stream>>>(ea, R);
+      rc = launch_check("mul_mat epilogue");
+    }
+    if (rc) {
       shlo_release(o);
       return 1;
     }
@@ -883,7 +930,7 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
     shlo_release(o);
     return 1;
   }
-  MMArgs a;
+  MMArgs a = ea;
   a.wp = (const float *)wpk->ptr;
   a.xp = (const float *)xpk->ptr;
   a.w = (const float *)data_ptr(w);
@@ -1229,7 +1276,9 @@ __global__ void g_norm(const float *__restrict__ x, float *__restrict__ y, int n
 constexpr int NORM_ROWS = 16, NORM_THREADS = 128, NORM_UNROLL = 4;
 
 __global__ void __launch_bounds__(NORM_THREADS) g_norm_rows(const float *__restrict__ x, float *__restrict__ y,
-                                                            int ncols, int64_t rows, float eps) {
+                                                            int ncols, int64_t rows, float eps,
+                                                            const float *__restrict__ gamma,
+                                                            const float *__restrict__ beta) {
   extern __shared__ float tile[];  // [NORM_ROWS][ncols + 1]
   __shared__ float ms[NORM_ROWS], ss[NORM_ROWS];
   const int tid = threadIdx.x;
@@ -1303,20 +1352,44 @@ __global__ void __launch_bounds__(NORM_THREADS) g_norm_rows(const float *__restr
     o.y = arm_nan(__fmul_rn(__fsub_rn(s[1], m), k));
     o.z = arm_nan(__fmul_rn(__fsub_rn(s[2], m), k));
     o.w = arm_nan(__fmul_rn(__fsub_rn(s[3], m), k));
+    if (gamma) {  // the executor's fused affine: (y * gamma) + beta, each rounded alone
+      const float4 g = __ldg(reinterpret_cast<const float4 *>(gamma + c));
+      const float4 b = __ldg(reinterpret_cast<const float4 *>(beta + c));
+      o = make_float4(__fadd_rn(__fmul_rn(o.x, g.x), b.x), __fadd_rn(__fmul_rn(o.y, g.y), b.y),
+                      __fadd_rn(__fmul_rn(o.z, g.z), b.z), __fadd_rn(__fmul_rn(o.w, g.w), b.w));
+    }
     yb[v] = o;
   }
 }
 
-int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
+// (y * gamma[c]) + beta[c] in place, for the norm path without a fused affine.
+__global__ void k_affine_rows(float *y, int64_t n, int ncols, const float *gamma, const float *beta) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const int c = (int)(i % ncols);
+    y[i] = __fadd_rn(__fmul_rn(y[i], gamma[c]), beta[c]);
+  }
+}
+
+int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out) { return k_norm_affine(dev, x, p, nullptr, nullptr, out); }
+
+int k_norm_affine(Device *dev, Arr *x, const uint32_t *p, Arr *gamma, Arr *beta, Arr **out) {
   const int64_t ncols = p[0], rows = p[1];
   const float eps = bitsf_host(p[2]);
   SHLO_TRY(require_dtype(x, kF32, "norm"));
   SHLO_TRY(check_elems(x, ncols * rows, "norm"));
+  const bool affine = gamma != nullptr;
+  if (affine) {
+    SHLO_TRY(require_dtype(gamma, kF32, "norm gamma") || check_elems(gamma, ncols, "norm gamma"));
+    SHLO_TRY(require_dtype(beta, kF32, "norm beta") || check_elems(beta, ncols, "norm beta"));
+  }
+  const float *gp = affine ? (const float *)data_ptr(gamma) : nullptr;
+  const float *bp = affine ? (const float *)data_ptr(beta) : nullptr;
   int64_t shape[1] = {ncols * rows};
   Arr *o;
   SHLO_TRY(new_array(dev, kF32, shape, 1, &o));
   const size_t smem = (size_t)NORM_ROWS * (ncols + 1) * sizeof(float);
-  const bool aligned = (((uintptr_t)data_ptr(x)) & 15) == 0;
+  const bool aligned = (((uintptr_t)data_ptr(x)) & 15) == 0 &&
+                       (!affine || ((((uintptr_t)gp) | ((uintptr_t)bp)) & 15) == 0);
   if (ncols * rows > 0 && p[3] == 0 && ncols % 4 == 0 && ncols <= 1024 && aligned) {
     static bool attr_done[64] = {false};
     if (!attr_done[dev->id]) {
@@ -1328,7 +1401,7 @@ int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
       attr_done[dev->id] = true;
     }
     g_norm_rows<<<(unsigned)((rows + NORM_ROWS - 1) / NORM_ROWS), NORM_THREADS, smem, dev->stream>>>(
-        (const float *)data_ptr(x), (float *)o->buf->ptr, (int)ncols, rows, eps);
+        (const float *)data_ptr(x), (float *)o->buf->ptr, (int)ncols, rows, eps, gp, bp);
     if (launch_check("norm")) {
       shlo_release(o);
       return 1;
@@ -1339,7 +1412,13 @@ int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
     if (blocks > (int64_t)dev->sm_count * 8) blocks = (int64_t)dev->sm_count * 8;
     g_norm<<<(unsigned)blocks, 256, 0, dev->stream>>>((const float *)data_ptr(x), (float *)o->buf->ptr, (int)ncols,
                                                        rows, eps, p[3] != 0);
-    if (launch_check("norm")) {
+    int rc = launch_check("norm");
+    if (!rc && affine) {
+      k_affine_rows<<<grid_for(ncols * rows, 256, dev), 256, 0, dev->stream>>>((float *)o->buf->ptr, ncols * rows,
+                                                                            (int)ncols, gp, bp);
+      rc = launch_check("norm affine");
+    }
+    if (rc) {
       shlo_release(o);
       return 1;
     }

@@ -28,16 +28,30 @@ SPECS = {
     "f32_of_f64": (["a", "p"], ["y"]),
 }
 
+# This backend's fused forms (no counterpart in the reference): a kernel and
+# the built-in adds / multiplies that follow it in one launch, every rounding
+# of the unfused sequence kept. The executor uses them when nothing else reads
+# the intermediate values.
+FUSED = {
+    "mul_mat_bias": (["w", "x", "bias", "res", "p"], ["y"]),
+    "norm_affine": (["x", "gamma", "beta", "p"], ["y"]),
+}
+EP_BIAS, EP_BIAS_LHS, EP_RES, EP_RES_LHS = 1, 2, 4, 8
+
 _cache: dict = {}
 
 
 def kernel(name: str) -> M.Kernel:
     k = _cache.get(name)
     if k is None:
-        if name not in SPECS:
+        if name in SPECS:
+            ins, outs = SPECS[name]
+            k = M.kernel_new("smlx_" + name, ins, outs, "", "")
+        elif name in FUSED:
+            ins, outs = FUSED[name]
+            k = M.kernel_new("shlo_" + name, ins, outs, "", "")
+        else:
             raise M.ShloError("no generated kernel %s" % name)
-        ins, outs = SPECS[name]
-        k = M.kernel_new("smlx_" + name, ins, outs, "", "")
         _cache[name] = k
     return k
 
@@ -126,3 +140,16 @@ def f64_of_f32(a, count):
 
 def f32_of_f64(a, count):
     return run("f32_of_f64", [a, params([count])], [count], M.dtF32, count, 256)
+
+
+def mul_mat_bias(w, x, K, M_, R, N, w_batch_stride, bias, res=None, flags=EP_BIAS):
+    """mul_mat, then + bias[m] (and + res[r][m] when EP_RES is in flags), each
+    add rounded alone in the module's operand order (EP_*_LHS: the added
+    value is the add's left operand)."""
+    return run("mul_mat_bias", [w, x, bias, res if res is not None else bias,
+                                params([K, M_, R, w_batch_stride, N, 0, flags])], [R * M_], M.dtF32, R * M_, 64)
+
+
+def norm_affine(x, ncols, rows, eps_bits, gamma, beta):
+    """norm, then (y * gamma[c]) + beta[c], each rounded alone."""
+    return run("norm_affine", [x, gamma, beta, params([ncols, rows, eps_bits, 0])], [rows * ncols], M.dtF32, rows, 64)
