@@ -556,6 +556,47 @@ int shlo_dtype(shlo_arr a, uint8_t *dtype) {
   return 0;
 }
 
+// Strides that read a strided array in a new shape without a copy, when its
+// dimensions merge and split only across runs of dimensions that are laid out
+// row-contiguously among themselves (size-1 dimensions ignored); false when
+// the new shape needs a copy.
+static bool reshape_strides(const Arr *a, const int64_t *shape, int ndim, int64_t *st) {
+  int64_t od[kMaxRank], os[kMaxRank];
+  int on = 0;
+  for (int i = 0; i < a->ndim; i++)
+    if (a->shape[i] != 1) {
+      od[on] = a->shape[i];
+      os[on] = a->strides[i];
+      on++;
+    }
+  int oi = 0, ni = 0;
+  for (int i = 0; i < ndim; i++) st[i] = 1;
+  while (ni < ndim && oi < on) {
+    if (shape[ni] == 1) {
+      ni++;
+      continue;
+    }
+    int oj = oi + 1, nj = ni + 1;
+    int64_t np = shape[ni], op = od[oi];
+    while (np != op) {
+      if (np < op) {
+        if (nj >= ndim) return false;
+        np *= shape[nj++];
+      } else {
+        if (oj >= on) return false;
+        op *= od[oj++];
+      }
+    }
+    for (int k = oi; k < oj - 1; k++)
+      if (os[k] != od[k + 1] * os[k + 1]) return false;
+    st[nj - 1] = os[oj - 1];
+    for (int k = nj - 1; k > ni; k--) st[k - 1] = st[k] * shape[k];
+    ni = nj;
+    oi = oj;
+  }
+  return oi == on;
+}
+
 int shlo_reshape(shlo_arr a, const int64_t *shape, int ndim, shlo_arr *out) {
   if (!a) return fail("reshape: null array");
   if (ndim > kMaxRank) return fail("reshape: rank above %d", kMaxRank);
@@ -565,6 +606,18 @@ int shlo_reshape(shlo_arr a, const int64_t *shape, int ndim, shlo_arr *out) {
     n *= shape[i];
   }
   if (n != numel(a)) return fail("reshape: %lld elements into %lld", (long long)numel(a), (long long)n);
+  int64_t st[kMaxRank];
+  if (!is_row_contiguous(a) && n > 0 && reshape_strides(a, shape, ndim, st)) {
+    // The same storage read with new strides: no copy.
+    Arr *v = new_view(a);
+    v->ndim = ndim;
+    for (int i = 0; i < ndim; i++) {
+      v->shape[i] = shape[i];
+      v->strides[i] = st[i];
+    }
+    *out = v;
+    return 0;
+  }
   Arr *c;
   SHLO_TRY(make_contiguous(a, &c));
   Arr *v = new_view(c);
