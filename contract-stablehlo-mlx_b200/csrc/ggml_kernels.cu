@@ -262,6 +262,7 @@ struct MMArgs {
   const float *bias;  // [M]
   const float *res;   // [R][M]
   int ep;
+  int *ctr;           // k_mul_mat_tm in quarters: arrivals per tile (0 between launches)
 };
 
 enum { EP_BIAS = 1, EP_BIAS_LHS = 2, EP_RES = 4, EP_RES_LHS = 8 };
@@ -435,6 +436,9 @@ template <int WM>
 struct Pipe {
   static constexpr int NS = WM == 2 ? 3 : 2;  // stages of BK k
   static constexpr size_t SMEM = (size_t)NS * Tile<WM>::STAGE_FLOATS * 4 + (size_t)LEVEL_FLOATS * 4;
+  // A CTA that computes a quarter of the tree needs no level-2 slab: the same
+  // shared memory holds more stages.
+  static constexpr int NS_QUARTER = (int)(SMEM / (Tile<WM>::STAGE_FLOATS * 4));
 };
 // Dynamic shared memory above a third of an SM's: at most two CTAs per SM, so
 // their TMEM columns (2 x 256) always fit the SM's 512.
@@ -477,8 +481,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
 // float4: no bank conflicts). Level 3 is pushed only at S = 7 (depth 3) and
 // popped only at S = 15 (depth 4); the caller parks it in global memory, so
 // here depth 3 leaves the value in acc and depth 4 stops after level 2.
-__device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, float4 *lv2, int S) {
-  const int depth = __ffs(~S) - 1;  // trailing one bits: 0..4
+__device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, float4 *lv2, int S, bool last = false) {
+  const int depth = last ? 2 : __ffs(~S) - 1;  // trailing one bits: 0..4 (a quarter's last: pop 0 and 1)
   const int pops = depth < 3 ? depth : 3;
 #pragma unroll
   for (int c = 0; c < 4; c++) {
@@ -504,7 +508,7 @@ __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, floa
     }
     if (depth < 2) {
       tmem_st16(tcol + 64 * depth + 16 * c, v);
-    } else if (depth == 2) {
+    } else if (depth == 2 && !last) {
 #pragma unroll
       for (int j = 0; j < 4; j++) lv2[(c * 4 + j) * mt::THREADS] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     }
@@ -517,11 +521,17 @@ __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, floa
 // tile in L2).
 // STAGE_FOLD: every segment spans whole stages (segp a multiple of 16), so the
 // fold check runs once per stage; otherwise after every group of 4 k.
-template <int WM, bool STAGE_FOLD>
+// QUARTER: the grid has four CTAs a tile, CTA q computing the subtree
+// T(4q..4q+3) of segments 4q..4q+3 (a 2-level stack, all in TMEM); each writes
+// its partial to a per-tile slice of a.park, and the last of the four to
+// arrive (an atomic count, no waiting) adds ((T0 + T1) + (T2 + T3)) -- the top
+// two levels of ggml's tree -- and runs the epilogue. Four times the CTAs fill
+// the last wave of a grid that would leave SMs idle.
+template <int WM, bool STAGE_FOLD, bool QUARTER>
 __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMArgs a) {
   using namespace mt;
   constexpr int BM = Tile<WM>::BM, BN = Tile<WM>::BN, STAGE_FLOATS = Tile<WM>::STAGE_FLOATS;
-  constexpr int NS = Pipe<WM>::NS;
+  constexpr int NS = QUARTER ? Pipe<WM>::NS_QUARTER : Pipe<WM>::NS;
   extern __shared__ __align__(16) float smem[];
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -532,21 +542,23 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
   // This CTA's tile: m0, batch bx, first row rl0 (recomputed where needed, so
   // nothing but the operand pointers stays live through the k-loop).
   auto pos = [&](int &m0, int &bx, int64_t &rl0) {
-    const int mtiles = a.Mp / BM, tile = blockIdx.x;
+    const int mtiles = a.Mp / BM, tile = QUARTER ? blockIdx.x >> 2 : blockIdx.x;
     m0 = (tile % mtiles) * BM;
     bx = (tile / mtiles) / a.r_tiles;
     rl0 = (int64_t)((tile / mtiles) % a.r_tiles) * BN;
   };
   const int Kq = 16 * a.segp;
+  // A quarter reads packed k rows [4 q segp, 4 (q + 1) segp): its four segments.
+  const int kq0 = QUARTER ? (int)(blockIdx.x & 3) * 4 * a.segp : 0;
   const float *wp, *xp;
   {
     int m0, bx;
     int64_t rl0;
     pos(m0, bx, rl0);
-    wp = a.wp + (a.wbs ? (int64_t)bx * Kq * a.Mp : 0) + m0;
-    xp = a.xp + (int64_t)bx * Kq * a.Np + rl0;
+    wp = a.wp + (a.wbs ? (int64_t)bx * Kq * a.Mp : 0) + (int64_t)kq0 * a.Mp + m0;
+    xp = a.xp + (int64_t)bx * Kq * a.Np + (int64_t)kq0 * a.Np + rl0;
   }
-  const int nstages = Kq / BK;
+  const int nstages = (QUARTER ? Kq / 4 : Kq) / BK;
 
   if (warp == 0) {
     uint32_t slot = (uint32_t)__cvta_generic_to_shared(&tmem_base);
@@ -613,11 +625,11 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
   int S = 0, gleft = a.segp / 4;
   auto end_group = [&]() {
     if (--gleft == 0) {
-      tfold_rt(acc2, tcol, lv2, S);
+      tfold_rt(acc2, tcol, lv2, S, QUARTER && S == 3);
       gleft = a.segp / 4;
       // After S = 7 the fold left T(0..7) in acc (depth 3 pushes nothing).
-      if (S == 7) park(false);
-      if (++S < 16) {
+      if (!QUARTER && S == 7) park(false);
+      if (++S < (QUARTER ? 4 : 16)) {
 #pragma unroll
         for (int i = 0; i < 32; i++) acc2[i] = make_float2(0.0f, 0.0f);
       }
@@ -667,9 +679,40 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_base), "n"(TMEM_COLS));
 
-  // Epilogue: the root of the tree, T(0..7) + T(8..15); then the tail (K mod 16
-  // elements, in order) and the store.
-  park(true);
+  if (QUARTER) {
+    // This quarter's T(4q..4q+3) to its slice; the last of the tile's four adds
+    // the top of the tree.
+    __shared__ int last;
+    const int tile = blockIdx.x >> 2, q = blockIdx.x & 3;
+    float4 *mine = reinterpret_cast<float4 *>(a.park + (size_t)blockIdx.x * (THREADS * 64)) + tid;
+#pragma unroll
+    for (int i = 0; i < 16; i++) mine[i * THREADS] = make_float4(acc2[2 * i].x, acc2[2 * i].y, acc2[2 * i + 1].x, acc2[2 * i + 1].y);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(a.ctr + tile, 1) == 3;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (tid == 0) a.ctr[tile] = 0;  // ready for the next launch
+    const float4 *base = reinterpret_cast<const float4 *>(a.park + (size_t)tile * 4 * (THREADS * 64)) + tid;
+    (void)q;
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      // all four partials from L2 (this CTA's own too: it wrote them above)
+      const float4 p0 = __ldcg(base + i * THREADS), p1 = __ldcg(base + 16 * THREADS + i * THREADS);
+      const float4 p2 = __ldcg(base + 32 * THREADS + i * THREADS), p3 = __ldcg(base + 48 * THREADS + i * THREADS);
+      auto add4 = [](float4 u, float4 v) {
+        return make_float4(__fadd_rn(u.x, v.x), __fadd_rn(u.y, v.y), __fadd_rn(u.z, v.z), __fadd_rn(u.w, v.w));
+      };
+      const float4 r = add4(add4(p0, p1), add4(p2, p3));
+      acc2[2 * i] = make_float2(r.x, r.y);
+      acc2[2 * i + 1] = make_float2(r.z, r.w);
+    }
+  } else {
+    // The root of the tree: T(0..7) + T(8..15).
+    park(true);
+  }
+  // Epilogue: the tail (K mod 16 elements, in order) and the store.
   int m0, bx;
   int64_t rl0;
   pos(m0, bx, rl0);
@@ -963,14 +1006,20 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   const size_t smem = WM == 1 ? mt::Pipe<1>::SMEM : mt::Pipe<2>::SMEM;
   static bool attr_done[64] = {false};
   if (!attr_done[dev->id]) {
-    if (cuda_check(cudaFuncSetAttribute(k_mul_mat_tm<1, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)mt::Pipe<1>::SMEM), "mul_mat attribute") ||
-        cuda_check(cudaFuncSetAttribute(k_mul_mat_tm<1, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)mt::Pipe<1>::SMEM), "mul_mat attribute") ||
-        cuda_check(cudaFuncSetAttribute(k_mul_mat_tm<2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)mt::Pipe<2>::SMEM), "mul_mat attribute") ||
-        cuda_check(cudaFuncSetAttribute(k_mul_mat_tm<2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        (int)mt::Pipe<2>::SMEM), "mul_mat attribute")) {
+    int rc = 0;
+    auto attr = [&](auto kern, size_t bytes) {
+      if (!rc) rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes),
+                               "mul_mat attribute");
+    };
+    attr(k_mul_mat_tm<1, false, false>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<1, true, false>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<2, false, false>, mt::Pipe<2>::SMEM);
+    attr(k_mul_mat_tm<2, true, false>, mt::Pipe<2>::SMEM);
+    attr(k_mul_mat_tm<1, false, true>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<1, true, true>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<2, false, true>, mt::Pipe<2>::SMEM);
+    attr(k_mul_mat_tm<2, true, true>, mt::Pipe<2>::SMEM);
+    if (rc) {
       buffer_release(wpk);
       buffer_release(xpk);
       shlo_release(o);
@@ -978,26 +1027,40 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
     }
     attr_done[dev->id] = true;
   }
-  const unsigned grid = (unsigned)((int64_t)(Mp / BM) * Bx * a.r_tiles);
-  Buffer *park;
-  if (buffer_alloc(dev, (size_t)grid * mt::THREADS * 64 * sizeof(float), &park)) {
+  // Quarters when they fill the last wave of two-CTA-per-SM slots markedly
+  // better ($SHLO_MM_SPLIT = 1 | 4 forces one form; both give the same bits).
+  const int64_t tiles = (int64_t)(Mp / BM) * Bx * a.r_tiles;
+  const int64_t slots = (int64_t)mt::CTAS_PER_SM * dev->sm_count;
+  auto wave_fill = [&](int64_t t) { return (double)t / (double)(((t + slots - 1) / slots) * slots); };
+  bool quarter = wave_fill(4 * tiles) > wave_fill(tiles) + 0.04;
+  if (const char *e = getenv("SHLO_MM_SPLIT")) quarter = atoi(e) == 4;
+  const unsigned grid = (unsigned)(quarter ? 4 * tiles : tiles);
+  Buffer *park, *ctr = nullptr;
+  if (buffer_alloc(dev, (size_t)grid * mt::THREADS * 64 * sizeof(float), &park) ||
+      (quarter && buffer_alloc(dev, (size_t)tiles * sizeof(int), &ctr)) ||
+      (quarter && cuda_check(cudaMemsetAsync(ctr->ptr, 0, (size_t)tiles * sizeof(int), dev->stream), "mul_mat counters"))) {
+    buffer_release(park);
+    buffer_release(ctr);
     buffer_release(wpk);
     buffer_release(xpk);
     shlo_release(o);
     return 1;
   }
   a.park = (float *)park->ptr;
+  a.ctr = quarter ? (int *)ctr->ptr : nullptr;
   const bool stage_fold = segp % 16 == 0;
-  if (WM == 1 && stage_fold)
-    k_mul_mat_tm<1, true><<<grid, mt::THREADS, smem, dev->stream>>>(a);
-  else if (WM == 1)
-    k_mul_mat_tm<1, false><<<grid, mt::THREADS, smem, dev->stream>>>(a);
-  else if (stage_fold)
-    k_mul_mat_tm<2, true><<<grid, mt::THREADS, smem, dev->stream>>>(a);
-  else
-    k_mul_mat_tm<2, false><<<grid, mt::THREADS, smem, dev->stream>>>(a);
+#define SHLO_TM(WMv, SF, Q) k_mul_mat_tm<WMv, SF, Q><<<grid, mt::THREADS, smem, dev->stream>>>(a)
+  if (WM == 1) {
+    if (stage_fold) quarter ? SHLO_TM(1, true, true) : SHLO_TM(1, true, false);
+    else quarter ? SHLO_TM(1, false, true) : SHLO_TM(1, false, false);
+  } else {
+    if (stage_fold) quarter ? SHLO_TM(2, true, true) : SHLO_TM(2, true, false);
+    else quarter ? SHLO_TM(2, false, true) : SHLO_TM(2, false, false);
+  }
+#undef SHLO_TM
   int rc = launch_check("mul_mat");
   buffer_release(park);
+  buffer_release(ctr);
   buffer_release(wpk);
   buffer_release(xpk);
   if (rc) {
