@@ -281,6 +281,24 @@ __device__ __forceinline__ float epilogue_adds(const MMArgs &a, float v, int64_t
   return v;
 }
 
+// The epilogue operands of four outputs (r, mb..mb+3): 16-byte loads when M is
+// a multiple of 4 and the four are in range, element loads otherwise.
+__device__ __forceinline__ float4 ep_load4(const float *base, int64_t row, int mb, int M, bool vec) {
+  const float *q = base + row * M + mb;
+  if (vec && mb + 3 < M) return __ldg(reinterpret_cast<const float4 *>(q));
+  float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  if (mb < M) v.x = __ldg(q);
+  if (mb + 1 < M) v.y = __ldg(q + 1);
+  if (mb + 2 < M) v.z = __ldg(q + 2);
+  if (mb + 3 < M) v.w = __ldg(q + 3);
+  return v;
+}
+__device__ __forceinline__ float ep_add(int ep, float v, float b, float h) {
+  if (ep & EP_BIAS) v = (ep & EP_BIAS_LHS) ? __fadd_rn(b, v) : __fadd_rn(v, b);
+  if (ep & EP_RES) v = (ep & EP_RES_LHS) ? __fadd_rn(h, v) : __fadd_rn(v, h);
+  return v;
+}
+
 // The same adds over a finished y of R x M (the paths without a fused epilogue).
 __global__ void k_mm_epilogue(MMArgs a, int64_t R) {
   const int64_t n = R * a.M;
@@ -527,7 +545,9 @@ __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, floa
 // arrive (an atomic count, no waiting) adds ((T0 + T1) + (T2 + T3)) -- the top
 // two levels of ggml's tree -- and runs the epilogue. Four times the CTAs fill
 // the last wave of a grid that would leave SMs idle.
-template <int WM, bool STAGE_FOLD, bool QUARTER>
+// EPI: the fused bias / residual adds in the epilogue (a separate instance, so
+// the plain product compiles without them).
+template <int WM, bool STAGE_FOLD, bool QUARTER, bool EPI>
 __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMArgs a) {
   using namespace mt;
   constexpr int BM = Tile<WM>::BM, BN = Tile<WM>::BN, STAGE_FLOATS = Tile<WM>::STAGE_FLOATS;
@@ -718,6 +738,48 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
   pos(m0, bx, rl0);
   const int64_t rbase = (int64_t)bx * a.Nx;
   const bool vec = (a.M & 3) == 0;
+  if constexpr (EPI) {
+    // Per half h: the bias and all eight rows' residuals loaded first (one
+    // round trip), then the adds and the stores.
+#pragma unroll
+    for (int h = 0; h < 2; h++) {
+      const int mb = m0 + mo + 32 * h;
+      const float4 bv = (a.ep & EP_BIAS) ? ep_load4(a.bias, 0, mb, a.M, vec) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      float4 rv[8];
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int64_t rl = rl0 + ro + (j & 3) + (j >> 2) * 16;
+        rv[j] = (a.ep & EP_RES) && rl < a.Nx ? ep_load4(a.res, rbase + rl, mb, a.M, vec) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int64_t rl = rl0 + ro + (j & 3) + (j >> 2) * 16;
+        if (rl >= a.Nx) continue;
+        const int64_t r = rbase + rl;
+        const float bs[4] = {bv.x, bv.y, bv.z, bv.w}, hs[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float2 pr = acc2[j * 4 + 2 * h + (i >> 1)];
+          v[i] = (i & 1) ? pr.y : pr.x;
+          const int m = mb + i;
+          if (a.np < a.K && m < a.M) {
+            const float *wr = a.w + (a.wbs ? (int64_t)bx * a.wbs : 0) + (int64_t)m * a.K;
+            v[i] = dot_tail(wr, a.x + r * a.K, a.np, a.K, v[i], a.flavor);
+          }
+          v[i] = ep_add(a.ep, arm_nan(v[i]), bs[i], hs[i]);
+        }
+        if (vec && mb + 3 < a.M) {
+          *reinterpret_cast<float4 *>(a.y + r * a.M + mb) = make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 4; i++)
+            if (mb + i < a.M) a.y[r * a.M + mb + i] = v[i];
+        }
+      }
+    }
+    return;
+  }
 #pragma unroll
   for (int j = 0; j < 8; j++) {
     const int64_t rl = rl0 + ro + (j & 3) + (j >> 2) * 16;
@@ -736,7 +798,7 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
           const float *wr = a.w + (a.wbs ? (int64_t)bx * a.wbs : 0) + (int64_t)m * a.K;
           v[i] = dot_tail(wr, a.x + r * a.K, a.np, a.K, v[i], a.flavor);
         }
-        v[i] = epilogue_adds(a, arm_nan(v[i]), r, m);
+        v[i] = arm_nan(v[i]);
       }
       if (vec && mb + 3 < a.M) {
         *reinterpret_cast<float4 *>(a.y + r * a.M + mb) = make_float4(v[0], v[1], v[2], v[3]);
@@ -798,6 +860,7 @@ __device__ __forceinline__ void all_segs(const float *ws, const float *xs, float
   (seg_regs<S>(ws, xs, acc, st), ...);
 }
 
+template <bool EPI>
 __global__ void __launch_bounds__(ms::THREADS, 2) k_mul_mat_short(MMArgs a) {
   using namespace ms;
   __shared__ __align__(16) float ws[KQ * BM];
@@ -829,6 +892,14 @@ __global__ void __launch_bounds__(ms::THREADS, 2) k_mul_mat_short(MMArgs a) {
   const int64_t rbase = (int64_t)bx * a.Nx;
   const bool vec = (a.M & 3) == 0;
   const int mb = m0 + mo;
+  float4 bv = make_float4(0.0f, 0.0f, 0.0f, 0.0f), rv[4];
+  if (EPI) {  // the fused adds' operands, loaded before any is used
+    if (a.ep & EP_BIAS) bv = ep_load4(a.bias, 0, mb, a.M, vec);
+#pragma unroll
+    for (int j = 0; j < 4; j++)
+      rv[j] = (a.ep & EP_RES) && rl0 + ro + j < a.Nx ? ep_load4(a.res, rbase + rl0 + ro + j, mb, a.M, vec)
+                                                      : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
 #pragma unroll
   for (int j = 0; j < 4; j++) {
     const int64_t rl = rl0 + ro + j;
@@ -842,7 +913,11 @@ __global__ void __launch_bounds__(ms::THREADS, 2) k_mul_mat_short(MMArgs a) {
         const float *wr = a.w + (a.wbs ? (int64_t)bx * a.wbs : 0) + (int64_t)m * a.K;
         v[i] = dot_tail(wr, a.x + r * a.K, a.np, a.K, v[i], a.flavor);
       }
-      v[i] = epilogue_adds(a, arm_nan(v[i]), r, m);
+      v[i] = arm_nan(v[i]);
+      if (EPI) {
+        const float bs[4] = {bv.x, bv.y, bv.z, bv.w}, hs[4] = {rv[j].x, rv[j].y, rv[j].z, rv[j].w};
+        v[i] = ep_add(a.ep, v[i], bs[i], hs[i]);
+      }
     }
     if (vec && mb + 3 < a.M) {
       *reinterpret_cast<float4 *>(a.y + r * a.M + mb) = make_float4(v[0], v[1], v[2], v[3]);
@@ -992,7 +1067,10 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   a.bx_count = (int)Bx;
   if (short_k) {
     const unsigned grid = (unsigned)((int64_t)(Mp / BM) * Bx * a.r_tiles);
-    k_mul_mat_short<<<grid, ms::THREADS, 0, dev->stream>>>(a);
+    if (ep)
+      k_mul_mat_short<true><<<grid, ms::THREADS, 0, dev->stream>>>(a);
+    else
+      k_mul_mat_short<false><<<grid, ms::THREADS, 0, dev->stream>>>(a);
     int rc = launch_check("mul_mat");
     buffer_release(wpk);
     buffer_release(xpk);
@@ -1011,14 +1089,22 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
       if (!rc) rc = cuda_check(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes),
                                "mul_mat attribute");
     };
-    attr(k_mul_mat_tm<1, false, false>, mt::Pipe<1>::SMEM);
-    attr(k_mul_mat_tm<1, true, false>, mt::Pipe<1>::SMEM);
-    attr(k_mul_mat_tm<2, false, false>, mt::Pipe<2>::SMEM);
-    attr(k_mul_mat_tm<2, true, false>, mt::Pipe<2>::SMEM);
-    attr(k_mul_mat_tm<1, false, true>, mt::Pipe<1>::SMEM);
-    attr(k_mul_mat_tm<1, true, true>, mt::Pipe<1>::SMEM);
-    attr(k_mul_mat_tm<2, false, true>, mt::Pipe<2>::SMEM);
-    attr(k_mul_mat_tm<2, true, true>, mt::Pipe<2>::SMEM);
+    attr(k_mul_mat_tm<1, false, false, false>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<1, true, false, false>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<2, false, false, false>, mt::Pipe<2>::SMEM);
+    attr(k_mul_mat_tm<2, true, false, false>, mt::Pipe<2>::SMEM);
+    attr(k_mul_mat_tm<1, false, true, false>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<1, true, true, false>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<2, false, true, false>, mt::Pipe<2>::SMEM);
+    attr(k_mul_mat_tm<2, true, true, false>, mt::Pipe<2>::SMEM);
+    attr(k_mul_mat_tm<1, false, false, true>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<1, true, false, true>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<2, false, false, true>, mt::Pipe<2>::SMEM);
+    attr(k_mul_mat_tm<2, true, false, true>, mt::Pipe<2>::SMEM);
+    attr(k_mul_mat_tm<1, false, true, true>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<1, true, true, true>, mt::Pipe<1>::SMEM);
+    attr(k_mul_mat_tm<2, false, true, true>, mt::Pipe<2>::SMEM);
+    attr(k_mul_mat_tm<2, true, true, true>, mt::Pipe<2>::SMEM);
     if (rc) {
       buffer_release(wpk);
       buffer_release(xpk);
@@ -1032,7 +1118,9 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   const int64_t tiles = (int64_t)(Mp / BM) * Bx * a.r_tiles;
   const int64_t slots = (int64_t)mt::CTAS_PER_SM * dev->sm_count;
   auto wave_fill = [&](int64_t t) { return (double)t / (double)(((t + slots - 1) / slots) * slots); };
-  bool quarter = wave_fill(4 * tiles) > wave_fill(tiles) + 0.04;
+  // (A quarter must be long enough to pay for its own pipeline fill and the
+  // partials: segp >= 64, i.e. K >= 1024, sixteen stages a quarter.)
+  bool quarter = segp >= 64 && wave_fill(4 * tiles) > wave_fill(tiles) + 0.04;
   if (const char *e = getenv("SHLO_MM_SPLIT")) quarter = atoi(e) == 4;
   const unsigned grid = (unsigned)(quarter ? 4 * tiles : tiles);
   Buffer *park, *ctr = nullptr;
@@ -1049,7 +1137,9 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   a.park = (float *)park->ptr;
   a.ctr = quarter ? (int *)ctr->ptr : nullptr;
   const bool stage_fold = segp % 16 == 0;
-#define SHLO_TM(WMv, SF, Q) k_mul_mat_tm<WMv, SF, Q><<<grid, mt::THREADS, smem, dev->stream>>>(a)
+#define SHLO_TM(WMv, SF, Q)                                                      \
+  (ep ? k_mul_mat_tm<WMv, SF, Q, true><<<grid, mt::THREADS, smem, dev->stream>>>(a) \
+      : k_mul_mat_tm<WMv, SF, Q, false><<<grid, mt::THREADS, smem, dev->stream>>>(a))
   if (WM == 1) {
     if (stage_fold) quarter ? SHLO_TM(1, true, true) : SHLO_TM(1, true, false);
     else quarter ? SHLO_TM(1, false, true) : SHLO_TM(1, false, false);
