@@ -818,7 +818,7 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
 // 4-level stack lives in registers: no TMEM, and no fold waits. A thread's m
 // are mo + [0,4), its r are ro + [0,4) (warps 2 (m) x 4 (r), lanes 8 x 4).
 namespace ms {
-constexpr int BM = 64, BN = 64, KQ = 64, THREADS = 256;
+constexpr int BM = 64, BN = 64, THREADS = 256;
 }
 
 template <int S>
@@ -834,14 +834,15 @@ __device__ __forceinline__ void fold_regs(float2 (&acc)[8], float2 (&st)[4][8]) 
   }
 }
 
-template <int S>
+template <int S, int NG>
 __device__ __forceinline__ void seg_regs(const float *ws, const float *xs, float2 (&acc)[8], float2 (&st)[4][8]) {
+  // ws, xs: this segment's 4 NG packed k rows (BM resp. BN wide)
 #pragma unroll
   for (int i = 0; i < 8; i++) acc[i] = make_float2(0.0f, 0.0f);
 #pragma unroll
-  for (int kk = 0; kk < 4; kk++) {
-    const float4 w4 = *reinterpret_cast<const float4 *>(ws + (4 * S + kk) * ms::BM);
-    const float4 x4 = *reinterpret_cast<const float4 *>(xs + (4 * S + kk) * ms::BN);
+  for (int kk = 0; kk < 4 * NG; kk++) {
+    const float4 w4 = *reinterpret_cast<const float4 *>(ws + kk * ms::BM);
+    const float4 x4 = *reinterpret_cast<const float4 *>(xs + kk * ms::BN);
     const float2 w01 = make_float2(w4.x, w4.y), w23 = make_float2(w4.z, w4.w);
     const float xr[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
@@ -854,17 +855,40 @@ __device__ __forceinline__ void seg_regs(const float *ws, const float *xs, float
   fold_regs<S>(acc, st);
 }
 
-template <int... S>
-__device__ __forceinline__ void all_segs(const float *ws, const float *xs, float2 (&acc)[8], float2 (&st)[4][8],
+// NG groups of 4 k a segment. NG = 1: the whole packed K (64 rows) is loaded
+// once; NG > 1: a ring of MS_NS one-segment stages.
+constexpr int MS_NS = 4;
+template <int NG>
+struct ShortSmem {
+  static constexpr int SEG = 4 * NG * (ms::BM + ms::BN);  // floats of one segment's stage
+  static constexpr int FLOATS = NG == 1 ? 16 * SEG : MS_NS * SEG;
+};
+
+template <int NG, typename Issue, int... S>
+__device__ __forceinline__ void all_segs(float *sm, int mo, int ro, float2 (&acc)[8], float2 (&st)[4][8], Issue issue,
                                          std::integer_sequence<int, S...>) {
-  (seg_regs<S>(ws, xs, acc, st), ...);
+  constexpr int SEG = ShortSmem<NG>::SEG;
+  if constexpr (NG == 1) {
+    (seg_regs<S, 1>(sm + S * SEG + mo, sm + S * SEG + 4 * ms::BM + ro, acc, st), ...);
+  } else {
+    auto one = [&](auto sc) {
+      constexpr int s = decltype(sc)::value;
+      cp_async_wait<MS_NS - 2>();
+      __syncthreads();
+      if (s + MS_NS - 1 < 16) issue(s + MS_NS - 1);
+      cp_async_commit();
+      float *b = sm + (s % MS_NS) * SEG;
+      seg_regs<s, NG>(b + mo, b + 4 * NG * ms::BM + ro, acc, st);
+    };
+    (one(std::integral_constant<int, S>{}), ...);
+  }
 }
 
-template <bool EPI>
+template <bool EPI, int NG>
 __global__ void __launch_bounds__(ms::THREADS, 2) k_mul_mat_short(MMArgs a) {
   using namespace ms;
-  __shared__ __align__(16) float ws[KQ * BM];
-  __shared__ __align__(16) float xs[KQ * BN];
+  constexpr int SEG = ShortSmem<NG>::SEG, KS = 4 * NG;  // packed k rows a segment
+  __shared__ __align__(16) float sm[ShortSmem<NG>::FLOATS];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int mo = (warp & 1) * 32 + (lane & 7) * 4;
   const int ro = (warp >> 1) * 16 + (lane >> 3) * 4;
@@ -873,20 +897,37 @@ __global__ void __launch_bounds__(ms::THREADS, 2) k_mul_mat_short(MMArgs a) {
   const int rb = blockIdx.x / mtiles;
   const int bx = rb / a.r_tiles;
   const int64_t rl0 = (int64_t)(rb % a.r_tiles) * BN;
-  const float *wp = a.wp + (a.wbs ? (int64_t)bx * KQ * a.Mp : 0) + m0;
-  const float *xp = a.xp + (int64_t)bx * KQ * a.Np + rl0;
+  const int64_t Kq = 16 * KS;
+  const float *wp = a.wp + (a.wbs ? (int64_t)bx * Kq * a.Mp : 0) + m0;
+  const float *xp = a.xp + (int64_t)bx * Kq * a.Np + rl0;
+  // segment s's packed rows [s KS, (s + 1) KS) of w and x into buffer b
+  auto copy_seg = [&](int s, float *b) {
 #pragma unroll
-  for (int i = 0; i < KQ * BM / 4 / THREADS; i++) {
-    const int q = tid + i * THREADS, row = q / (BM / 4), col = (q % (BM / 4)) * 4;
-    cp_async16(ws + row * BM + col, wp + (int64_t)row * a.Mp + col);
-    cp_async16(xs + row * BN + col, xp + (int64_t)row * a.Np + col);
+    for (int i = 0; i < (KS * BM / 4 + THREADS - 1) / THREADS; i++) {
+      const int q = tid + i * THREADS;
+      if (q < KS * BM / 4) {
+        const int row = q / (BM / 4), col = (q % (BM / 4)) * 4;
+        cp_async16(b + row * BM + col, wp + (int64_t)(s * KS + row) * a.Mp + col);
+        cp_async16(b + KS * BM + row * BN + col, xp + (int64_t)(s * KS + row) * a.Np + col);
+      }
+    }
+  };
+  if constexpr (NG == 1) {
+    for (int s = 0; s < 16; s++) copy_seg(s, sm + s * SEG);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+  } else {
+#pragma unroll
+    for (int s = 0; s < MS_NS - 1; s++) {
+      copy_seg(s, sm + s * SEG);
+      cp_async_commit();
+    }
   }
-  cp_async_commit();
-  cp_async_wait<0>();
-  __syncthreads();
+  auto issue = [&](int s) { copy_seg(s, sm + (s % MS_NS) * SEG); };
 
   float2 acc[8], st[4][8];
-  all_segs(ws + mo, xs + ro, acc, st, std::make_integer_sequence<int, 16>{});
+  all_segs<NG>(sm, mo, ro, acc, st, issue, std::make_integer_sequence<int, 16>{});
 
   // Epilogue: the tail (K mod 16 elements, in order) and the store.
   const int64_t rbase = (int64_t)bx * a.Nx;
@@ -1002,7 +1043,9 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   }
   const int seg = (int)(np / 16);
   const int segp = (seg + 3) & ~3;
-  const bool short_k = segp == 4;  // every segment 4 packed k: k_mul_mat_short
+  // k_mul_mat_short (register stack, 64 x 64 tiles): every segment 4 packed k,
+  // or up to 16 when M <= 64 (attention's value product).
+  const bool short_k = segp == 4 || (M <= 64 && segp <= 16);
   const int WM = M <= 64 ? 1 : 2;
   const int BM = short_k ? ms::BM : WM == 1 ? mt::Tile<1>::BM : mt::Tile<2>::BM;
   const int BN = short_k ? ms::BN : WM == 1 ? mt::Tile<1>::BN : mt::Tile<2>::BN;
@@ -1067,10 +1110,16 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   a.bx_count = (int)Bx;
   if (short_k) {
     const unsigned grid = (unsigned)((int64_t)(Mp / BM) * Bx * a.r_tiles);
-    if (ep)
-      k_mul_mat_short<true><<<grid, ms::THREADS, 0, dev->stream>>>(a);
-    else
-      k_mul_mat_short<false><<<grid, ms::THREADS, 0, dev->stream>>>(a);
+#define SHLO_MS(NG)                                                                  \
+  (ep ? k_mul_mat_short<true, NG><<<grid, ms::THREADS, 0, dev->stream>>>(a)          \
+      : k_mul_mat_short<false, NG><<<grid, ms::THREADS, 0, dev->stream>>>(a))
+    switch (segp / 4) {
+      case 1: SHLO_MS(1); break;
+      case 2: SHLO_MS(2); break;
+      case 3: SHLO_MS(3); break;
+      default: SHLO_MS(4); break;
+    }
+#undef SHLO_MS
     int rc = launch_check("mul_mat");
     buffer_release(wpk);
     buffer_release(xpk);
