@@ -39,10 +39,10 @@ MM_SHAPES = [  # K, M, R, N, batched
 
 
 @pytest.mark.parametrize("flavor", ["pinned", "stock"])
-@pytest.mark.parametrize("path", ["fast", "naive", "fast-split1", "fast-split4"])
+@pytest.mark.parametrize("path", ["fast", "naive", "fast-split1", "fast-split2", "fast-split4"])
 @pytest.mark.parametrize("K,Mm,R,N,batched", MM_SHAPES)
 def test_mul_mat_random(K, Mm, R, N, batched, path, flavor, monkeypatch):
-    # the fast path in one CTA a tile, or in four (quarters of the fold tree)
+    # the fast path in one CTA a tile, or in two or four (halves, quarters of the fold tree)
     monkeypatch.setenv("SHLO_MUL_MAT_PATH", path.split("-")[0])
     if "-split" in path:
         monkeypatch.setenv("SHLO_MM_SPLIT", path.split("split")[1])
