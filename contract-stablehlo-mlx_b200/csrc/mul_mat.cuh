@@ -198,6 +198,8 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
 // float4: no bank conflicts). Level 3 is pushed only at S = 7 (depth 3) and
 // popped only at S = 15 (depth 4); the caller parks it in global memory, so
 // here depth 3 leaves the value in acc and depth 4 stops after level 2.
+// PAIR: the adds as paired FP32 adds (fewer issue slots, more register pressure).
+template <bool PAIR>
 __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, float4 *lv2, int S, bool last = false) {
   const int depth = last ? 2 : __ffs(~S) - 1;  // trailing one bits: 0..4 (a quarter's last: pop 0 and 1)
   const int pops = depth < 3 ? depth : 3;
@@ -220,8 +222,17 @@ __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, floa
           t[4 * j] = u.x; t[4 * j + 1] = u.y; t[4 * j + 2] = u.z; t[4 * j + 3] = u.w;
         }
       }
+      if (PAIR) {
 #pragma unroll
-      for (int i = 0; i < 16; i++) v[i] = __fadd_rn(t[i], v[i]);
+        for (int i = 0; i < 8; i++) {  // each component rounds as __fadd_rn
+          const float2 r = __fadd2_rn(make_float2(t[2 * i], t[2 * i + 1]), make_float2(v[2 * i], v[2 * i + 1]));
+          v[2 * i] = r.x;
+          v[2 * i + 1] = r.y;
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < 16; i++) v[i] = __fadd_rn(t[i], v[i]);
+      }
     }
     if (depth < 2) {
       tmem_st16(tcol + 64 * depth + 16 * c, v);
@@ -333,8 +344,8 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
       float2 &p0 = acc2[2 * i], &p1 = acc2[2 * i + 1];
       if (load) {
         const float4 l3 = q[i * THREADS];
-        p0 = make_float2(__fadd_rn(l3.x, p0.x), __fadd_rn(l3.y, p0.y));
-        p1 = make_float2(__fadd_rn(l3.z, p1.x), __fadd_rn(l3.w, p1.y));
+        p0 = __fadd2_rn(make_float2(l3.x, l3.y), p0);
+        p1 = __fadd2_rn(make_float2(l3.z, l3.w), p1);
       } else {
         q[i * THREADS] = make_float4(p0.x, p0.y, p1.x, p1.y);
       }
@@ -346,20 +357,19 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
   // depth: the number of trailing one bits of S).
   float4 *lv2 = reinterpret_cast<float4 *>(smem + NS * STAGE_FLOATS) + tid;
   int S = 0, gleft = a.segp / 4;
-  auto end_group = [&]() {
-    if (--gleft == 0) {
-      tfold_rt(acc2, tcol, lv2, S, QUARTER && S == 3);
-      gleft = a.segp / 4;
-      // After S = 7 the fold left T(0..7) in acc (depth 3 pushes nothing).
-      if (SPLIT == 1 && S == 7) park(false);
-      if (++S < SEGS) {
+  auto fold_segment = [&]() {
+    tfold_rt<STAGE_FOLD>(acc2, tcol, lv2, S, QUARTER && S == 3);
+    // After S = 7 the fold left T(0..7) in acc (depth 3 pushes nothing).
+    if (SPLIT == 1 && S == 7) park(false);
+    if (++S < SEGS) {
 #pragma unroll
-        for (int i = 0; i < 32; i++) acc2[i] = make_float2(0.0f, 0.0f);
-      }
+      for (int i = 0; i < 32; i++) acc2[i] = make_float2(0.0f, 0.0f);
     }
   };
   int so = 0;  // offset of stage st % NS
-  for (int st = 0; st < nstages; st++) {
+  // One stage: wait for its copies, start the copies NS - 1 stages ahead, and
+  // run its 16 k (after each group of 4 k, group_end()).
+  auto stage = [&](int st, auto group_end) {
     cp_async_wait<NS - 2>();
     __syncthreads();
     if (st + NS - 1 < nstages) issue(st + NS - 1);
@@ -385,13 +395,25 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
           for (int i = 0; i < 4; i++) acc2[j * 4 + i] = __ffma2_rn(wp2[i], xj, acc2[j * 4 + i]);
         }
       }
-      if (!STAGE_FOLD) end_group();
-    }
-    if (STAGE_FOLD) {
-      gleft -= GPS - 1;
-      end_group();
+      group_end();
     }
     so = so + STAGE_FLOATS == NS * STAGE_FLOATS ? 0 : so + STAGE_FLOATS;
+  };
+  if constexpr (STAGE_FOLD) {
+    // Segments of whole stages: the fold between the segments' stage loops.
+    const int sps = a.segp / BK;
+    for (int st = 0; S < SEGS;) {
+      for (int e = st + sps; st < e; st++) stage(st, [] {});
+      fold_segment();
+    }
+  } else {
+    for (int st = 0; st < nstages; st++)
+      stage(st, [&] {
+        if (--gleft == 0) {
+          gleft = a.segp / 4;
+          fold_segment();
+        }
+      });
   }
   cp_async_wait<0>();
 
@@ -419,7 +441,9 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
     if (tid == 0) a.ctr[tile] = 0;  // ready for the next launch
     const float4 *base = reinterpret_cast<const float4 *>(a.park + (size_t)tile * SPLIT * (THREADS * 64)) + tid;
     auto add4 = [](float4 u, float4 v) {
-      return make_float4(__fadd_rn(u.x, v.x), __fadd_rn(u.y, v.y), __fadd_rn(u.z, v.z), __fadd_rn(u.w, v.w));
+      const float2 lo = __fadd2_rn(make_float2(u.x, u.y), make_float2(v.x, v.y));
+      const float2 hi = __fadd2_rn(make_float2(u.z, u.w), make_float2(v.z, v.w));
+      return make_float4(lo.x, lo.y, hi.x, hi.y);
     };
 #pragma unroll
     for (int i = 0; i < 16; i++) {
@@ -534,7 +558,7 @@ __device__ __forceinline__ void fold_regs(float2 (&acc)[8], float2 (&st)[4][8]) 
 #pragma unroll
   for (int L = 0; L < depth; L++)
 #pragma unroll
-    for (int i = 0; i < 8; i++) acc[i] = make_float2(__fadd_rn(st[L][i].x, acc[i].x), __fadd_rn(st[L][i].y, acc[i].y));
+    for (int i = 0; i < 8; i++) acc[i] = __fadd2_rn(st[L][i], acc[i]);
   if (depth < 4) {
 #pragma unroll
     for (int i = 0; i < 8; i++) st[depth][i] = acc[i];
