@@ -52,7 +52,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     # Short runs to wrap in a profiler (no JSON line): one warm denoiser step,
     # mul_mat alone at --mm-shape K,M,R[,N], or every exact kernel once (batch 16).
-    ap.add_argument("--profile-run", choices=["step", "mul_mat", "kernels"])
+    ap.add_argument("--profile-run", choices=["step", "mul_mat", "kernels", "attention"])
     ap.add_argument("--mm-shape", default="512,1536,16384")
     return ap.parse_args()
 
@@ -253,6 +253,14 @@ def kernel_suite(B: int, cfg, small: bool = False):
         out.append(("f64_ew %s 2^24" % nm, 3 * 8 * n64, 0, (lambda o: lambda: Run.f64_ew(o, fa, fb, n64))(op)))
     out.append(("f64_of_f32 2^25", 12 * n32, 0, lambda: Run.f64_of_f32(da, n32)))
     out.append(("f32_of_f64 2^24", 12 * n64, 0, lambda: Run.f32_of_f64(fa, n64)))
+    # the fused attention of a layer: q, k, v strided slices of one [B, S, 3, H, 64] projection
+    Ba = B if not small else 16
+    qkv = f32(Ba, cfg.seq, 3, cfg.heads, cfg.dh)
+    qkv_v = [M.reshape(M.slice_(qkv, [0, 0, i, 0, 0], [Ba, cfg.seq, i + 1, cfg.heads, cfg.dh], [1, 1, 1, 1, 1]),
+                       [Ba, cfg.seq, cfg.heads, cfg.dh]) for i in range(3)]
+    out.append(("attention [%dx%dx%dx%d] (scores, soft_max, value)" % (Ba, cfg.seq, cfg.heads, cfg.dh),
+                4 * 4 * Ba * cfg.seq * cfg.heads * cfg.dh, 4 * Ba * cfg.heads * cfg.seq * cfg.seq * cfg.dh,
+                lambda: Run.attention(*qkv_v, Ba, cfg.seq, cfg.heads, cfg.dh, cfg.scale_bits())))
     w1, x1 = f32(128, 256), f32(64, 256)
     out.append(("mul_mat [64x256]x[256x128] (config 1)", 4 * (64 * 256 + 256 * 128 + 64 * 128),
                 2 * 64 * 128 * 256, lambda: Run.mul_mat(w1, x1, 256, 128, 64, 64, 0)))
@@ -523,6 +531,17 @@ def profile_run(args):
         c1 = M.launch_count()
         M.eval_([M.apply(fn, X + W)[0]])  # the captured step
         print("launches: warm-up %d, step %d" % (c1 - c0, M.launch_count() - c1))
+    elif args.profile_run == "attention":
+        # the fused attention at batch 16 of the denoiser's shape, three launches
+        cfg = D.Config(layers=1)
+        B = 16
+        rng = np.random.default_rng(0)
+        qkv = M.of_numpy(rng.standard_normal((B, cfg.seq, 3, cfg.heads, cfg.dh)).astype(np.float32))
+        qkv_v = [M.reshape(M.slice_(qkv, [0, 0, i, 0, 0], [B, cfg.seq, i + 1, cfg.heads, cfg.dh], [1, 1, 1, 1, 1]),
+                           [B, cfg.seq, cfg.heads, cfg.dh]) for i in range(3)]
+        outs = [Run.attention(*qkv_v, B, cfg.seq, cfg.heads, cfg.dh, cfg.scale_bits()) for _ in range(3)]
+        M.eval_(outs)
+        print("attention [%dx%dx%dx%d]: 3 launches" % (B, cfg.seq, cfg.heads, cfg.dh))
     elif args.profile_run == "kernels":
         suite = kernel_suite(args.batch_per_gpu, D.Config(layers=args.layers), small=True)
         outs = [fn() for _, _, _, fn in suite]

@@ -18,7 +18,7 @@ namespace {
 
 enum KernelKind {
   KK_MUL_MAT, KK_SOFT_MAX, KK_NORM, KK_SILU, KK_GELU_ERF, KK_ERFF_MAP, KK_DIVIDE, KK_SQRT, KK_F64_EW,
-  KK_F64_OF_F32, KK_F32_OF_F64, KK_MUL_MAT_EP, KK_NORM_AFFINE
+  KK_F64_OF_F32, KK_F32_OF_F64, KK_MUL_MAT_EP, KK_NORM_AFFINE, KK_ATTENTION
 };
 
 struct KernelInfo {
@@ -47,6 +47,7 @@ const KernelInfo kKernels[] = {
     // rounding of the unfused sequence is kept):
     {"shlo_mul_mat_bias", KK_MUL_MAT_EP, 5, 4, 7, kF32},  // w, x, bias, residual, p = [mul_mat's six, flags]
     {"shlo_norm_affine", KK_NORM_AFFINE, 4, 3, 4, kF32},  // x, gamma, beta, p = [norm's four]
+    {"shlo_attention", KK_ATTENTION, 4, 3, 5, kF32},      // q, k, v, p = [B, S, H, width, scale bits]
 };
 
 }  // namespace
@@ -267,8 +268,16 @@ int shlo_kernel_apply(shlo_kernel k, const shlo_arr *inputs, int n_inputs, const
   int rc = 0;
   for (int i = 0; i < n_inputs && !rc; i++) {
     if (i == ki.param_index) continue;
-    if (inputs[i]->buf && inputs[i]->buf->dev != dev) rc = fail("kernel %s: inputs on two devices", ki.name);
-    else rc = make_contiguous(inputs[i], &in[i]);
+    if (inputs[i]->buf && inputs[i]->buf->dev != dev) {
+      rc = fail("kernel %s: inputs on two devices", ki.name);
+      break;
+    }
+    if (ki.kind == KK_ATTENTION) {  // reads strided views itself (and copies what it cannot)
+      inputs[i]->rc.fetch_add(1);
+      in[i] = inputs[i];
+      continue;
+    }
+    rc = make_contiguous(inputs[i], &in[i]);
     // Kernels read with 16-byte vector loads: an offset view gets its own copy.
     if (!rc && in[i]->buf && ((uintptr_t)data_ptr(in[i]) & 15)) {
       Arr *c = nullptr;
@@ -295,6 +304,7 @@ int shlo_kernel_apply(shlo_kernel k, const shlo_arr *inputs, int n_inputs, const
       case KK_F32_OF_F64: rc = k_f32_of_f64(dev, in[0], p, &o); break;
       case KK_MUL_MAT_EP: rc = k_mul_mat_ep(dev, in[0], in[1], p, in[2], in[3], (int)p[6], &o); break;
       case KK_NORM_AFFINE: rc = k_norm_affine(dev, in[0], p, in[1], in[2], &o); break;
+      case KK_ATTENTION: rc = k_attention(dev, in[0], in[1], in[2], p, &o); break;
     }
   }
   for (Arr *a : in)

@@ -1,0 +1,382 @@
+// Fused attention for the executor: ggml's scores (mul_mat over the head width),
+// soft_max with its scale, and the value product (mul_mat over the keys) of one
+// (batch, head) in one launch, every rounding of the three kernels kept
+// (StablehloMlx/Kernels/Shaders.lean:55-123 for the two kernels; the module's
+// dot_general / ggml.soft_max / dot_general / transpose chain, Lower.lean:157-182).
+//
+// One CTA of 16 warps per (batch, head, 64 queries), one CTA an SM:
+//   1. K (all S keys) and the CTA's 64 queries, transposed into shared memory
+//      with the head width in ggml's packed class-major order (K = 64: sixteen
+//      segments of 4);
+//   2. the 64 x S scores with ggml_vec_dot_f32's chains and tree (the
+//      register-stack fold of k_mul_mat_short), NaN made arm64's, into a
+//      row-major shared tile;
+//   3. soft_max over each row exactly as g_soft_max (x * scale, the
+//      sequential max scan, ggml_v_expf(x - max), the four-lane group sums
+//      added in order to a binary64 sum, y = e * (float)(1 / sum)) while V's
+//      rows are copied in, in packed key order;
+//   4. the value product, the 16 key segments split over two halves of the
+//      CTA (the left and right subtrees of ggml's tree, added as its root),
+//      written straight into the [B][S][H][64] layout of the merged heads.
+#include "common.cuh"
+#include "ggml_math.cuh"
+#include "mul_mat.cuh"
+
+namespace shlo {
+
+namespace at {
+constexpr int DH = 64;        // head width: the scores' K
+constexpr int NQ = 64;        // queries a CTA
+constexpr int THREADS = 512;  // 16 warps
+template <int S>
+struct Smem {
+  static constexpr int SW = S + 4;   // a score row (16-byte aligned, rows 4 banks apart)
+  static constexpr int A = DH * S;   // Ks [64 packed d][S keys], then Vs [S packed keys][64 d]
+  static constexpr int Q = DH * NQ;  // Qs [64 packed d][64 queries], then the soft_max parts
+  static constexpr int SS = NQ * SW; // scores [64 queries][S keys], then the upper half's partials
+  static constexpr int P = S * NQ;   // probabilities [S packed keys][64 queries] (swizzled)
+  static constexpr size_t BYTES = (size_t)(A + Q + SS + P) * sizeof(float);
+};
+static_assert(Smem<256>::BYTES <= 227 * 1024, "one CTA an SM");
+}  // namespace at
+
+struct AttnArgs {
+  const float *q, *k, *v;
+  int64_t qs[3], ks[3], vs[3];  // element strides of batch, position, head (the width is contiguous)
+  float *o;                     // [B][S][H][64]
+  int H;
+  float sc;
+};
+
+// Packed position of head-width index d (K = 64: segments of 4, no padding).
+__device__ __forceinline__ constexpr int pk_d(int d) { return leaf_of_class(d & 15) * 4 + (d >> 4); }
+// Packed position of key j for the value product (segments of S / 16).
+template <int S>
+__device__ __forceinline__ constexpr int pk_key(int j) { return leaf_of_class(j & 15) * (S / 16) + (j >> 4); }
+// Column of query q in probability row pk: the float4 group index XORed with a
+// function of the row, so the soft_max's scattered stores spread over banks.
+template <int S>
+__device__ __forceinline__ constexpr int p_col(int pk, int q) {
+  return ((((q >> 2) ^ ((pk % (S / 16)) ^ (pk / (S / 16)))) & 15) << 2) | (q & 3);
+}
+
+// Score segment SG (packed d rows 4 SG .. 4 SG + 3): keys key..key+3 (w, m) by
+// queries qr..qr+3 (x, r), then the fold into the register stack.
+template <int SG, int S>
+__device__ __forceinline__ void score_seg(const float *Ks, const float *Qs, int key, int qr, float2 (&acc)[8],
+                                          float2 (&st)[4][8]) {
+#pragma unroll
+  for (int i = 0; i < 8; i++) acc[i] = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int kk = 0; kk < 4; kk++) {
+    const int p = 4 * SG + kk;
+    const float4 w4 = *reinterpret_cast<const float4 *>(Ks + p * S + key);
+    const float4 x4 = *reinterpret_cast<const float4 *>(Qs + p * at::NQ + qr);
+    const float2 w01 = make_float2(w4.x, w4.y), w23 = make_float2(w4.z, w4.w);
+    const float xr[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float2 xj = make_float2(xr[j], xr[j]);
+      acc[2 * j] = __ffma2_rn(w01, xj, acc[2 * j]);
+      acc[2 * j + 1] = __ffma2_rn(w23, xj, acc[2 * j + 1]);
+    }
+  }
+  fold_regs<SG>(acc, st);
+}
+
+template <int S, int... SG>
+__device__ __forceinline__ void score_segs(const float *Ks, const float *Qs, int key, int qr, float2 (&acc)[8],
+                                           float2 (&st)[4][8], std::integer_sequence<int, SG...>) {
+  (score_seg<SG, S>(Ks, Qs, key, qr, acc, st), ...);
+}
+
+// One pass of scores: keys key..key+3 by queries qr..qr+3 into the score rows
+// (NaN made arm64's). Not inlined, so that one pass's registers are all the
+// compiler allocates for it.
+template <int S>
+__device__ __noinline__ void score_pass(const float *Ks, const float *Qs, float *Ss, int key, int qr) {
+  float2 acc[8], st[4][8];
+  score_segs<S>(Ks, Qs, key, qr, acc, st, std::make_integer_sequence<int, 16>{});
+#pragma unroll
+  for (int j = 0; j < 4; j++)
+    *reinterpret_cast<float4 *>(Ss + (qr + j) * at::Smem<S>::SW + key) =
+        make_float4(arm_nan(acc[2 * j].x), arm_nan(acc[2 * j].y), arm_nan(acc[2 * j + 1].x), arm_nan(acc[2 * j + 1].y));
+}
+
+// Value segment BASE + SG (packed key rows (BASE + SG) S/16 ..): head-width
+// indices mo..mo+3 (w, m) by queries ro..ro+3 (x, r); the fold is the
+// subtree's (SG = 0..7).
+template <int BASE, int SG, int S>
+__device__ __forceinline__ void value_seg(const float *Vs, const float *Ps, int mo, int ro, float2 (&acc)[8],
+                                          float2 (&st)[4][8]) {
+  constexpr int SEGK = S / 16;
+#pragma unroll
+  for (int i = 0; i < 8; i++) acc[i] = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int kk = 0; kk < SEGK; kk++) {
+    const int p = (BASE + SG) * SEGK + kk;
+    const float4 w4 = *reinterpret_cast<const float4 *>(Vs + p * at::DH + mo);
+    const float4 x4 = *reinterpret_cast<const float4 *>(Ps + p * at::NQ + p_col<S>(p, ro));
+    const float2 w01 = make_float2(w4.x, w4.y), w23 = make_float2(w4.z, w4.w);
+    const float xr[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float2 xj = make_float2(xr[j], xr[j]);
+      acc[2 * j] = __ffma2_rn(w01, xj, acc[2 * j]);
+      acc[2 * j + 1] = __ffma2_rn(w23, xj, acc[2 * j + 1]);
+    }
+  }
+  fold_regs<SG>(acc, st);
+}
+
+template <int BASE, int S, int... SG>
+__device__ __forceinline__ void value_segs(const float *Vs, const float *Ps, int mo, int ro, float2 (&acc)[8],
+                                           float2 (&st)[4][8], std::integer_sequence<int, SG...>) {
+  (value_seg<BASE, SG, S>(Vs, Ps, mo, ro, acc, st), ...);
+}
+
+template <int S>
+__global__ void __launch_bounds__(at::THREADS, 1) k_attention(AttnArgs a) {
+  using namespace at;
+  using L = Smem<S>;
+  extern __shared__ __align__(16) float sm[];
+  float *A = sm, *Qs = sm + L::A, *Ss = Qs + L::Q, *Ps = Ss + L::SS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  constexpr int NQB = S / NQ;
+  const int qb = blockIdx.x % NQB, bh = blockIdx.x / NQB, h = bh % a.H, b = bh / a.H;
+  const int i0 = qb * NQ;
+
+  // 1. K and Q transposed: warp w moves head-width floats 4w..4w+3 of 32
+  //    consecutive rows (lane = row), so each store instruction writes one
+  //    packed row's 32 consecutive columns.
+  {
+    // rows of K, then of Q, 128 at a time (four 16-byte loads a lane in flight)
+    const float *kb = a.k + (int64_t)b * a.ks[0] + (int64_t)h * a.ks[2] + 4 * warp;
+    const float *qbp = a.q + (int64_t)b * a.qs[0] + (int64_t)(i0 * a.qs[1]) + (int64_t)h * a.qs[2] + 4 * warp;
+    int p[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) p[e] = pk_d(4 * warp + e);
+#pragma unroll 1
+    for (int r0 = 0; r0 < S + NQ; r0 += 128) {
+      float4 t[4];
+#pragma unroll
+      for (int it = 0; it < 4; it++) {
+        const int rr = r0 + it * 32 + lane;
+        if (rr < S + NQ)
+          t[it] = __ldg(reinterpret_cast<const float4 *>(rr < S ? kb + (int64_t)rr * a.ks[1]
+                                                                  : qbp + (int64_t)(rr - S) * a.qs[1]));
+      }
+#pragma unroll
+      for (int it = 0; it < 4; it++) {
+        const int rr = r0 + it * 32 + lane;
+        if (rr >= S + NQ) break;
+        float *d = rr < S ? A + rr : Qs + (rr - S);
+        const int w = rr < S ? S : NQ;
+        d[p[0] * w] = t[it].x;
+        d[p[1] * w] = t[it].y;
+        d[p[2] * w] = t[it].z;
+        d[p[3] * w] = t[it].w;
+      }
+    }
+  }
+  __syncthreads();
+
+  // 2. Scores, 128 keys a pass: warps 4 (keys) x 4 (queries), lanes 8 x 4.
+  {
+    const int km = (warp & 3) * 32 + (lane & 7) * 4;
+    const int qr = (warp >> 2) * 16 + (lane >> 3) * 4;
+#pragma unroll 1
+    for (int kb = 0; kb < S; kb += 128) score_pass<S>(A, Qs, Ss, kb + km, qr);
+  }
+  __syncthreads();
+
+  // 3. V's rows into A (now free) in packed key order, while soft_max runs.
+  {
+    const float *vb = a.v + (int64_t)b * a.vs[0] + (int64_t)h * a.vs[2];
+#pragma unroll
+    for (int i = 0; i < S * 16 / THREADS; i++) {
+      const int c = tid + i * THREADS, j = c >> 4, dq = (c & 15) * 4;
+      cp_async16(A + pk_key<S>(j) * DH + dq, vb + (int64_t)j * a.vs[1] + dq);
+    }
+    cp_async_commit();
+  }
+  // soft_max: warp w owns rows 4w..4w+3, eight lanes a row; lane g of a row
+  // takes the four-key groups g, g + 8, g + 16, ... The exponentials replace
+  // the scores in place until the normalisation.
+  {
+    constexpr int G = S / 32;  // groups a lane
+    const int r = lane >> 3, g = lane & 7, q = 4 * warp + r;
+    float *row = Ss + q * L::SW;
+    float *parts = Qs + q * (S / 4);  // the row's group sums, in group order
+    float mx = -INFINITY;
+    bool nan = false;
+#pragma unroll
+    for (int t = 0; t < G; t++) {
+      float4 x = *reinterpret_cast<const float4 *>(row + 4 * (g + 8 * t));
+      x.x = __fmul_rn(x.x, a.sc); x.y = __fmul_rn(x.y, a.sc); x.z = __fmul_rn(x.z, a.sc); x.w = __fmul_rn(x.w, a.sc);
+      nan |= (x.x != x.x) | (x.y != x.y) | (x.z != x.z) | (x.w != x.w);
+      mx = fmaxf(mx, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
+    }
+    // The max of a row without NaN is order-free (which zero it is cannot
+    // change an output); a row with a NaN takes the spec's sequential scan.
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const unsigned rowmask = 0xFFu << (8 * r);
+    const bool row_nan = (__ballot_sync(0xffffffffu, nan) & rowmask) != 0;
+    if (row_nan && g == 0) {
+      float m = -INFINITY;
+      for (int i = 0; i < S; i++) {
+        const float wv = __fmul_rn(row[i], a.sc);
+        m = (m > wv) ? m : wv;
+      }
+      mx = m;
+    }
+    mx = __shfl_sync(0xffffffffu, mx, 8 * r);
+    __syncwarp();  // the scan's reads before the exponentials overwrite the row
+#pragma unroll
+    for (int t = 0; t < G; t++) {
+      float4 *px = reinterpret_cast<float4 *>(row + 4 * (g + 8 * t));
+      const float4 x = *px;
+      float4 y;
+      y.x = ggml_v_expf(__fsub_rn(__fmul_rn(x.x, a.sc), mx));
+      y.y = ggml_v_expf(__fsub_rn(__fmul_rn(x.y, a.sc), mx));
+      y.z = ggml_v_expf(__fsub_rn(__fmul_rn(x.z, a.sc), mx));
+      y.w = ggml_v_expf(__fsub_rn(__fmul_rn(x.w, a.sc), mx));
+      *px = y;
+      parts[g + 8 * t] = __fadd_rn(__fadd_rn(y.x, y.y), __fadd_rn(y.z, y.w));
+    }
+    __syncwarp();
+    float inv = 0.0f;
+    if (g == 0) {
+      double sum = 0.0;
+      for (int k = 0; k < S / 4; k += 8) {  // eight parts loaded ahead of their serial adds
+        double v[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) v[i] = (double)parts[k + i];
+#pragma unroll
+        for (int i = 0; i < 8; i++) sum = __dadd_rn(sum, v[i]);
+      }
+      inv = __double2float_rn(__ddiv_rn(1.0, sum));
+    }
+    inv = __shfl_sync(0xffffffffu, inv, 8 * r);
+#pragma unroll
+    for (int t = 0; t < G; t++) {
+      const int j0 = 4 * (g + 8 * t);
+      const float4 e = *reinterpret_cast<const float4 *>(row + j0);
+      const float y[4] = {arm_nan(__fmul_rn(e.x, inv)), arm_nan(__fmul_rn(e.y, inv)), arm_nan(__fmul_rn(e.z, inv)),
+                          arm_nan(__fmul_rn(e.w, inv))};
+#pragma unroll
+      for (int c = 0; c < 4; c++) {
+        const int p = pk_key<S>(j0 + c);
+        Ps[p * NQ + p_col<S>(p, q)] = y[c];
+      }
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+
+  // 4. The value product: warps 0-7 the segments 0-7 (T(0..7)), warps 8-15
+  //    the segments 8-15 (T(8..15)); each half's warps 2 (width) x 4 (queries).
+  {
+    const int wg = warp & 7, half = warp >> 3;
+    const int mo = (wg & 1) * 32 + (lane & 7) * 4;
+    const int ro = (wg >> 1) * 16 + (lane >> 3) * 4;
+    float2 acc[8], st[4][8];
+    if (half == 0)
+      value_segs<0, S>(A, Ps, mo, ro, acc, st, std::make_integer_sequence<int, 8>{});
+    else
+      value_segs<8, S>(A, Ps, mo, ro, acc, st, std::make_integer_sequence<int, 8>{});
+    float4 *part = reinterpret_cast<float4 *>(Ss) + (tid & 255);
+    if (half == 1) {
+#pragma unroll
+      for (int i = 0; i < 4; i++) part[i * 256] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
+    }
+    __syncthreads();
+    if (half == 0) {
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float4 u = part[j * 256];
+        const float2 lo = __fadd2_rn(acc[2 * j], make_float2(u.x, u.y));      // the root: T(0..7) + T(8..15)
+        const float2 hi = __fadd2_rn(acc[2 * j + 1], make_float2(u.z, u.w));
+        float *dst = a.o + (((int64_t)b * S + i0 + ro + j) * a.H + h) * DH + mo;
+        *reinterpret_cast<float4 *>(dst) = make_float4(arm_nan(lo.x), arm_nan(lo.y), arm_nan(hi.x), arm_nan(hi.y));
+      }
+    }
+  }
+}
+
+// q, k, v: [B][S][H][64] views (any element strides of the first three
+// dimensions, the width contiguous); p = [B, S, H, width, scale bits].
+int k_attention(Device *dev, Arr *q, Arr *k, Arr *v, const uint32_t *p, Arr **out) {
+  const int64_t B = p[0], S = p[1], H = p[2], W = p[3];
+  const float sc = bitsf_host(p[4]);
+  if (W != at::DH || (S != 128 && S != 256) || B <= 0 || H <= 0)
+    return fail("attention: B=%lld S=%lld H=%lld width=%lld not carried (width 64, S 128 or 256)", (long long)B,
+                (long long)S, (long long)H, (long long)W);
+  Arr *in[3] = {q, k, v};
+  Arr *own[3] = {nullptr, nullptr, nullptr};
+  AttnArgs a{};
+  int64_t *strides[3] = {a.qs, a.ks, a.vs};
+  const float *ptrs[3];
+  int rc = 0;
+  for (int i = 0; i < 3 && !rc; i++) {
+    Arr *x = in[i];
+    if (x->dtype != kF32) {
+      rc = fail("attention: input %d is %s, f32 expected", i, dtype_name(x->dtype));
+      break;
+    }
+    if (x->ndim != 4 || x->shape[0] != B || x->shape[1] != S || x->shape[2] != H || x->shape[3] != W) {
+      rc = fail("attention: input %d is not [%lld, %lld, %lld, %lld]", i, (long long)B, (long long)S, (long long)H,
+                (long long)W);
+      break;
+    }
+    // 16-byte rows: the width contiguous, every row start a multiple of 4 floats.
+    bool ok = x->strides[3] == 1 && ((uintptr_t)data_ptr(x) & 15) == 0;
+    for (int d = 0; d < 3; d++) ok = ok && x->strides[d] % 4 == 0;
+    if (!ok) {
+      if ((rc = make_contiguous(x, &own[i]))) break;
+      x = own[i];
+    }
+    for (int d = 0; d < 3; d++) strides[i][d] = x->strides[d];
+    ptrs[i] = (const float *)data_ptr(x);
+  }
+  Arr *o = nullptr;
+  if (!rc) {
+    int64_t shape[1] = {B * S * H * W};
+    rc = new_array(dev, kF32, shape, 1, &o);
+  }
+  if (!rc) {
+    a.q = ptrs[0];
+    a.k = ptrs[1];
+    a.v = ptrs[2];
+    a.o = (float *)o->buf->ptr;
+    a.H = (int)H;
+    a.sc = sc;
+    static bool attr_done[64] = {false};
+    if (!attr_done[dev->id]) {
+      rc = cuda_check(cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)at::Smem<128>::BYTES), "attention attribute") ||
+           cuda_check(cudaFuncSetAttribute(k_attention<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           (int)at::Smem<256>::BYTES), "attention attribute");
+      if (!rc) attr_done[dev->id] = true;
+    }
+  }
+  if (!rc) {
+    const unsigned grid = (unsigned)(B * H * (S / at::NQ));
+    if (S == 256)
+      k_attention<256><<<grid, at::THREADS, at::Smem<256>::BYTES, dev->stream>>>(a);
+    else
+      k_attention<128><<<grid, at::THREADS, at::Smem<128>::BYTES, dev->stream>>>(a);
+    rc = launch_check("attention");
+  }
+  for (int i = 0; i < 3; i++)
+    if (own[i]) shlo_release(own[i]);
+  if (rc) {
+    if (o) shlo_release(o);
+    return 1;
+  }
+  *out = o;
+  return 0;
+}
+
+}  // namespace shlo

@@ -182,6 +182,9 @@ int k_soft_max(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 // norm with the executor's fused affine: (y * gamma[c]) + beta[c].
 int k_norm_affine(Device *dev, Arr *x, const uint32_t *p, Arr *gamma, Arr *beta, Arr **out);
+// The executor's fused attention (scores, soft_max, value product): q, k, v
+// [B][S][H][64] views, p = [B, S, H, 64, scale bits]; the result is [B][S][H][64].
+int k_attention(Device *dev, Arr *q, Arr *k, Arr *v, const uint32_t *p, Arr **out);
 int k_silu(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 int k_gelu_erf(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 int k_erff_map(Device *dev, const uint32_t *p, Arr **out);

@@ -5,14 +5,12 @@
 // SHLO_MUL_MAT_INSTANCES; ggml_kernels.cu calls them through the launchers
 // declared at the end.
 #pragma once
+#include <utility>
+
 #include "common.cuh"
+#include "ggml_math.cuh"
 
 namespace shlo {
-
-// arm64's default NaN, what an invalid operation (inf*0, inf-inf, 0/0) gives
-// there (FPCR.DN clear produces it for invalid operations; the GPU's own NaN is
-// 0x7FFFFFFF). The reductions return it for every NaN result.
-__device__ __forceinline__ float arm_nan(float v) { return v != v ? __uint_as_float(0x7FC00000u) : v; }
 
 // =============================================================== mul_mat ====
 // y[r*M + m] = ggml_vec_dot_f32(w row (r/N)*wbs + m*K, x row r), K long

@@ -1,7 +1,7 @@
 """Bit-preserving fusions for the executor (an optimisation of Lower.lean's
 one-op-at-a-time lowering; the reference has none).
 
-Two patterns of the denoiser and encoder modules are run as one launch each,
+Three patterns of the denoiser and encoder modules are run as one launch each,
 when nothing else reads the intermediate values:
 
   * dense: dot_general (no batching dimensions, one free dimension on the
@@ -10,7 +10,12 @@ when nothing else reads the intermediate values:
     `shlo_mul_mat_bias`, whose epilogue runs the same binary32 adds, rounded
     one at a time, in the module's operand order;
   * layer norm: ggml.norm -> multiply by a broadcast 1-D gain -> add a
-    broadcast 1-D bias: `shlo_norm_affine`.
+    broadcast 1-D bias: `shlo_norm_affine`;
+  * attention of one head width 64 over 128 or 256 positions: dot_general
+    (q k^T, batching over batch and head) -> ggml.soft_max -> dot_general
+    (p v) -> transpose to [batch, position, head, width]: `shlo_attention`,
+    which reads q, k and v where they lie (strided views of the projection)
+    and writes the transposed layout.
 
 Every rounding of the unfused sequence is kept, so the results are the same
 bits (tests/test_gpu_fuse.py checks whole modules fused against unfused). The
@@ -28,13 +33,15 @@ from . import run as Run
 
 @dataclass
 class Fused:
-    kind: str                 # "dense" or "norm"
+    kind: str                 # "dense", "norm" or "attention"
     result: str               # the value the last fused op defines
     skip: List[int]           # op indices replaced by this one
     bias: str = ""
     gain: str = ""
     res: str = ""
     flags: int = 0
+    v: str = ""               # attention: the value operand
+    scale: int = 0            # attention: the soft_max scale (binary32 bits)
 
 
 def any_fault(f: L.Faults) -> bool:
@@ -48,6 +55,51 @@ def _bcast_last_1d(op: L.Op) -> bool:
     mp = L.ints(op.attr("broadcast_dimensions") or "")
     out = op.out_tys[0]
     return mp == [len(out.dims) - 1] and op.in_tys[0].dims[0] == out.dims[-1]
+
+
+def _ggml(op: L.Op) -> str:
+    """The ggml.* routine a custom_call or composite names, else ""."""
+    if op.name not in ("stablehlo.custom_call", "stablehlo.composite"):
+        return ""
+    return (op.attr("name") or op.attr("call_target_name") or "").replace('"', "")
+
+
+def _dims(dn: str, key: str) -> List[int]:
+    return L.ints(L.field_(dn, key))
+
+
+def _attention(ops: List[L.Op], i: int, single_user, ready_before) -> Optional[Fused]:
+    """The attention chain whose scores dot_general is ops[i], if it matches."""
+    o = ops[i]
+    dn = o.attr("dot_dimension_numbers") or ""
+    if (_dims(dn, "lhs_batching_dimensions") != [0, 2] or _dims(dn, "rhs_batching_dimensions") != [0, 2]
+            or _dims(dn, "lhs_contracting_dimensions") != [3] or _dims(dn, "rhs_contracting_dimensions") != [3]):
+        return None
+    tq, tk = o.in_tys
+    if tq.el != "f32" or tk.el != "f32" or len(tq.dims) != 4 or list(tq.dims) != list(tk.dims):
+        return None
+    B, S, H, W = tq.dims
+    if W != 64 or S not in (128, 256) or list(o.out_tys[0].dims) != [B, H, S, S]:
+        return None
+    j = single_user(o.results[0])
+    if j is None or _ggml(ops[j]) != "ggml.soft_max" or ops[j].operands[0] != o.results[0]:
+        return None
+    attrs = ops[j].attr("composite_attributes") or ops[j].attr("backend_config") or ""
+    l = single_user(ops[j].results[0])
+    if l is None or ops[l].name != "stablehlo.dot_general" or ops[l].operands[0] != ops[j].results[0]:
+        return None
+    dn2 = ops[l].attr("dot_dimension_numbers") or ""
+    if (_dims(dn2, "lhs_batching_dimensions") != [0, 1] or _dims(dn2, "rhs_batching_dimensions") != [0, 2]
+            or _dims(dn2, "lhs_contracting_dimensions") != [3] or _dims(dn2, "rhs_contracting_dimensions") != [1]):
+        return None
+    v = ops[l].operands[1]
+    if list(ops[l].in_tys[1].dims) != [B, S, H, W] or ops[l].in_tys[1].el != "f32" or not ready_before(v, i):
+        return None
+    t = single_user(ops[l].results[0])
+    if (t is None or ops[t].name != "stablehlo.transpose"
+            or L.ints(ops[t].attr("permutation") or "") != [0, 2, 1, 3] or list(ops[t].out_tys[0].dims) != [B, S, H, W]):
+        return None
+    return Fused("attention", ops[t].results[0], [j, l, t], v=v, scale=L.f32_attr(attrs, "scale"))
 
 
 def plan(fn) -> Dict[int, Fused]:
@@ -82,6 +134,10 @@ def plan(fn) -> Dict[int, Fused]:
         if o.name == "stablehlo.dot_general" and o.out_tys and o.out_tys[0].el == "f32":
             dn = o.attr("dot_dimension_numbers") or ""
             if L.ints(L.field_(dn, "lhs_batching_dimensions")) or L.ints(L.field_(dn, "rhs_batching_dimensions")):
+                fz = _attention(ops, i, single_user, ready_before)
+                if fz is not None and not taken.intersection(fz.skip):
+                    out[i] = fz
+                    taken.update(fz.skip)
                 continue
             if len(o.in_tys[1].dims) != 2:
                 continue
@@ -126,6 +182,10 @@ def plan(fn) -> Dict[int, Fused]:
 
 def run_fused(fz: Fused, o: L.Op, env: Dict[str, M.Arr]) -> M.Arr:
     out = o.out_tys[0]
+    if fz.kind == "attention":
+        B, S, H, W = o.in_tys[0].dims
+        y = Run.attention(env[o.operands[0]], env[o.operands[1]], env[fz.v], B, S, H, W, fz.scale)
+        return M.reshape(y, [B, S, H, W])
     if fz.kind == "dense":
         dn = o.attr("dot_dimension_numbers") or ""
         lc = L.ints(L.field_(dn, "lhs_contracting_dimensions"))[0]

@@ -35,6 +35,7 @@ SPECS = {
 FUSED = {
     "mul_mat_bias": (["w", "x", "bias", "res", "p"], ["y"]),
     "norm_affine": (["x", "gamma", "beta", "p"], ["y"]),
+    "attention": (["q", "k", "v", "p"], ["y"]),
 }
 EP_BIAS, EP_BIAS_LHS, EP_RES, EP_RES_LHS = 1, 2, 4, 8
 
@@ -153,3 +154,10 @@ def mul_mat_bias(w, x, K, M_, R, N, w_batch_stride, bias, res=None, flags=EP_BIA
 def norm_affine(x, ncols, rows, eps_bits, gamma, beta):
     """norm, then (y * gamma[c]) + beta[c], each rounded alone."""
     return run("norm_affine", [x, gamma, beta, params([ncols, rows, eps_bits, 0])], [rows * ncols], M.dtF32, rows, 64)
+
+
+def attention(q, k, v, B, S, H, W, scale_bits):
+    """q, k, v [B, S, H, W] (any strides): per (batch, head) mul_mat(k, q)
+    (the scores, K = W), soft_max(scale), mul_mat(v^T, p) (K = S), the result
+    [B, S, H, W] -- the transposed layout of the merged heads."""
+    return run("attention", [q, k, v, params([B, S, H, W, scale_bits])], [B * S * H * W], M.dtF32, B * S * H, 64)

@@ -81,3 +81,43 @@ def test_modules_fused_equal_unfused(cfg, B):
         got = M.to_numpy(E.call(E.prepare(fused, None, compile_), X + W)[0])
         want = M.to_numpy(E.call(E.prepare(plain, None, compile_), X + W)[0])
         assert np.array_equal(bits(got), bits(want))
+
+
+def attn_text(B, S, H, W, scale_bits):
+    T = lambda *d: "tensor<" + "".join("%dx" % x for x in d) + "f32>"
+    q, s_, o, qkv = T(B, S, H, W), T(B, H, S, S), T(B, H, S, W), T(B, S, 3, H, W)
+    sl = T(B, S, 1, H, W)
+    parts = []
+    for i in range(3):
+        parts.append(
+            f'    %sl{i} = "stablehlo.slice"(%qkv) {{start_indices = array<i64: 0, 0, {i}, 0, 0>, limit_indices = '
+            f'array<i64: {B}, {S}, {i + 1}, {H}, {W}>, strides = array<i64: 1, 1, 1, 1, 1>}} : ({qkv}) -> {sl}\n'
+            f'    %x{i} = "stablehlo.reshape"(%sl{i}) : ({sl}) -> {q}\n')
+    return f"""module {{
+  func.func public @main(%qkv: {qkv}) -> ({q}) {{
+{''.join(parts)}    %s = "stablehlo.dot_general"(%x0, %x1) {{dot_dimension_numbers = #stablehlo.dot<lhs_batching_dimensions = [0, 2], rhs_batching_dimensions = [0, 2], lhs_contracting_dimensions = [3], rhs_contracting_dimensions = [3]>}} : ({q}, {q}) -> {s_}
+    %p = "stablehlo.custom_call"(%s) {{call_target_name = "ggml.soft_max", backend_config = "scale = 0x{scale_bits:08X} : f32"}} : ({s_}) -> {s_}
+    %o = "stablehlo.dot_general"(%p, %x2) {{dot_dimension_numbers = #stablehlo.dot<lhs_batching_dimensions = [0, 1], rhs_batching_dimensions = [0, 2], lhs_contracting_dimensions = [3], rhs_contracting_dimensions = [1]>}} : ({s_}, {q}) -> {o}
+    %t = "stablehlo.transpose"(%o) {{permutation = array<i64: 0, 2, 1, 3>}} : ({o}) -> {q}
+    func.return %t : {q}
+  }}
+}}
+"""
+
+
+@pytest.mark.parametrize("B,S,H,scale,special", [(2, 256, 8, 0x3E000000, False), (1, 128, 3, 0x3E000000, True),
+                                                 (3, 256, 2, 0x3F800000, True), (1, 256, 1, 0x41000000, False)])
+def test_attention_matches_unfused(B, S, H, scale, special):
+    # q, k, v as the strided slices of one projection, as in the encoder layer;
+    # specials give NaN and infinite score rows (the soft_max's sequential scan)
+    rng = np.random.default_rng(B * 1000 + S + H)
+    a = specials(rng, (B, S, 3, H, 64)) if special else rng.standard_normal((B, S, 3, H, 64)).astype(np.float32)
+    x = [M.of_numpy(a * np.float32(4.0))]
+    text = attn_text(B, S, H, 64, scale)
+    fused = E.load(text)
+    plain = E.load(text)
+    plain.module.fuse = False
+    for compile_ in (False, True):
+        got = M.to_numpy(E.call(E.prepare(fused, None, compile_), x)[0])
+        want = M.to_numpy(E.call(E.prepare(plain, None, compile_), x)[0])
+        assert np.array_equal(bits(got), bits(want))
