@@ -4,17 +4,21 @@
 // (StablehloMlx/Kernels/Shaders.lean:55-123 for the two kernels; the module's
 // dot_general / ggml.soft_max / dot_general / transpose chain, Lower.lean:157-182).
 //
-// One CTA of 16 warps per (batch, head, 64 queries), one CTA an SM:
-//   1. K (all S keys) and the CTA's 64 queries, transposed into shared memory
-//      with the head width in ggml's packed class-major order (K = 64: sixteen
-//      segments of 4);
-//   2. the 64 x S scores with ggml_vec_dot_f32's chains and tree (the
+// One CTA of 8 warps per (batch, head, 32 queries), two CTAs an SM, so that one
+// CTA's loads and soft_max overlap the other's products (both products are
+// bound by shared-memory reads: a 4 x 4 tile a thread, the most the register
+// stack of the fold leaves room for):
+//   1. K (all S keys) and the CTA's 32 queries, loaded row-contiguously and
+//      stored transposed into shared memory with the head width in ggml's
+//      packed class-major order (K = 64: sixteen segments of 4);
+//   2. the 32 x S scores with ggml_vec_dot_f32's chains and tree (the
 //      register-stack fold of k_mul_mat_short), NaN made arm64's, into a
 //      row-major shared tile;
-//   3. soft_max over each row exactly as g_soft_max (x * scale, the
-//      sequential max scan, ggml_v_expf(x - max), the four-lane group sums
-//      added in order to a binary64 sum, y = e * (float)(1 / sum)) while V's
-//      rows are copied in, in packed key order;
+//   3. soft_max over each row exactly as g_soft_max (x * scale, the max,
+//      ggml_v_expf(x - max), the four-lane group sums added in order to a
+//      binary64 sum, y = e * (float)(1 / sum)), the rows held in registers so
+//      that the probabilities can replace the scores in packed key order, while
+//      V's rows are copied in;
 //   4. the value product, the 16 key segments split over two halves of the
 //      CTA (the left and right subtrees of ggml's tree, added as its root),
 //      written straight into the [B][S][H][64] layout of the merged heads.
@@ -26,18 +30,17 @@ namespace shlo {
 
 namespace at {
 constexpr int DH = 64;        // head width: the scores' K
-constexpr int NQ = 64;        // queries a CTA
-constexpr int THREADS = 512;  // 16 warps
+constexpr int NQ = 32;        // queries a CTA
+constexpr int THREADS = 256;  // 8 warps
 template <int S>
 struct Smem {
   static constexpr int SW = S + 4;   // a score row (16-byte aligned, rows 4 banks apart)
-  static constexpr int A = DH * S;   // Ks [64 packed d][S keys], then Vs [S packed keys][64 d]
-  static constexpr int Q = DH * NQ;  // Qs [64 packed d][64 queries], then the soft_max parts
-  static constexpr int SS = NQ * SW; // scores [64 queries][S keys], then the upper half's partials
-  static constexpr int P = S * NQ;   // probabilities [S packed keys][64 queries] (swizzled)
-  static constexpr size_t BYTES = (size_t)(A + Q + SS + P) * sizeof(float);
+  static constexpr int A = DH * S;   // K^T [64 packed d][S keys], then V [S packed keys][64 d]
+  static constexpr int Q = DH * NQ;  // Q^T [64 packed d][32 queries], then the group sums, then partials
+  static constexpr int SP = NQ * SW > S * NQ ? NQ * SW : S * NQ;  // scores [32][SW], then P [S packed keys][32]
+  static constexpr size_t BYTES = (size_t)(A + Q + SP) * sizeof(float);
 };
-static_assert(Smem<256>::BYTES <= 227 * 1024, "one CTA an SM");
+static_assert(Smem<256>::BYTES <= 113 * 1024, "two CTAs an SM");
 }  // namespace at
 
 struct AttnArgs {
@@ -53,11 +56,19 @@ __device__ __forceinline__ constexpr int pk_d(int d) { return leaf_of_class(d & 
 // Packed position of key j for the value product (segments of S / 16).
 template <int S>
 __device__ __forceinline__ constexpr int pk_key(int j) { return leaf_of_class(j & 15) * (S / 16) + (j >> 4); }
-// Column of query q in probability row pk: the float4 group index XORed with a
-// function of the row, so the soft_max's scattered stores spread over banks.
+// Shared-memory places. Each XORs the float4 group index of a column with a
+// function of the row, so that the transposing stores spread over the banks
+// while a thread's four consecutive columns stay one 16-byte vector.
 template <int S>
-__device__ __forceinline__ constexpr int p_col(int pk, int q) {
-  return ((((q >> 2) ^ ((pk % (S / 16)) ^ (pk / (S / 16)))) & 15) << 2) | (q & 3);
+__device__ __forceinline__ constexpr int k_at(int p, int key) {  // K^T
+  return p * S + ((((key >> 2) ^ (p & 15)) << 2) | (key & 3));
+}
+__device__ __forceinline__ constexpr int q_at(int p, int q) {  // Q^T
+  return p * at::NQ + ((((q >> 2) ^ (p & 7)) << 2) | (q & 3));
+}
+template <int S>
+__device__ __forceinline__ constexpr int p_at(int p, int q) {  // P: the same for both halves of the value product
+  return p * at::NQ + (((((q >> 2) ^ (p % (S / 16)) ^ ((p / (S / 16)) & 7))) & 7) << 2) + (q & 3);
 }
 
 // Score segment SG (packed d rows 4 SG .. 4 SG + 3): keys key..key+3 (w, m) by
@@ -70,8 +81,8 @@ __device__ __forceinline__ void score_seg(const float *Ks, const float *Qs, int 
 #pragma unroll
   for (int kk = 0; kk < 4; kk++) {
     const int p = 4 * SG + kk;
-    const float4 w4 = *reinterpret_cast<const float4 *>(Ks + p * S + key);
-    const float4 x4 = *reinterpret_cast<const float4 *>(Qs + p * at::NQ + qr);
+    const float4 w4 = *reinterpret_cast<const float4 *>(Ks + k_at<S>(p, key));
+    const float4 x4 = *reinterpret_cast<const float4 *>(Qs + q_at(p, qr));
     const float2 w01 = make_float2(w4.x, w4.y), w23 = make_float2(w4.z, w4.w);
     const float xr[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
@@ -103,20 +114,21 @@ __device__ __noinline__ void score_pass(const float *Ks, const float *Qs, float 
         make_float4(arm_nan(acc[2 * j].x), arm_nan(acc[2 * j].y), arm_nan(acc[2 * j + 1].x), arm_nan(acc[2 * j + 1].y));
 }
 
-// Value segment BASE + SG (packed key rows (BASE + SG) S/16 ..): head-width
-// indices mo..mo+3 (w, m) by queries ro..ro+3 (x, r); the fold is the
-// subtree's (SG = 0..7).
-template <int BASE, int SG, int S>
+// Value segment SG of a half (its packed key rows SG S/16 .. of Vs and Ps,
+// which point at the half's first row): head-width indices mo..mo+3 (w, m) by
+// queries ro..ro+3 (x, r); the fold is the subtree's (SG = 0..7). Both halves
+// run this one code, four k a trip.
+template <int SG, int S>
 __device__ __forceinline__ void value_seg(const float *Vs, const float *Ps, int mo, int ro, float2 (&acc)[8],
                                           float2 (&st)[4][8]) {
   constexpr int SEGK = S / 16;
 #pragma unroll
   for (int i = 0; i < 8; i++) acc[i] = make_float2(0.0f, 0.0f);
-#pragma unroll
+#pragma unroll 4
   for (int kk = 0; kk < SEGK; kk++) {
-    const int p = (BASE + SG) * SEGK + kk;
+    const int p = SG * SEGK + kk;
     const float4 w4 = *reinterpret_cast<const float4 *>(Vs + p * at::DH + mo);
-    const float4 x4 = *reinterpret_cast<const float4 *>(Ps + p * at::NQ + p_col<S>(p, ro));
+    const float4 x4 = *reinterpret_cast<const float4 *>(Ps + p_at<S>(p, ro));
     const float2 w01 = make_float2(w4.x, w4.y), w23 = make_float2(w4.z, w4.w);
     const float xr[4] = {x4.x, x4.y, x4.z, x4.w};
 #pragma unroll
@@ -129,64 +141,58 @@ __device__ __forceinline__ void value_seg(const float *Vs, const float *Ps, int 
   fold_regs<SG>(acc, st);
 }
 
-template <int BASE, int S, int... SG>
+template <int S, int... SG>
 __device__ __forceinline__ void value_segs(const float *Vs, const float *Ps, int mo, int ro, float2 (&acc)[8],
                                            float2 (&st)[4][8], std::integer_sequence<int, SG...>) {
-  (value_seg<BASE, SG, S>(Vs, Ps, mo, ro, acc, st), ...);
+  (value_seg<SG, S>(Vs, Ps, mo, ro, acc, st), ...);
 }
 
 template <int S>
-__global__ void __launch_bounds__(at::THREADS, 1) k_attention(AttnArgs a) {
+__global__ void __launch_bounds__(at::THREADS, 2) k_attention(AttnArgs a) {
   using namespace at;
   using L = Smem<S>;
   extern __shared__ __align__(16) float sm[];
-  float *A = sm, *Qs = sm + L::A, *Ss = Qs + L::Q, *Ps = Ss + L::SS;
+  float *A = sm, *Qs = sm + L::A, *SP = Qs + L::Q;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   constexpr int NQB = S / NQ;
   const int qb = blockIdx.x % NQB, bh = blockIdx.x / NQB, h = bh % a.H, b = bh / a.H;
   const int i0 = qb * NQ;
 
-  // 1. K and Q transposed: warp w moves head-width floats 4w..4w+3 of 32
-  //    consecutive rows (lane = row), so each store instruction writes one
-  //    packed row's 32 consecutive columns.
+  // 1. K and Q: sixteen lanes read a row's 256 bytes (two rows an instruction),
+  //    every load in flight at once; lane l's four head-width floats 4 (l % 16)
+  //    .. + 3 go to their packed rows.
   {
-    // rows of K, then of Q, 128 at a time (four 16-byte loads a lane in flight)
-    const float *kb = a.k + (int64_t)b * a.ks[0] + (int64_t)h * a.ks[2] + 4 * warp;
-    const float *qbp = a.q + (int64_t)b * a.qs[0] + (int64_t)(i0 * a.qs[1]) + (int64_t)h * a.qs[2] + 4 * warp;
-    int p[4];
+    constexpr int NR = (S + NQ) * 16 / THREADS;  // 16-byte loads a thread
+    const int dc = tid & 15, r0 = tid >> 4;
+    const float *kb = a.k + (int64_t)b * a.ks[0] + (int64_t)h * a.ks[2] + 4 * dc;
+    const float *qbp = a.q + (int64_t)b * a.qs[0] + (int64_t)i0 * a.qs[1] + (int64_t)h * a.qs[2] + 4 * dc;
+    float4 t[NR];
 #pragma unroll
-    for (int e = 0; e < 4; e++) p[e] = pk_d(4 * warp + e);
-#pragma unroll 1
-    for (int r0 = 0; r0 < S + NQ; r0 += 128) {
-      float4 t[4];
+    for (int i = 0; i < NR; i++) {
+      const int row = r0 + 16 * i;
+      t[i] = __ldg(reinterpret_cast<const float4 *>(i < S / 16 ? kb + (int64_t)row * a.ks[1]
+                                                               : qbp + (int64_t)(row - S) * a.qs[1]));
+    }
 #pragma unroll
-      for (int it = 0; it < 4; it++) {
-        const int rr = r0 + it * 32 + lane;
-        if (rr < S + NQ)
-          t[it] = __ldg(reinterpret_cast<const float4 *>(rr < S ? kb + (int64_t)rr * a.ks[1]
-                                                                  : qbp + (int64_t)(rr - S) * a.qs[1]));
-      }
+    for (int e = 0; e < 4; e++) {
+      const int p = pk_d(4 * dc + e);
 #pragma unroll
-      for (int it = 0; it < 4; it++) {
-        const int rr = r0 + it * 32 + lane;
-        if (rr >= S + NQ) break;
-        float *d = rr < S ? A + rr : Qs + (rr - S);
-        const int w = rr < S ? S : NQ;
-        d[p[0] * w] = t[it].x;
-        d[p[1] * w] = t[it].y;
-        d[p[2] * w] = t[it].z;
-        d[p[3] * w] = t[it].w;
+      for (int i = 0; i < NR; i++) {
+        const int row = r0 + 16 * i;
+        const float v = e == 0 ? t[i].x : e == 1 ? t[i].y : e == 2 ? t[i].z : t[i].w;
+        if (i < S / 16) A[k_at<S>(p, row)] = v;
+        else Qs[q_at(p, row - S)] = v;
       }
     }
   }
   __syncthreads();
 
-  // 2. Scores, 128 keys a pass: warps 4 (keys) x 4 (queries), lanes 8 x 4.
+  // 2. Scores, 128 keys a pass: warps 4 (keys) x 2 (queries), lanes 8 x 4.
   {
     const int km = (warp & 3) * 32 + (lane & 7) * 4;
     const int qr = (warp >> 2) * 16 + (lane >> 3) * 4;
 #pragma unroll 1
-    for (int kb = 0; kb < S; kb += 128) score_pass<S>(A, Qs, Ss, kb + km, qr);
+    for (int kb = 0; kb < S; kb += 128) score_pass<S>(A, Qs, SP, kb + km, qr);
   }
   __syncthreads();
 
@@ -201,19 +207,20 @@ __global__ void __launch_bounds__(at::THREADS, 1) k_attention(AttnArgs a) {
     cp_async_commit();
   }
   // soft_max: warp w owns rows 4w..4w+3, eight lanes a row; lane g of a row
-  // takes the four-key groups g, g + 8, g + 16, ... The exponentials replace
-  // the scores in place until the normalisation.
+  // holds the four-key groups g, g + 8, g + 16, ... in registers.
   {
     constexpr int G = S / 32;  // groups a lane
     const int r = lane >> 3, g = lane & 7, q = 4 * warp + r;
-    float *row = Ss + q * L::SW;
+    const float *row = SP + q * L::SW;
     float *parts = Qs + q * (S / 4);  // the row's group sums, in group order
+    float4 e[G];
     float mx = -INFINITY;
     bool nan = false;
 #pragma unroll
     for (int t = 0; t < G; t++) {
       float4 x = *reinterpret_cast<const float4 *>(row + 4 * (g + 8 * t));
       x.x = __fmul_rn(x.x, a.sc); x.y = __fmul_rn(x.y, a.sc); x.z = __fmul_rn(x.z, a.sc); x.w = __fmul_rn(x.w, a.sc);
+      e[t] = x;
       nan |= (x.x != x.x) | (x.y != x.y) | (x.z != x.z) | (x.w != x.w);
       mx = fmaxf(mx, fmaxf(fmaxf(x.x, x.y), fmaxf(x.z, x.w)));
     }
@@ -232,17 +239,14 @@ __global__ void __launch_bounds__(at::THREADS, 1) k_attention(AttnArgs a) {
       mx = m;
     }
     mx = __shfl_sync(0xffffffffu, mx, 8 * r);
-    __syncwarp();  // the scan's reads before the exponentials overwrite the row
 #pragma unroll
     for (int t = 0; t < G; t++) {
-      float4 *px = reinterpret_cast<float4 *>(row + 4 * (g + 8 * t));
-      const float4 x = *px;
       float4 y;
-      y.x = ggml_v_expf(__fsub_rn(__fmul_rn(x.x, a.sc), mx));
-      y.y = ggml_v_expf(__fsub_rn(__fmul_rn(x.y, a.sc), mx));
-      y.z = ggml_v_expf(__fsub_rn(__fmul_rn(x.z, a.sc), mx));
-      y.w = ggml_v_expf(__fsub_rn(__fmul_rn(x.w, a.sc), mx));
-      *px = y;
+      y.x = ggml_v_expf(__fsub_rn(e[t].x, mx));
+      y.y = ggml_v_expf(__fsub_rn(e[t].y, mx));
+      y.z = ggml_v_expf(__fsub_rn(e[t].z, mx));
+      y.w = ggml_v_expf(__fsub_rn(e[t].w, mx));
+      e[t] = y;
       parts[g + 8 * t] = __fadd_rn(__fadd_rn(y.x, y.y), __fadd_rn(y.z, y.w));
     }
     __syncwarp();
@@ -259,43 +263,39 @@ __global__ void __launch_bounds__(at::THREADS, 1) k_attention(AttnArgs a) {
       inv = __double2float_rn(__ddiv_rn(1.0, sum));
     }
     inv = __shfl_sync(0xffffffffu, inv, 8 * r);
+    __syncthreads();  // every score read (the scans too): P may now replace them
+    float *Ps = SP;
 #pragma unroll
     for (int t = 0; t < G; t++) {
       const int j0 = 4 * (g + 8 * t);
-      const float4 e = *reinterpret_cast<const float4 *>(row + j0);
-      const float y[4] = {arm_nan(__fmul_rn(e.x, inv)), arm_nan(__fmul_rn(e.y, inv)), arm_nan(__fmul_rn(e.z, inv)),
-                          arm_nan(__fmul_rn(e.w, inv))};
+      const float y[4] = {arm_nan(__fmul_rn(e[t].x, inv)), arm_nan(__fmul_rn(e[t].y, inv)),
+                          arm_nan(__fmul_rn(e[t].z, inv)), arm_nan(__fmul_rn(e[t].w, inv))};
 #pragma unroll
-      for (int c = 0; c < 4; c++) {
-        const int p = pk_key<S>(j0 + c);
-        Ps[p * NQ + p_col<S>(p, q)] = y[c];
-      }
+      for (int c = 0; c < 4; c++) Ps[p_at<S>(pk_key<S>(j0 + c), q)] = y[c];
     }
   }
   cp_async_wait<0>();
   __syncthreads();
 
-  // 4. The value product: warps 0-7 the segments 0-7 (T(0..7)), warps 8-15
-  //    the segments 8-15 (T(8..15)); each half's warps 2 (width) x 4 (queries).
+  // 4. The value product: warps 0-3 the segments 0-7 (T(0..7)), warps 4-7 the
+  //    segments 8-15 (T(8..15)); each half's warps 2 (width) x 2 (queries).
   {
-    const int wg = warp & 7, half = warp >> 3;
+    const int wg = warp & 3, half = warp >> 2;
     const int mo = (wg & 1) * 32 + (lane & 7) * 4;
     const int ro = (wg >> 1) * 16 + (lane >> 3) * 4;
+    const int row0 = half * 8 * (S / 16);  // the half's first packed key row
     float2 acc[8], st[4][8];
-    if (half == 0)
-      value_segs<0, S>(A, Ps, mo, ro, acc, st, std::make_integer_sequence<int, 8>{});
-    else
-      value_segs<8, S>(A, Ps, mo, ro, acc, st, std::make_integer_sequence<int, 8>{});
-    float4 *part = reinterpret_cast<float4 *>(Ss) + (tid & 255);
+    value_segs<S>(A + row0 * DH, SP + row0 * NQ, mo, ro, acc, st, std::make_integer_sequence<int, 8>{});
+    float4 *part = reinterpret_cast<float4 *>(Qs) + (tid & 127);  // the group sums are spent
     if (half == 1) {
 #pragma unroll
-      for (int i = 0; i < 4; i++) part[i * 256] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
+      for (int i = 0; i < 4; i++) part[i * 128] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
     }
     __syncthreads();
     if (half == 0) {
 #pragma unroll
       for (int j = 0; j < 4; j++) {
-        const float4 u = part[j * 256];
+        const float4 u = part[j * 128];
         const float2 lo = __fadd2_rn(acc[2 * j], make_float2(u.x, u.y));      // the root: T(0..7) + T(8..15)
         const float2 hi = __fadd2_rn(acc[2 * j + 1], make_float2(u.z, u.w));
         float *dst = a.o + (((int64_t)b * S + i0 + ro + j) * a.H + h) * DH + mo;
