@@ -461,9 +461,12 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   auto wave_fill = [&](int64_t t) { return (double)t / (double)(((t + slots - 1) / slots) * slots); };
   // Halves where measured faster (B200, the denoiser's shapes): long K
   // (>= 2048) or narrow M (<= 512), each half at least 16 stages of 16 k and
-  // the grid no fuller in its last wave than halved. Quarters only on request.
+  // the grid no fuller in its last wave than halved. Quarters for tiny grids (below).
   int split = 1;
   if (segp / 2 >= 16 && (segp >= 128 || M <= 512) && wave_fill(2 * tiles) + 0.01 >= wave_fill(tiles)) split = 2;
+  // A grid of a few tiles (the timestep MLP) leaves most SMs
+  // idle: quarters make each CTA's K four times shorter.
+  if (4 * tiles <= slots / 2 && segp >= 8) split = 4;
   if (const char *e = getenv("SHLO_MM_SPLIT")) split = atoi(e) == 4 ? 4 : atoi(e) == 2 ? 2 : 1;
   const bool shared_tile = split > 1;
   const unsigned grid = (unsigned)(split * tiles);
