@@ -381,6 +381,10 @@ int shlo_apply(shlo_fn f, const shlo_arr *inputs, int n_inputs, shlo_arr *output
     Arr *r;
     int rc = new_array(dev, o->dtype, o->shape, o->ndim, &r);
     if (!rc && r->buf) rc = launch_copy_strided(dev, o, r->buf->ptr);
+    // a result is often read back at once, while the next call computes
+    if (!rc && r->buf && !dev->capturing)
+      rc = cuda_check(cudaEventCreateWithFlags(&r->buf->ready, cudaEventDisableTiming), "apply") ||
+           cuda_check(cudaEventRecord(r->buf->ready, dev->stream), "apply");
     if (rc) {
       if (r) shlo_release(r);
       release_all(outputs, n);

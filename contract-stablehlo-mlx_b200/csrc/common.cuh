@@ -52,8 +52,7 @@ struct Device {
   int id = 0;
   int sm_count = 0;
   cudaStream_t stream = nullptr;  // all compute
-  cudaStream_t copy = nullptr;    // host<->device copies of shlo_of_bytes
-  cudaEvent_t copy_done = nullptr;
+  cudaStream_t copy = nullptr;    // device-to-host copies of shlo_to_bytes
   std::mutex mu;                  // allocator
   std::multimap<size_t, void *> free_blocks;
   size_t pooled_bytes = 0;
@@ -82,6 +81,10 @@ struct Buffer {
   // block is never pooled while the graph lives.
   void *graph_owner = nullptr;
   bool no_recycle = false;  // written at capture time (a constant): never reused inside the capture
+  // Recorded on the compute stream right after the buffer was written, where a
+  // reader off that stream may come (the results of a graph replay): the
+  // device-to-host copy of shlo_to_bytes waits for it and nothing later.
+  cudaEvent_t ready = nullptr;
   // Derived layouts (e.g. the packed operand of mul_mat), keyed by how they
   // were derived, each with the launch that derives it again. Storage is
   // immutable once written, so they stay valid for the buffer's lifetime; the

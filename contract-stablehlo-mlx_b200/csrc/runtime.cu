@@ -97,6 +97,7 @@ static int init_device(int id, Device **out) {
     d->id = id;
     SHLO_CUDA(cudaDeviceGetAttribute(&d->sm_count, cudaDevAttrMultiProcessorCount, id));
     SHLO_CUDA(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
+    SHLO_CUDA(cudaStreamCreateWithFlags(&d->copy, cudaStreamNonBlocking));
     g_devs[id] = d;
   }
   *out = g_devs[id];
@@ -220,6 +221,7 @@ void buffer_release(Buffer *b) {
       dev->capture_free.emplace(b->bytes, b->ptr);
     }
   }
+  if (b->ready) cudaEventDestroy(b->ready);
   delete b;
 }
 
@@ -323,14 +325,14 @@ int make_contiguous(Arr *a, Arr **out) {
 }
 
 // Wait for all queued work on a device, bounded by SHLO_EVAL_TIMEOUT_S.
-static int wait_device(Device *dev, const char *what) {
+static int wait_stream(Device *dev, cudaStream_t stream, const char *what) {
   static double limit = [] {
     const char *e = getenv("SHLO_EVAL_TIMEOUT_S");
     return e ? atof(e) : 600.0;
   }();
   auto t0 = std::chrono::steady_clock::now();
   for (int spins = 0;; spins++) {
-    cudaError_t e = cudaStreamQuery(dev->stream);
+    cudaError_t e = cudaStreamQuery(stream);
     if (e == cudaSuccess) return 0;
     if (e != cudaErrorNotReady) return cuda_check(e, what);
     double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
@@ -339,6 +341,8 @@ static int wait_device(Device *dev, const char *what) {
     else std::this_thread::sleep_for(std::chrono::microseconds(50));
   }
 }
+
+static int wait_device(Device *dev, const char *what) { return wait_stream(dev, dev->stream, what); }
 
 int device_wait(Device *dev, const char *what) { return wait_device(dev, what); }
 
@@ -537,8 +541,28 @@ int shlo_to_bytes(shlo_arr a, void *dst, size_t cap) {
   SHLO_TRY(arr_device(a, &dev));
   Arr *c;
   SHLO_TRY(make_contiguous(a, &c));
-  cudaError_t e = cudaMemcpyAsync(dst, data_ptr(c), bytes, cudaMemcpyDeviceToHost, dev->stream);
-  int rc = cuda_check(e, "toBytes") || wait_device(dev, "toBytes");
+  int rc;
+  if (dev->capturing) {
+    rc = cuda_check(cudaMemcpyAsync(dst, data_ptr(c), bytes, cudaMemcpyDeviceToHost, dev->stream), "toBytes") ||
+         wait_device(dev, "toBytes");
+  } else {
+    // On the copy stream, after the array's producer: its buffer's ready event
+    // where it has one (a graph replay's result), so that work queued on the
+    // compute stream after the producer runs on while the bytes cross to the
+    // host; otherwise everything queued on the compute stream so far.
+    cudaEvent_t ready = c->buf->ready, own = nullptr;
+    rc = 0;
+    if (!ready) {
+      rc = cuda_check(cudaEventCreateWithFlags(&own, cudaEventDisableTiming), "toBytes") ||
+           cuda_check(cudaEventRecord(own, dev->stream), "toBytes");
+      ready = own;
+    }
+    if (!rc)
+      rc = cuda_check(cudaStreamWaitEvent(dev->copy, ready, 0), "toBytes") ||
+           cuda_check(cudaMemcpyAsync(dst, data_ptr(c), bytes, cudaMemcpyDeviceToHost, dev->copy), "toBytes") ||
+           wait_stream(dev, dev->copy, "toBytes");
+    if (own) cudaEventDestroy(own);
+  }
   release_arr(c);
   return rc;
 }
