@@ -56,6 +56,9 @@ struct Device {
   std::mutex mu;                  // allocator
   std::multimap<size_t, void *> free_blocks;
   size_t pooled_bytes = 0;
+  // Blocks of shlo_of_bytes's uploads, each with the event recorded on `stream`
+  // when it was released (see alloc_upload).
+  std::multimap<size_t, std::pair<void *, cudaEvent_t>> upload_free;
   // A CUDA-graph capture in progress on `stream` (shlo_apply of a compiled
   // function): blocks allocated meanwhile belong to `capture_owner` and are
   // listed in `capture_allocs`; blocks the capture frees go to `capture_free`
@@ -85,6 +88,7 @@ struct Buffer {
   // reader off that stream may come (the results of a graph replay): the
   // device-to-host copy of shlo_to_bytes waits for it and nothing later.
   cudaEvent_t ready = nullptr;
+  bool upload = false;  // from the upload pool (shlo_of_bytes on the copy stream)
   // Derived layouts (e.g. the packed operand of mul_mat), keyed by how they
   // were derived, each with the launch that derives it again. Storage is
   // immutable once written, so they stay valid for the buffer's lifetime; the

@@ -201,6 +201,50 @@ static int alloc_block(Device *dev, size_t bytes, bool constant, Buffer **out) {
 }
 
 int buffer_alloc(Device *dev, size_t bytes, Buffer **out) { return alloc_block(dev, bytes, false, out); }
+
+// A block for an upload of shlo_of_bytes on the copy stream. Upload blocks have
+// a pool of their own: a block goes back to it with an event recorded on the
+// compute stream when it is released (after every read of it queued so far),
+// and the copy stream waits for that event alone before writing it again, so
+// an upload never waits for unrelated compute.
+static int alloc_upload(Device *dev, size_t bytes, Buffer **out) {
+  const size_t want = round_bytes(bytes);
+  void *p = nullptr;
+  size_t got = want;
+  cudaEvent_t ev = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(dev->mu);
+    auto it = dev->upload_free.lower_bound(want);
+    if (it != dev->upload_free.end() && it->first <= want * 2 + 65536) {
+      got = it->first;
+      p = it->second.first;
+      ev = it->second.second;
+      dev->upload_free.erase(it);
+    }
+  }
+  if (p) {
+    cudaError_t e = cudaSuccess;
+    if (!ev) {  // released without an event: after everything queued so far
+      e = cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+      if (e == cudaSuccess) e = cudaEventRecord(ev, dev->stream);
+    }
+    if (e == cudaSuccess) e = cudaStreamWaitEvent(dev->copy, ev, 0);
+    if (ev) cudaEventDestroy(ev);
+    if (e != cudaSuccess) {
+      cudaFree(p);
+      return cuda_check(e, "ofBytes: upload block");
+    }
+  } else {
+    SHLO_CUDA(cudaMalloc(&p, want));
+  }
+  Buffer *b = new Buffer();
+  b->dev = dev;
+  b->ptr = p;
+  b->bytes = got;
+  b->upload = true;
+  *out = b;
+  return 0;
+}
 int buffer_alloc_constant(Device *dev, size_t bytes, Buffer **out) { return alloc_block(dev, bytes, true, out); }
 
 void buffer_retain(Buffer *b) {
@@ -212,9 +256,21 @@ void buffer_release(Buffer *b) {
   if (b->rc.fetch_sub(1) != 1) return;
   for (auto &kv : b->derived) buffer_release(kv.second);
   Device *dev = b->dev;
+  // An upload block's release event (none while a capture records on the
+  // stream: the next upload into the block then waits for the whole stream).
+  cudaEvent_t freed = nullptr;
+  if (b->upload && !dev->capturing &&
+      (cudaEventCreateWithFlags(&freed, cudaEventDisableTiming) != cudaSuccess ||
+       cudaEventRecord(freed, dev->stream) != cudaSuccess)) {
+    cudaGetLastError();
+    if (freed) cudaEventDestroy(freed);
+    freed = nullptr;
+  }
   {
     std::lock_guard<std::mutex> lk(dev->mu);
-    if (!b->graph_owner) {
+    if (b->upload) {
+      dev->upload_free.emplace(b->bytes, std::make_pair(b->ptr, freed));
+    } else if (!b->graph_owner) {
       dev->free_blocks.emplace(b->bytes, b->ptr);
       dev->pooled_bytes += b->bytes;
     } else if (dev->capturing && dev->capture_owner == b->graph_owner && !b->no_recycle) {
@@ -506,11 +562,31 @@ int shlo_of_bytes(const void *data, size_t nbytes, const int64_t *shape, int ndi
     *out = a;
     return 0;
   }
+  cudaPointerAttributes at;
+  const bool pinned = nbytes && cudaPointerGetAttributes(&at, data) == cudaSuccess && at.type == cudaMemoryTypeHost;
+  cudaGetLastError();
+  if (pinned && nbytes >= ((size_t)1 << 20)) {
+    // A large pinned input: uploaded on the copy stream into an upload block,
+    // beside the compute still queued (the host waits for the copy alone).
+    a = new Arr();
+    a->dtype = dtype;
+    a->ndim = ndim;
+    for (int i = 0; i < ndim; i++) a->shape[i] = shape[i];
+    set_row_major(a);
+    if (alloc_upload(dev, nbytes, &a->buf)) {
+      delete a;
+      return 1;
+    }
+    if (cuda_check(cudaMemcpyAsync(a->buf->ptr, data, nbytes, cudaMemcpyHostToDevice, dev->copy), "ofBytes") ||
+        wait_stream(dev, dev->copy, "ofBytes")) {
+      release_arr(a);
+      return 1;
+    }
+    *out = a;
+    return 0;
+  }
   SHLO_TRY(new_array(dev, dtype, shape, ndim, &a));
   if (nbytes) {
-    cudaPointerAttributes at;
-    bool pinned = cudaPointerGetAttributes(&at, data) == cudaSuccess && at.type == cudaMemoryTypeHost;
-    cudaGetLastError();
     cudaError_t e = cudaMemcpyAsync(a->buf->ptr, data, nbytes, cudaMemcpyHostToDevice, dev->stream);
     if (e == cudaSuccess && pinned) e = cudaStreamSynchronize(dev->stream);  // consumed before return
     if (cuda_check(e, "ofBytes: host to device copy")) {
