@@ -239,6 +239,9 @@ __global__ void __launch_bounds__(at::THREADS, 2) k_attention(AttnArgs a) {
       mx = m;
     }
     mx = __shfl_sync(0xffffffffu, mx, 8 * r);
+    int pmin = 255, pmax = 0;
+    bool pspecial = false;
+    double psum = 0.0;
 #pragma unroll
     for (int t = 0; t < G; t++) {
       float4 y;
@@ -247,11 +250,39 @@ __global__ void __launch_bounds__(at::THREADS, 2) k_attention(AttnArgs a) {
       y.z = ggml_v_expf(__fsub_rn(e[t].z, mx));
       y.w = ggml_v_expf(__fsub_rn(e[t].w, mx));
       e[t] = y;
-      parts[g + 8 * t] = __fadd_rn(__fadd_rn(y.x, y.y), __fadd_rn(y.z, y.w));
+      const float part = __fadd_rn(__fadd_rn(y.x, y.y), __fadd_rn(y.z, y.w));
+      parts[g + 8 * t] = part;
+      // the binades the row's group sums span (all positive or zero)
+      const uint32_t pb = fbits(part) & 0x7FFFFFFFu;
+      const int pe = (int)(pb >> 23);
+      pspecial |= pe == 255;
+      if (pb) {
+        pmin = min(pmin, pe ? pe : 1);
+        pmax = max(pmax, pe ? pe : 1);
+      }
+      psum = __dadd_rn(psum, (double)part);
     }
-    __syncwarp();
+    // When the group sums' nonzero terms span few enough binades, every partial
+    // sum of them is exact in binary64 (multiples of 2^(pmin - 150) below
+    // 2^(pmax - 126 + log2(S / 4))), so the order of the adds cannot matter: the
+    // row's eight lanes add their parts and a shuffle tree gives the spec's sum.
+    // Otherwise one lane runs the spec's serial chain.
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) {
+      pmin = min(pmin, __shfl_xor_sync(0xffffffffu, pmin, o));
+      pmax = max(pmax, __shfl_xor_sync(0xffffffffu, pmax, o));
+    }
+    constexpr int LG = S == 256 ? 6 : 5;  // log2 of the group count
+    const bool exact = (__ballot_sync(0xffffffffu, pspecial) & rowmask) == 0 && (pmin > pmax || pmax - pmin + 24 + LG <= 53);
+    // Every lane takes part in the shuffles and the barrier (the four rows of a
+    // warp may differ in `exact`); the branches below hold no warp collective.
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) psum = __dadd_rn(psum, __shfl_xor_sync(0xffffffffu, psum, o));
+    __syncwarp();  // the parts, for the serial chain
     float inv = 0.0f;
-    if (g == 0) {
+    if (exact) {
+      inv = __double2float_rn(__ddiv_rn(1.0, psum));
+    } else if (g == 0) {
       double sum = 0.0;
       for (int k = 0; k < S / 4; k += 8) {  // eight parts loaded ahead of their serial adds
         double v[8];

@@ -134,6 +134,43 @@ def test_norm(shape):
     assert_bits(got, want, "norm %s" % (shape,))
 
 
+@pytest.mark.parametrize("ncols", [512, 1024, 36])
+def test_norm_wide_and_narrow_ranges(ncols):
+    # rows whose terms span few binades (the sums may be added in any order),
+    # rows just past that span, rows of many binades, zeros and signed zeros,
+    # and rows with an infinity or a NaN (the serial chains)
+    rng = np.random.default_rng(ncols)
+    rows = []
+    for kind in range(12):
+        r = (rng.standard_normal(ncols) * 2).astype(np.float32)
+        if kind == 1:
+            r[rng.integers(0, ncols, 3)] = np.float32(1e-6)   # about 20 binades below the rest
+        elif kind == 2:
+            r[rng.integers(0, ncols, 3)] = np.float32(3e-8)   # past the span: serial
+        elif kind == 3:
+            r = (rng.standard_normal(ncols) * np.float32(2.0) ** rng.integers(-60, 60, ncols)).astype(np.float32)
+        elif kind == 4:
+            r[:] = 0.0
+            r[::3] = -0.0
+        elif kind == 5:
+            r[rng.integers(0, ncols)] = np.inf
+        elif kind == 6:
+            r[rng.integers(0, ncols)] = np.nan
+        elif kind == 7:
+            r[:] = np.float32(1e-41)  # subnormals
+            r[0] = np.float32(1.0)
+        elif kind == 8:
+            r = np.full(ncols, np.float32(7.25))
+        elif kind == 9:
+            r[rng.integers(0, ncols, 5)] = np.float32(3e37)
+        rows.append(r)
+    x = np.stack(rows).astype(np.float32)
+    eps = 0x3727C5AC
+    got = M.to_numpy(Run.norm(M.of_numpy(x), ncols, x.shape[0], eps))
+    want = O.norm(x, ncols, x.shape[0], float(np.array([eps], np.uint32).view(np.float32)[0]))
+    assert_bits(got, want, "norm ranges %d" % ncols)
+
+
 def specials32(n=1 << 16, seed=1):
     rng = np.random.default_rng(seed)
     s = rng.integers(0, 2**32, n, dtype=np.uint64).astype(np.uint32)
