@@ -563,6 +563,12 @@ __global__ void g_soft_max(const float *__restrict__ x, float *__restrict__ y, i
     }
     double sum = 0.0;
     float fs = 0.0f;
+    // With the row in registers (G > 0), the group sums' binades: when every
+    // partial sum of them is exact in binary64 (see exact_sum), the lanes add
+    // their own parts and a shuffle tree replaces lane 0's chain.
+    int pmin = 255, pmax = 0;
+    bool pspecial = false;
+    double psum = 0.0;
     // Chunks of 32*max(G,8) groups: parts into shared memory, lane 0 chains them.
     const int chunk = 32 * (G > 0 ? G : 8);
     for (int c0 = 0; c0 < ng; c0 += chunk) {
@@ -585,11 +591,39 @@ __global__ void g_soft_max(const float *__restrict__ x, float *__restrict__ y, i
           if (G > 0) v[i] = e;
           else yr[gi] = e;
           // widened here, by every lane, so lane 0's chain is adds alone
-          parts[lane + 32 * i] = (double)__fadd_rn(__fadd_rn(e.x, e.y), __fadd_rn(e.z, e.w));
+          const float part = __fadd_rn(__fadd_rn(e.x, e.y), __fadd_rn(e.z, e.w));
+          parts[lane + 32 * i] = (double)part;
+          if (G > 0) {
+            const uint32_t pb = fbits(part) & 0x7FFFFFFFu;
+            const int pe = (int)(pb >> 23);
+            pspecial |= pe == 255;
+            if (pb) {
+              pmin = min(pmin, pe ? pe : 1);
+              pmax = max(pmax, pe ? pe : 1);
+            }
+            psum = __dadd_rn(psum, (double)part);
+          }
         }
       }
       __syncwarp();
-      if (lane == 0) {
+      // Nonzero terms with exponent fields in [pmin, pmax] are multiples of
+      // 2^(pmin - 150) below 2^(pmax - 126); ng of them sum, in any order, to
+      // multiples of 2^(pmin - 150) below 2^(pmax - 126 + ceil(log2 ng)), all
+      // exact in binary64 when pmax - pmin + 24 + ceil(log2 ng) <= 53. (G > 0:
+      // one chunk holds the whole row. Not for the planted float chain.)
+      bool exact = false;
+      if (G > 0) {
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          pmin = min(pmin, __shfl_xor_sync(0xffffffffu, pmin, o));
+          pmax = max(pmax, __shfl_xor_sync(0xffffffffu, pmax, o));
+          psum = __dadd_rn(psum, __shfl_xor_sync(0xffffffffu, psum, o));
+        }
+        const int lg = ng > 1 ? 32 - __clz(ng - 1) : 0;
+        exact = !float_sum && !__any_sync(0xffffffffu, pspecial) && (pmin > pmax || pmax - pmin + 24 + lg <= 53);
+        if (exact) sum = psum;
+      }
+      if (lane == 0 && !exact) {
         int n = ng - c0 < chunk ? ng - c0 : chunk;
         if (float_sum) {
           for (int k = 0; k < n; k++) fs = __fadd_rn(fs, (float)parts[k]);

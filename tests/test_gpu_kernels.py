@@ -118,6 +118,26 @@ def test_soft_max(shape):
         assert_bits(got, want, "soft_max %s scale %08x" % (shape, scale))
 
 
+@pytest.mark.parametrize("ncols", [256, 1024, 2048, 100])
+@pytest.mark.parametrize("amp", [0.05, 1.0, 3.0, 40.0])
+def test_soft_max_binade_spans(ncols, amp):
+    # small amplitudes keep a row's group sums within a few binades (added in any
+    # order), large ones spread them (the serial chain); rows of -inf, zeros,
+    # equal values, a NaN and an infinity mixed in
+    rng = np.random.default_rng(ncols * 7 + int(amp * 100))
+    x = (rng.standard_normal((40, ncols)) * amp).astype(np.float32)
+    x[1] = 0.0
+    x[2] = np.float32(3.5)
+    x[3, rng.integers(0, ncols, 10)] = -np.inf
+    x[4, 5] = np.nan
+    x[5, 7] = np.inf
+    x[6, :] = -np.inf
+    x[6, 3] = 0.0
+    got = M.to_numpy(Run.soft_max(M.of_numpy(x), ncols, 40, 0x3F800000))
+    want = O.soft_max(x, ncols, 40, 1.0)
+    assert_bits(got, want, "soft_max spans %d %g" % (ncols, amp))
+
+
 def test_soft_max_refuses_tail():
     x = M.of_numpy(np.zeros((2, 13), np.float32))
     with pytest.raises(M.ShloError, match="not carried"):
