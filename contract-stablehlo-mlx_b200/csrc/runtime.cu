@@ -565,9 +565,10 @@ int shlo_of_bytes(const void *data, size_t nbytes, const int64_t *shape, int ndi
   cudaPointerAttributes at;
   const bool pinned = nbytes && cudaPointerGetAttributes(&at, data) == cudaSuccess && at.type == cudaMemoryTypeHost;
   cudaGetLastError();
-  if (pinned && nbytes >= ((size_t)1 << 20)) {
-    // A large pinned input: uploaded on the copy stream into an upload block,
-    // beside the compute still queued (the host waits for the copy alone).
+  if (pinned && nbytes > 256) {
+    // A pinned input (above the size whose bytes are also kept on the host):
+    // uploaded on the copy stream into an upload block, beside the compute
+    // still queued (the host waits for the copy alone).
     a = new Arr();
     a->dtype = dtype;
     a->ndim = ndim;

@@ -1,4 +1,4 @@
-"""Host transfers beside compute: large pinned inputs of ofBytes are uploaded on
+"""Host transfers beside compute: pinned inputs of ofBytes (above 256 bytes) are uploaded on
 the library's copy stream into blocks of their own pool, and toBytes reads a
 compiled function's result on the copy stream after that result's ready event,
 so both run while other work is queued on the compute stream. These tests
@@ -80,3 +80,26 @@ def test_pipelined_readback_of_compiled_results():
     for g, x in zip(got, xs):
         want = M.to_numpy(step([w, M.of_numpy(x)])[0]).reshape(R, Mm)
         assert np.array_equal(bits(g), bits(want))
+
+
+def test_small_uploads_beside_queued_compute():
+    # small pinned inputs (a timestep embedding's size) take the upload path too:
+    # each is added to a product still queued on the compute stream
+    rng = np.random.default_rng(5)
+    K, Mm, R = 512, 512, 4096
+    w = M.of_numpy((rng.standard_normal((Mm, K)) * 0.05).astype(np.float32))
+    x = M.of_numpy(rng.standard_normal((R, K)).astype(np.float32))
+    small = torch.empty(Mm, dtype=torch.float32).pin_memory()
+    outs, wants = [], []
+    for i in range(8):
+        y = Run.mul_mat(w, x, K, Mm, R, R, 0)  # queued
+        v = rng.standard_normal(Mm).astype(np.float32)
+        small.copy_(torch.from_numpy(v))
+        b = upload(small)
+        outs.append(M.binary(M.opAdd, M.reshape(y, [R, Mm]), M.broadcast(M.reshape(b, [1, Mm]), [R, Mm])))
+        wants.append(v)
+        del b
+    y = M.to_numpy(Run.mul_mat(w, x, K, Mm, R, R, 0)).reshape(R, Mm)
+    for o, v in zip(outs, wants):
+        want = (y + v[None, :]).astype(np.float32)
+        assert np.array_equal(bits(M.to_numpy(o)), bits(want))
