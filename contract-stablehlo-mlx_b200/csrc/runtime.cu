@@ -183,6 +183,12 @@ static int alloc_block(Device *dev, size_t bytes, bool constant, Buffer **out) {
       for (auto &kv : dev->free_blocks) cudaFree(kv.second);
       dev->free_blocks.clear();
       dev->pooled_bytes = 0;
+      // idle upload blocks too (their release events are behind the synchronize)
+      for (auto &kv : dev->upload_free) {
+        if (kv.second.second) cudaEventDestroy(kv.second.second);
+        cudaFree(kv.second.first);
+      }
+      dev->upload_free.clear();
       e = cudaMalloc(&p, want);
       if (e != cudaSuccess) return cuda_check(e, "cudaMalloc");
     }
