@@ -896,6 +896,134 @@ __global__ void k_affine_rows(float *y, int64_t n, int ncols, const float *gamma
   }
 }
 
+// One warp a row, for rows of 128 c (c <= 8) values held in registers: lane l
+// holds the four-value groups l, l + 32, ..., so each 16-byte load is a group.
+// Each binary64 sum (the values; then the group sums) is reassociated only when
+// no partial sum can round: nonzero binary32 terms whose exponent fields lie in
+// [emin, emax] are multiples of 2^(emin - 150) below 2^(emax - 126), so n of
+// them, in any order, stay multiples of 2^(emin - 150) below
+// 2^(emax - 126 + ceil(log2 n)), exact in binary64 when emax - emin + 24 +
+// ceil(log2 n) <= 53; then the lanes add their own terms and a shuffle tree
+// gives the spec's sum. Otherwise (or with an infinity or NaN) the row goes to
+// the warp's shared-memory buffer and lane 0 runs the spec's serial chain.
+// Every warp collective sits outside the per-row branches.
+template <int C>  // float4 groups a lane: ncols = 128 C
+__global__ void __launch_bounds__(128) g_norm_warp(const float *__restrict__ x, float *__restrict__ y, int64_t rows,
+                                                   float eps, const float *__restrict__ gamma,
+                                                   const float *__restrict__ beta) {
+  constexpr int N = 128 * C;
+  __shared__ float buf[4][N];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  float *rowbuf = buf[w];
+  const int lg_n = 32 - __clz(N - 1), lg_g = 32 - __clz(N / 4 - 1);
+  auto span = [&](float v, int &lo, int &hi, bool &sp) {
+    const uint32_t b = fbits(v) & 0x7FFFFFFFu;
+    const int e = (int)(b >> 23);
+    sp |= e == 255;
+    if (b) {
+      lo = min(lo, e ? e : 1);
+      hi = max(hi, e ? e : 1);
+    }
+  };
+  auto exact = [&](int lo, int hi, bool sp, int lg) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    return !__any_sync(0xffffffffu, sp) && (lo > hi || hi - lo + 24 + lg <= 53);
+  };
+  for (int64_t row = (int64_t)blockIdx.x * 4 + w; row < rows; row += (int64_t)gridDim.x * 4) {
+    const float4 *xr = reinterpret_cast<const float4 *>(x + row * N);
+    float4 v[C];
+#pragma unroll
+    for (int c = 0; c < C; c++) v[c] = __ldg(xr + lane + 32 * c);
+    // the row sum
+    int lo = 255, hi = 0;
+    bool sp = false;
+    double sum = 0.0;
+#pragma unroll
+    for (int c = 0; c < C; c++) {
+      span(v[c].x, lo, hi, sp); span(v[c].y, lo, hi, sp); span(v[c].z, lo, hi, sp); span(v[c].w, lo, hi, sp);
+      sum = __dadd_rn(__dadd_rn(__dadd_rn(__dadd_rn(sum, (double)v[c].x), (double)v[c].y), (double)v[c].z),
+                      (double)v[c].w);
+    }
+    const bool ex1 = exact(lo, hi, sp, lg_n);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) sum = __dadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+    if (!ex1) {  // warp-uniform
+#pragma unroll
+      for (int c = 0; c < C; c++) reinterpret_cast<float4 *>(rowbuf)[lane + 32 * c] = v[c];
+      __syncwarp();
+      if (lane == 0) {
+        double s0 = 0.0;
+        for (int k = 0; k < N; k += 8) {  // eight values loaded ahead of their serial adds
+          double t[8];
+#pragma unroll
+          for (int i = 0; i < 8; i++) t[i] = (double)rowbuf[k + i];
+#pragma unroll
+          for (int i = 0; i < 8; i++) s0 = __dadd_rn(s0, t[i]);
+        }
+        sum = s0;
+      }
+      sum = __shfl_sync(0xffffffffu, sum, 0);
+      __syncwarp();
+    }
+    const float mean = __fdiv_rn(__double2float_rn(sum), (float)N);
+    // the group sums of squared deviations
+    float q[C];
+    lo = 255; hi = 0; sp = false;
+    double s2 = 0.0;
+#pragma unroll
+    for (int c = 0; c < C; c++) {
+      const float d0 = __fsub_rn(v[c].x, mean), d1 = __fsub_rn(v[c].y, mean);
+      const float d2 = __fsub_rn(v[c].z, mean), d3 = __fsub_rn(v[c].w, mean);
+      q[c] = __fadd_rn(__fadd_rn(__fmul_rn(d0, d0), __fmul_rn(d1, d1)), __fadd_rn(__fmul_rn(d2, d2), __fmul_rn(d3, d3)));
+      span(q[c], lo, hi, sp);
+      s2 = __dadd_rn(s2, (double)q[c]);
+    }
+    const bool ex2 = exact(lo, hi, sp, lg_g);
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s2 = __dadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, o));
+    if (!ex2) {  // warp-uniform: the group sums in group order
+#pragma unroll
+      for (int c = 0; c < C; c++) rowbuf[lane + 32 * c] = q[c];
+      __syncwarp();
+      if (lane == 0) {
+        double t2 = 0.0;
+        for (int k = 0; k < N / 4; k += 8) {
+          double t[8];
+#pragma unroll
+          for (int i = 0; i < 8; i++) t[i] = (double)rowbuf[k + i];
+#pragma unroll
+          for (int i = 0; i < 8; i++) t2 = __dadd_rn(t2, t[i]);
+        }
+        s2 = t2;
+      }
+      s2 = __shfl_sync(0xffffffffu, s2, 0);
+      __syncwarp();
+    }
+    const float var = __double2float_rn(__ddiv_rn(s2, (double)N));
+    const float scl = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    float4 *yr = reinterpret_cast<float4 *>(y + row * N);
+#pragma unroll
+    for (int c = 0; c < C; c++) {
+      float4 o;
+      o.x = arm_nan(__fmul_rn(__fsub_rn(v[c].x, mean), scl));
+      o.y = arm_nan(__fmul_rn(__fsub_rn(v[c].y, mean), scl));
+      o.z = arm_nan(__fmul_rn(__fsub_rn(v[c].z, mean), scl));
+      o.w = arm_nan(__fmul_rn(__fsub_rn(v[c].w, mean), scl));
+      if (gamma) {  // the executor's fused affine: (y * gamma) + beta, each rounded alone
+        const float4 g = __ldg(reinterpret_cast<const float4 *>(gamma) + lane + 32 * c);
+        const float4 b = __ldg(reinterpret_cast<const float4 *>(beta) + lane + 32 * c);
+        o = make_float4(__fadd_rn(__fmul_rn(o.x, g.x), b.x), __fadd_rn(__fmul_rn(o.y, g.y), b.y),
+                        __fadd_rn(__fmul_rn(o.z, g.z), b.z), __fadd_rn(__fmul_rn(o.w, g.w), b.w));
+      }
+      yr[lane + 32 * c] = o;
+    }
+  }
+}
+
 int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out) { return k_norm_affine(dev, x, p, nullptr, nullptr, out); }
 
 int k_norm_affine(Device *dev, Arr *x, const uint32_t *p, Arr *gamma, Arr *beta, Arr **out) {
@@ -916,7 +1044,27 @@ int k_norm_affine(Device *dev, Arr *x, const uint32_t *p, Arr *gamma, Arr *beta,
   const size_t smem = (size_t)NORM_ROWS * (ncols + 1) * sizeof(float);
   const bool aligned = (((uintptr_t)data_ptr(x)) & 15) == 0 &&
                        (!affine || ((((uintptr_t)gp) | ((uintptr_t)bp)) & 15) == 0);
-  if (ncols * rows > 0 && p[3] == 0 && ncols % 4 == 0 && ncols <= 1024 && aligned) {
+  if (ncols * rows > 0 && p[3] == 0 && ncols % 128 == 0 && ncols <= 1024 && aligned) {
+    // one warp a row, the row in registers
+    int64_t blocks = (rows + 3) / 4;
+    if (blocks > (int64_t)dev->sm_count * 32) blocks = (int64_t)dev->sm_count * 32;
+    const float *xp = (const float *)data_ptr(x);
+    float *yp = (float *)o->buf->ptr;
+    switch (ncols / 128) {
+      case 1: g_norm_warp<1><<<(unsigned)blocks, 128, 0, dev->stream>>>(xp, yp, rows, eps, gp, bp); break;
+      case 2: g_norm_warp<2><<<(unsigned)blocks, 128, 0, dev->stream>>>(xp, yp, rows, eps, gp, bp); break;
+      case 3: g_norm_warp<3><<<(unsigned)blocks, 128, 0, dev->stream>>>(xp, yp, rows, eps, gp, bp); break;
+      case 4: g_norm_warp<4><<<(unsigned)blocks, 128, 0, dev->stream>>>(xp, yp, rows, eps, gp, bp); break;
+      case 5: g_norm_warp<5><<<(unsigned)blocks, 128, 0, dev->stream>>>(xp, yp, rows, eps, gp, bp); break;
+      case 6: g_norm_warp<6><<<(unsigned)blocks, 128, 0, dev->stream>>>(xp, yp, rows, eps, gp, bp); break;
+      case 7: g_norm_warp<7><<<(unsigned)blocks, 128, 0, dev->stream>>>(xp, yp, rows, eps, gp, bp); break;
+      default: g_norm_warp<8><<<(unsigned)blocks, 128, 0, dev->stream>>>(xp, yp, rows, eps, gp, bp); break;
+    }
+    if (launch_check("norm")) {
+      shlo_release(o);
+      return 1;
+    }
+  } else if (ncols * rows > 0 && p[3] == 0 && ncols % 4 == 0 && ncols <= 1024 && aligned) {
     static bool attr_done[64] = {false};
     if (!attr_done[dev->id]) {
       if (cuda_check(cudaFuncSetAttribute(g_norm_rows, cudaFuncAttributeMaxDynamicSharedMemorySize,
