@@ -721,25 +721,30 @@ __global__ void k_binary(int op, Iter it, Operand x, Operand y, Operand z) {
   }
 }
 
-// binary32 operands and result laid out as [rows, cols] with cols % 4 == 0:
-// each operand walks its columns contiguously (a row segment, stride 1) or not
-// at all (one value per row, stride 0), and rows at any stride. Four elements
-// per thread with 16-byte accesses: the layout of bias adds, norm affines and
-// residual adds.
+// binary32 operands and result laid out as [planes, rows, cols] with
+// cols % 4 == 0: each operand walks its columns contiguously (a row segment,
+// stride 1) or not at all (one value per row, stride 0), and rows and planes at
+// any stride. Four elements per thread with 16-byte accesses: the layout of
+// bias adds, norm affines, residual adds and per-sample broadcasts
+// ([B, S, D] + [B, 1, D]).
 struct VecOperand {
   const float *p;
-  int64_t row;  // row stride, floats
-  int col;      // 1 = contiguous columns, 0 = one value per row
+  int64_t plane;  // plane stride, floats
+  int64_t row;    // row stride, floats
+  int col;        // 1 = contiguous columns, 0 = one value per row
 };
 
-__global__ void k_binary_f32v(int op, uint32_t nv, uint32_t colsv, VecOperand a, VecOperand b, float4 *__restrict__ y) {
+__global__ void k_binary_f32v(int op, uint32_t nv, uint32_t colsv, uint32_t rows, VecOperand a, VecOperand b,
+                              float4 *__restrict__ y) {
   GRID_LOOP(uint32_t, v, nv) {
-    uint32_t r = v / colsv, c = (v - r * colsv) * 4;
+    const uint32_t r = v / colsv, c = (v - r * colsv) * 4;
+    const uint32_t pl = r / rows, rr = r - pl * rows;
+    const float *ap = a.p + pl * a.plane + rr * a.row, *bp = b.p + pl * b.plane + rr * b.row;
     float4 u, w;
-    if (a.col) u = *reinterpret_cast<const float4 *>(a.p + r * a.row + c);
-    else u.x = u.y = u.z = u.w = a.p[r * a.row];
-    if (b.col) w = *reinterpret_cast<const float4 *>(b.p + r * b.row + c);
-    else w.x = w.y = w.z = w.w = b.p[r * b.row];
+    if (a.col) u = *reinterpret_cast<const float4 *>(ap + c);
+    else u.x = u.y = u.z = u.w = *ap;
+    if (b.col) w = *reinterpret_cast<const float4 *>(bp + c);
+    else w.x = w.y = w.z = w.w = *bp;
     float4 o;
     o.x = binary_float(op, u.x, w.x);
     o.y = binary_float(op, u.y, w.y);
@@ -749,31 +754,37 @@ __global__ void k_binary_f32v(int op, uint32_t nv, uint32_t colsv, VecOperand a,
   }
 }
 
-// The vectorized layout of `it`'s operands, when it applies.
-static bool vec_layout(const Iter &it, const Operand *ops, int nin, uint32_t &rows, uint32_t &cols, VecOperand *vo) {
-  if (it.ndim > 2 || it.n >= ((int64_t)1 << 31)) return false;
+// The vectorized layout of `it`'s operands, when it applies (at most three
+// axes after collapsing; `rows` counts the rows of one plane).
+static bool vec_layout(const Iter &it, const Operand *ops, int nin, uint32_t &planes, uint32_t &rows, uint32_t &cols,
+                       VecOperand *vo) {
+  if (it.ndim < 1 || it.ndim > 3 || it.n >= ((int64_t)1 << 31)) return false;
   const int last = it.ndim - 1;
-  int64_t C = it.shape[last];
+  const int64_t C = it.shape[last];
+  const int64_t R = it.ndim >= 2 ? it.shape[last - 1] : 1;
   if (C % 4) return false;
   for (int k = 0; k <= nin; k++) {
     if (ops[k].dtype != kF32) return false;
-    int64_t cs = ops[k].strides[last];
-    int64_t rs = it.ndim == 2 ? ops[k].strides[0] : 0;
+    const int64_t cs = ops[k].strides[last];
+    const int64_t rs = it.ndim >= 2 ? ops[k].strides[last - 1] : 0;
+    const int64_t ps = it.ndim == 3 ? ops[k].strides[0] : 0;
     if (k == nin) {  // the output: row-major
-      if (cs != 1 || (it.ndim == 2 && rs != C)) return false;
+      if (cs != 1 || (it.ndim >= 2 && rs != C) || (it.ndim == 3 && ps != R * C)) return false;
       if (!aligned(ops[k].ptr, 16)) return false;
       continue;
     }
     if (cs == 1) {
-      if (rs % 4 || !aligned(ops[k].ptr, 16)) return false;
+      if (rs % 4 || ps % 4 || !aligned(ops[k].ptr, 16)) return false;
     } else if (cs != 0) {
       return false;
     }
     vo[k].p = reinterpret_cast<const float *>(ops[k].ptr);
+    vo[k].plane = ps;
     vo[k].row = rs;
     vo[k].col = cs == 1;
   }
-  rows = (uint32_t)(it.n / C);
+  rows = (uint32_t)R;
+  planes = (uint32_t)(it.n / (R * C));
   cols = (uint32_t)C;
   return true;
 }
@@ -811,11 +822,11 @@ int op_binary(uint32_t op, Arr *a, Arr *b, Arr **out) {
     prepare_iter(o, ins, 2, it, ops);
     if (it.n > 0) {
       unsigned g = grid_for(it.n, 256, dev, 16);
-      uint32_t vr, vc;
+      uint32_t vp, vr, vc;
       VecOperand vo[2];
-      if (!is_compare(op) && vec_layout(it, ops, 2, vr, vc, vo)) {
-        uint32_t nv = vr * (vc / 4);
-        k_binary_f32v<<<grid_for(nv, 256, dev, 16), 256, 0, dev->stream>>>((int)op, nv, vc / 4, vo[0], vo[1],
+      if (!is_compare(op) && vec_layout(it, ops, 2, vp, vr, vc, vo)) {
+        uint32_t nv = vp * vr * (vc / 4);
+        k_binary_f32v<<<grid_for(nv, 256, dev, 16), 256, 0, dev->stream>>>((int)op, nv, vc / 4, vr, vo[0], vo[1],
                                                                           (float4 *)ops[2].ptr);
       } else {
         by_rank(it, [&](auto ndc, auto ic) {

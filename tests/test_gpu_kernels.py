@@ -320,3 +320,39 @@ def test_builtins_against_numpy():
     assert np.array_equal(M.to_numpy(h), a.astype(np.float16))
     bc = M.broadcast(M.of_numpy(b), [2, 3, 4])
     assert np.array_equal(M.to_numpy(bc), np.broadcast_to(b, (2, 3, 4)))
+
+
+@pytest.mark.parametrize("bshape", [(6, 1, 8), (1, 5, 8), (6, 5, 1), (6, 1, 1), (1, 1, 8), (6, 5, 8)])
+@pytest.mark.parametrize("op", ["add", "sub", "mul", "div", "max"])
+def test_binary_three_axis_layouts(bshape, op):
+    """f32 binary ops over [planes, rows, cols] with one operand broadcast along
+    any axis or transposed (the 16-byte-access path), on both operand sides,
+    against the same op over column-strided copies of the operands (the
+    general strided path) bit for bit, and against numpy's IEEE results for
+    the correctly rounded ops (MLX's divide is the GPU's approximate division,
+    within 2 ulp)."""
+    rng = np.random.default_rng(7)
+    a = rng.standard_normal((6, 5, 8)).astype(np.float32)
+    b = (rng.standard_normal(bshape) + 3.0).astype(np.float32)
+    code = {"add": M.opAdd, "sub": M.opSub, "mul": M.opMul, "div": M.opDiv, "max": M.opMax}[op]
+    f = {"add": np.add, "sub": np.subtract, "mul": np.multiply, "div": np.divide, "max": np.maximum}[op]
+
+    def strided(x):  # the same values at column stride 2
+        w = np.zeros(x.shape[:-1] + (2 * x.shape[-1],), np.float32)
+        w[..., ::2] = x
+        nd = x.ndim
+        return M.slice_(M.of_numpy(w), [0] * nd, list(w.shape), [1] * (nd - 1) + [2])
+
+    at = np.ascontiguousarray(a.transpose(1, 0, 2))
+    tv = M.transpose(M.of_numpy(at), [1, 0, 2])  # planes walked at a stride, columns contiguous
+    for x, y, xm, ym, what in ((a, b, M.of_numpy(a), M.of_numpy(b), "a,b"), (b, a, M.of_numpy(b), M.of_numpy(a), "b,a"),
+                               (a, b, tv, M.of_numpy(b), "at,b")):
+        got = M.to_numpy(M.binary(code, xm, ym))
+        ref = M.to_numpy(M.binary(code, strided(x), strided(y)))
+        assert_bits(got, ref, "%s %s %s vs strided" % (op, what, bshape))
+        with np.errstate(all="ignore"):
+            want = f(x, y)
+        if op == "div":
+            assert np.all(np.abs(got.view(np.int32).astype(np.int64) - want.view(np.int32).astype(np.int64)) <= 2)
+        else:
+            assert_bits(got, want, "%s %s %s" % (op, what, bshape))
