@@ -215,6 +215,25 @@ def test_silu_and_gelu():
     assert_bits(got, want, "gelu_erf")
 
 
+@pytest.mark.parametrize("tail", [0, 1, 4, 5, 7])
+def test_gelu_polynomial_range(tail):
+    """gelu_erf where erff runs its polynomials (|x| / sqrt(2) below 4): a
+    strided sweep of every binade from 2^-40 to 6.5 on both signs (both
+    polynomial forms, the rows' edges, the slow path's rare inputs by chance),
+    the FFN's own N(0, 0.45) values, and lengths whose last values take the
+    one-float4 and scalar tails; bit for bit against the oracle."""
+    lo, hi = 0x2B800000, 0x40D00000
+    sweep = np.arange(lo, hi, 97, dtype=np.uint32)
+    pos = sweep.view(np.float32)
+    rng = np.random.default_rng(11)
+    x = np.concatenate([pos, -pos, (rng.standard_normal(1 << 20) * 0.45).astype(np.float32)])
+    x = x[: (x.size // 8) * 8 + tail] if tail else x[: (x.size // 8) * 8 - 8]
+    got = M.to_numpy(Run.gelu_erf(M.of_numpy(x), x.size))
+    assert_bits(got, O.gelu_erf(x), "gelu_erf tail %d" % tail)
+    small = x[: 8 + tail]
+    assert_bits(M.to_numpy(Run.gelu_erf(M.of_numpy(small), small.size)), O.gelu_erf(small), "gelu_erf small")
+
+
 def test_gelu_stock_is_refused():
     M.set_flavor("stock")
     with pytest.raises(M.ShloError, match="not carried"):
