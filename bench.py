@@ -1,20 +1,25 @@
 """Benchmark: bit-exact motion-denoiser steps on B200, through the executor's
 C ABI (BASELINE.json metric; configuration 5).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch-per-gpu B] [--impl shlo|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--global-batch G | --batch-per-gpu B]
+                    [--impl shlo|reference]
 
-One process per GPU (torchrun for N > 1). Each rank runs the whole 8-layer
-denoiser module on its own shard of the batch (weak scaling; there is no
-data-path collective: samples are independent). The control plane (barrier,
-max over ranks) is torch.distributed over gloo.
+One process per GPU (torchrun for N > 1). By default the global batch G = 512
+(the largest of configuration 5's sweep) is split over the ranks (strong
+scaling); --batch-per-gpu B gives every rank B samples instead (weak scaling).
+Each rank runs the whole 8-layer denoiser module on its share: samples are
+independent, so there is no data-path collective. The control plane (barrier,
+max over ranks) is torch.distributed over gloo; the one data collective is the
+final gather of the results to rank 0 over NCCL, inside the end-to-end loop.
 
 value: sample-steps/s of the whole job with inputs already on the device, timed
 with CUDA events on the library's stream, max over ranks. e2e: the same through
-the public API with the inputs copied from pinned host memory every step and
-the step's output read back to the host. roofline: the dominant kernel
-(mul_mat, ggml_vec_dot_f32 order on FP32 CUDA cores) against the measured
-cuBLAS SGEMM throughput of this GPU. cpu_baseline / --impl reference: the C
-oracle (this repo's restatement of ggml-cpu's arm64 order) on the host cores.
+the public API with every step's inputs copied from pinned host memory and the
+step's whole result brought to rank 0's host memory (gathered over NCCL for
+N > 1). roofline: the dominant kernel (mul_mat, ggml_vec_dot_f32 order on FP32
+CUDA cores) against the FP32 CUDA-core peak at the SM clock sampled during the
+timed region. cpu_baseline / --impl reference: the C oracle (this repo's
+restatement of ggml-cpu's arm64 order) on the host cores.
 """
 from __future__ import annotations
 
@@ -46,10 +51,12 @@ def parse_args():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
-    ap.add_argument("--batch-per-gpu", type=int, default=64)
+    ap.add_argument("--global-batch", type=int, default=512)
+    ap.add_argument("--batch-per-gpu", type=int, default=0, help="weak scaling: this many samples on every GPU")
     ap.add_argument("--layers", type=int, default=8)
     ap.add_argument("--impl", default="shlo", choices=["shlo", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-single-thread", action="store_true", help="skip the single-thread CPU leg")
     # Short runs to wrap in a profiler (no JSON line): one warm denoiser step,
     # mul_mat alone at --mm-shape K,M,R[,N], or every exact kernel once (batch 16).
     ap.add_argument("--profile-run", choices=["step", "mul_mat", "kernels", "attention"])
@@ -175,15 +182,22 @@ def measured_peaks() -> dict:
 
 
 def profile_traffic(name: str):
-    """dram bytes per launch from a committed ncu summary (profiles/<name>), or None."""
+    """DRAM bytes per launch of the dominant kernel, and where the figure comes
+    from: the ncu capture summarised in profiles/<name> (bench.py cannot run
+    ncu itself), with the commit its build was captured at."""
     path = os.path.join(ROOT, "profiles", name)
+    val, commit, launch = None, None, None
     try:
         for line in open(path):
             if line.startswith("dram_bytes_per_launch:"):
-                return float(line.split(":", 1)[1].split()[0])
+                val = float(line.split(":", 1)[1].split()[0])
+            elif line.startswith("capture_commit:"):
+                commit = line.split(":", 1)[1].strip()
+            elif line.startswith("capture_launch:"):
+                launch = line.split(":", 1)[1].strip()
     except OSError:
         pass
-    return None
+    return val, "ncu capture of %s (profiles/%s), build of commit %s" % (launch or "k_mul_mat_tm", name, commit or "?")
 
 
 # ------------------------------------------------------------ our arm ----
@@ -299,27 +313,109 @@ def time_kernels(timer, suite, n: int, hbm_gbs: float) -> dict:
     return res
 
 
+def shard_of(args, ws: int, rank: int):
+    """(global batch, this rank's [lo, hi) of it, scaling). Strong scaling by
+    default: the global batch is fixed and split over the ranks; with
+    --batch-per-gpu every rank takes that many samples (weak scaling)."""
+    from shlo import shard as S
+    if args.batch_per_gpu:
+        G = args.batch_per_gpu * ws
+        return G, (rank * args.batch_per_gpu, (rank + 1) * args.batch_per_gpu), "weak"
+    G = args.global_batch
+    return G, S.split(G, ws, rank), "strong"
+
+
+class _DeviceView:
+    """A library array's storage as a CUDA array for torch (no copy)."""
+
+    def __init__(self, ptr: int, n: int):
+        self.__cuda_array_interface__ = {"shape": (n,), "typestr": "<f4", "data": (ptr, False), "version": 3,
+                                         "strides": None, "stream": None}
+
+
+class FinalGather:
+    """The one collective of the job: every rank's result rows to rank 0, as
+    NCCL sends and receives straight from the library's result storage (no
+    kernel reads another GPU's memory), into one global-batch buffer that rank
+    0 then copies to pinned host memory. Ordered after the producing step by an
+    event on the library's stream; the library's stream is ordered after the
+    transfer before the result is released, so its storage is not reused while
+    NCCL still reads it."""
+
+    def __init__(self, torch, dist, group, rank, ws, shares, row_elems, lib_stream, device):
+        self.torch, self.dist, self.group, self.rank, self.ws = torch, dist, group, rank, ws
+        self.counts = [(hi - lo) * row_elems for lo, hi in shares]
+        self.offs = [lo * row_elems for lo, _ in shares]
+        self.lib_stream = lib_stream
+        self.device = device
+        self.stream = torch.cuda.Stream(device=device)
+        total = sum(self.counts)
+        self.big = torch.empty(total, dtype=torch.float32, device=device) if rank == 0 else None
+        self.host = torch.empty(total, dtype=torch.float32).pin_memory() if rank == 0 else None
+        self.bytes_in = sum(self.counts[1:]) * 4 if rank == 0 else 0
+
+    def __call__(self, M, arr):
+        t = self.torch
+        ptr, _ = M.device_ptr(arr)
+        ready = t.cuda.Event()
+        ready.record(self.lib_stream)
+        with t.cuda.stream(self.stream):
+            self.stream.wait_event(ready)
+            mine = t.as_tensor(_DeviceView(ptr, self.counts[self.rank]), device=self.device)
+            if self.rank == 0:
+                self.big[: self.counts[0]].copy_(mine)
+                ops = [self.dist.P2POp(self.dist.irecv, self.big[self.offs[k]: self.offs[k] + self.counts[k]], k,
+                                       group=self.group) for k in range(1, self.ws)]
+            else:
+                ops = [self.dist.P2POp(self.dist.isend, mine, 0, group=self.group)]
+            for req in self.dist.batch_isend_irecv(ops):
+                req.wait()
+            done = t.cuda.Event()
+            done.record(self.stream)
+            self.lib_stream.wait_event(done)
+            if self.rank == 0:
+                self.host.copy_(self.big, non_blocking=True)
+
+    def sync(self):
+        self.stream.synchronize()
+
+
+def fp32_nominal_tflops(sm_count: int, sm_mhz: float) -> float:
+    """FP32 CUDA-core peak: every SM issues 128 FFMA lanes a cycle (2 flop each)."""
+    return sm_count * 128 * 2 * sm_mhz * 1e6 / 1e12
+
+
 def run_shlo(args):
     rank, local_rank, ws, dist = dist_init()
     import torch
 
-    import shlo  # noqa: F401  (loads libshlo_cuda)
     from shlo import denoiser as D
     from shlo import exec as E
-    from shlo import mlx as M
+    from shlo import mlx as M  # loads libshlo_cuda (fails loudly without it)
     from shlo import run as Run
 
     torch.cuda.set_device(local_rank)
     M.set_device(local_rank)
     M.set_flavor("pinned")
     cfg = D.Config(layers=args.layers)
-    B = args.batch_per_gpu
+    G, (lo, hi), scaling = shard_of(args, ws, rank)
+    B = hi - lo
+    shares = [shard_of(args, ws, r)[1] for r in range(ws)]
     w = D.init_weights(cfg, seed=1)
-    ins = D.inputs(cfg, B, seed=1 + rank)
+    # The global batch's inputs, seeded once; each rank takes its rows.
+    ins_all = D.inputs(cfg, G, seed=1)
+    ins = [np.ascontiguousarray(a[lo:hi]) for a in ins_all]
+    del ins_all
     W = [M.of_numpy(w[n]) for n, _ in D.weight_specs(cfg)]
     X = [M.of_numpy(a) for a in ins]
     fn = E.prepare(E.load(D.module_text(cfg, B)), None, True)
     timer = EventTimer(M.current_stream(), local_rank)
+    nccl = None
+    if dist is not None:
+        nccl = dist.new_group(backend="nccl")
+        z = torch.zeros(1, device="cuda")
+        dist.all_reduce(z, group=nccl)  # the communicator is set up here, outside any timing
+        torch.cuda.synchronize()
 
     def step():
         return M.apply(fn, X + W)[0]
@@ -346,6 +442,55 @@ def run_shlo(args):
     dt_max = all_max(dist, dt)
     deterministic = bool(np.array_equal(first.view(np.uint32), last.view(np.uint32)))
 
+    # ---- e2e: pinned host inputs copied in every step; the step's result read
+    # back (N = 1), or gathered to rank 0 over NCCL and read back there (N > 1).
+    # Step i's result is read (or gathered) once step i + 1 is queued, so the
+    # transfer overlaps the next step's compute; the last one is timed too.
+    pinned_in = [torch.from_numpy(a).pin_memory() for a in ins]
+    row_elems = cfg.seq * cfg.d
+    gather = FinalGather(torch, dist, nccl, rank, ws, shares, row_elems, timer.stream,
+                         torch.device("cuda", local_rank)) if ws > 1 else None
+    pinned_out = torch.empty(first.shape, dtype=torch.float32).pin_memory() if ws == 1 else None
+    out_bytes = B * row_elems * 4
+
+    def finish(o):
+        if gather is None:
+            M.to_ptr(o, pinned_out.data_ptr(), out_bytes)
+        else:
+            gather(M, o)
+
+    def e2e_steps(n):
+        prev = None
+        for _ in range(n):
+            xs = [M.of_ptr(p.data_ptr(), p.numel() * 4, list(p.shape), M.dtF32) for p in pinned_in]
+            o = M.apply(fn, xs + W)[0]
+            if prev is not None:
+                finish(prev)
+            prev = o
+        finish(prev)
+        if gather is not None:
+            gather.sync()
+
+    e2e_steps(max(args.warmup, 1))
+    barrier(dist)
+    t0 = time.perf_counter()
+    e2e_steps(args.steps)
+    e2e_dt = all_max(dist, time.perf_counter() - t0)
+    barrier(dist)
+    h2d = sum(a.nbytes for a in D.inputs(cfg, 1, seed=1)) * G  # every rank's inputs, whole job
+    d2h = G * row_elems * 4                                       # the whole batch's result, read once
+    # the gathered batch holds every rank's rows as each rank computed them
+    gather_ok = None
+    if ws > 1:
+        import hashlib
+        mine = hashlib.sha256(last.tobytes()).hexdigest()
+        digests = [None] * ws
+        dist.all_gather_object(digests, mine)
+        if rank == 0:
+            host = gather.host.numpy()
+            gather_ok = all(hashlib.sha256(host[gather.offs[k]: gather.offs[k] + gather.counts[k]].tobytes())
+                            .hexdigest() == digests[k] for k in range(ws))
+
     # ---- batch-1 step latency: the module recorded as a CUDA graph (compile
     # enabled, as the executor prepares it) against plain eager calls
     latency = {}
@@ -361,34 +506,9 @@ def run_shlo(args):
         del f1
     del X1
 
-    # ---- e2e: pinned host inputs copied in, output read back, every step
-    pinned_in = [torch.from_numpy(a).pin_memory() for a in ins]
-    pinned_out = torch.empty(first.shape, dtype=torch.float32).pin_memory()
-    h2d = sum(a.numel() * 4 for a in pinned_in)
-    d2h = pinned_out.numel() * 4
-    # Each step's inputs copied in and its result read back; step i's result is
-    # read (on the library's copy stream) once step i + 1 is queued, so the read
-    # overlaps the next step's compute. The last read is inside the timing too.
-    # The same loop runs W steps untimed first (its upload blocks allocated then).
-    def e2e_steps(n):
-        prev = None
-        for _ in range(n):
-            xs = [M.of_ptr(p.data_ptr(), p.numel() * 4, list(p.shape), M.dtF32) for p in pinned_in]
-            o = M.apply(fn, xs + W)[0]
-            if prev is not None:
-                M.to_ptr(prev, pinned_out.data_ptr(), d2h)
-            prev = o
-        M.to_ptr(prev, pinned_out.data_ptr(), d2h)
-
-    e2e_steps(max(args.warmup, 1))
-    barrier(dist)
-    t0 = time.perf_counter()
-    e2e_steps(args.steps)
-    e2e_dt = all_max(dist, time.perf_counter() - t0)
-    barrier(dist)
-
-    # ---- the dominant kernel: mul_mat at a layer's six shapes (four weight
-    # products, then attention's scores and value products, batched per head)
+    # ---- the dominant kernel: mul_mat at a layer's six shapes for this rank's
+    # batch (four weight products, then attention's scores and value products,
+    # batched per head), each launch with its activation pack
     R = B * cfg.seq
     BH = B * cfg.heads
     rng = np.random.default_rng(0)
@@ -397,6 +517,7 @@ def run_shlo(args):
               (cfg.seq, cfg.dh, BH * cfg.seq, cfg.seq, BH)]
     mm_flops, mm_time, mm_launches = 0.0, 0.0, 0
     per_shape = {}
+    weight_flops, weight_time = 0.0, 0.0
     for K, Mm, Rr, Nn, Wb in shapes:
         wa = M.of_numpy(rng.standard_normal((Wb * Mm, K)).astype(np.float32))
         xa = M.of_numpy(rng.standard_normal((Rr, K)).astype(np.float32))
@@ -404,11 +525,14 @@ def run_shlo(args):
         for _ in range(3):
             y = Run.mul_mat(wa, xa, K, Mm, Rr, Nn, wbs)
         M.eval_([y])
-        n = 20
+        n = 10
         t = timer.time(lambda: Run.mul_mat(wa, xa, K, Mm, Rr, Nn, wbs), n)
         mm_flops += 2.0 * K * Mm * Rr * n
         mm_time += t
         mm_launches += n
+        if Wb == 1:
+            weight_flops += 2.0 * K * Mm * Rr * n
+            weight_time += t
         per_shape["%s%dx%dx%d" % ("%dx" % Wb if Wb > 1 else "", Rr // Wb, Mm, K)] = round(
             2.0 * K * Mm * Rr / (t / n) / 1e12, 2)
         del wa, xa, y
@@ -422,12 +546,14 @@ def run_shlo(args):
     t1 = timer.time(lambda: Run.mul_mat(w1, x1, 256, 128, 64, 64, 0), n1)
     cfg1_tflops = 2.0 * 64 * 128 * 256 / (t1 / n1) / 1e12
 
-    kernels = time_kernels(timer, kernel_suite(B, cfg), 10, measured_peaks().get("hbm_gbs"))
+    kernels = time_kernels(timer, kernel_suite(64, cfg), 10, measured_peaks().get("hbm_gbs"))
 
-    peak_sgemm = fp32_peak_tflops(local_rank)
+    sgemm = fp32_peak_tflops(local_rank)
     sm_count = torch.cuda.get_device_properties(local_rank).multi_processor_count
     clocks = clk.summary()
-    nominal = sm_count * 128 * 2 * (clocks.get("sm_max_mhz") or 1965.0) * 1e6 / 1e12
+    sm_mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz") or measured_peaks().get("sm_max_mhz") or 1965.0
+    peak = fp32_nominal_tflops(sm_count, sm_mhz)
+    peak_max = fp32_nominal_tflops(sm_count, clocks.get("sm_max_mhz") or measured_peaks().get("sm_max_mhz") or 1965.0)
 
     if rank != 0:
         if dist is not None:
@@ -435,47 +561,64 @@ def run_shlo(args):
             dist.destroy_process_group()
         return
 
-    # ---- CPU baseline (rank 0, N = 1): the oracle on one sample, all host cores
-    cpu = None
+    # ---- CPU baselines (rank 0, N = 1): the oracle on one sample through every
+    # layer, rows split over all host cores, and on one thread (ggml_ref's mode)
+    cpu = cpu1 = None
     exact0 = None
     if ws == 1 and not args.no_cpu_baseline:
         from oracle import model_oracle as MO
         cores = os.cpu_count() or 1
+        one = [a[:1] for a in ins]
         t = time.perf_counter()
-        ref0 = MO.forward(cfg, w, [a[:1] for a in ins], nthreads=cores)
+        ref0 = MO.forward(cfg, w, one, nthreads=cores)
         cdt = time.perf_counter() - t
         exact0 = bool(np.array_equal(ref0.view(np.uint32), first[:1].view(np.uint32)))
         cpu = {"value": round(1.0 / cdt, 4), "unit": UNIT, "cores": cores, "kind": "port",
                "sample": "one sample (batch 1) through all %d layers on the C oracle, rows split over %d host threads; "
                          "%.1f s" % (cfg.layers, cores, cdt)}
+        if not args.no_single_thread:
+            t = time.perf_counter()
+            MO.forward(cfg, w, one, nthreads=1)
+            cdt1 = time.perf_counter() - t
+            cpu1 = {"value": round(1.0 / cdt1, 4), "unit": UNIT, "cores": 1, "kind": "port",
+                    "sample": "one sample through all %d layers on the C oracle on one thread (ggml_ref's own "
+                              "single-thread mode); %.1f s" % (cfg.layers, cdt1)}
 
-    value = ws * B * args.steps / dt_max
-    flops_step = cfg.flops_per_sample() * B
+    value = G * args.steps / dt_max
+    flops_step = cfg.flops_per_sample() * G
+    traffic, traffic_note = profile_traffic("mul_mat_denoiser_qkv.md")
     line = {
         "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": ws, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dt_max / args.steps * 1e3, 3), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "scaling": scaling, "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded N(0,1) noisy inputs and host sinusoid timestep embeddings, N(0,0.02) random-init weights",
-        "config": {"workload": WORKLOAD, "global_batch": ws * B, "batch_per_gpu": B, "seq_len": cfg.seq,
-                   "layers": cfg.layers, "parallelism": "dp%d (independent batch shards, no collective)" % ws,
-                   "l2": "no flush: per-step working set (100 MB weights + >1 GB activations at batch 64) exceeds the 126 MB L2",
-                   "ggml_build": "pinned"},
-        "model_tflops": round(flops_step * args.steps * ws / dt_max / 1e12, 2),
+        "config": config_of(cfg, G, ws, scaling),
+        "batch_per_gpu": B,
+        "model_tflops": round(flops_step * args.steps / dt_max / 1e12, 2),
         "roofline": {"bound": "fp32-cuda-core", "kernel": "mul_mat (k_mm_pack of x + k_mul_mat_tm)",
-                     "achieved": round(mm_tflops, 2), "peak": round(peak_sgemm, 2), "unit": "TFLOP/s",
-                     "frac": round(mm_tflops / peak_sgemm, 3),
-                     "peak_source": "measured cuBLAS SGEMM (TF32 off), 8192^3, this GPU, this run",
-                     "peak_nominal": round(nominal, 1), "frac_of_nominal": round(mm_tflops / nominal, 3),
+                     "achieved": round(mm_tflops, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
+                     "frac": round(mm_tflops / peak, 3),
+                     "peak_source": "FP32 CUDA-core peak: %d SMs x 128 FFMA lanes x 2 flop x %.0f MHz (median SM clock "
+                                    "sampled during the timed region; MEASURED_PEAKS.json has no FP32 figure)"
+                                    % (sm_count, sm_mhz),
+                     "peak_at_max_clock": round(peak_max, 2), "frac_at_max_clock": round(mm_tflops / peak_max, 3),
+                     "weight_products_tflops": round(weight_flops / weight_time / 1e12, 2),
+                     "sgemm_tflops": round(sgemm, 2),
+                     "sgemm_note": "cuBLAS SGEMM (TF32 off) 8192^3 on this GPU in this run, a side note: not the peak",
                      "per_shape": per_shape,
-                     "traffic": profile_traffic("mul_mat_denoiser_qkv.md"),
-                     "traffic_launch": "k_mul_mat_tm at 16384x1536x512 (ncu capture)"},
+                     "traffic": traffic, "traffic_source": traffic_note},
         "kernels": kernels,
         "dot_general": {"config1_64x256x128_tflops": round(cfg1_tflops, 4),
                         "config1_us_per_call": round(t1 / n1 * 1e6, 2),
                         "denoiser_shapes_tflops": round(mm_tflops, 2)},
         "cpu_baseline": cpu,
-        "e2e": {"value": round(ws * B * args.steps / e2e_dt, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
-                "d2h_bytes_per_step": d2h},
+        "cpu_baseline_single_thread": cpu1,
+        "e2e": {"value": round(G * args.steps / e2e_dt, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h,
+                "final_gather": None if ws == 1 else {"how": "NCCL send/recv of every rank's result rows to rank 0, "
+                                                             "then one device-to-host copy of the global batch",
+                                                      "nvlink_bytes_per_step": gather.bytes_in,
+                                                      "gathered_equals_ranks_results": gather_ok}},
         "gpu_launches": int(launches),
         "latency_b1_ms": latency,
         "clocks": clocks,
@@ -488,20 +631,34 @@ def run_shlo(args):
         dist.destroy_process_group()
 
 
+def config_of(cfg, G, ws, scaling):
+    return {"workload": WORKLOAD, "global_batch": G, "seq_len": cfg.seq, "layers": cfg.layers,
+            "parallelism": "dp%d (%s scaling: independent batch shards, no collective but the final gather)"
+                           % (ws, scaling),
+            "l2": "no flush: per-step working set (100 MB weights + >1 GB activations) exceeds the 126 MB L2",
+            "ggml_build": "pinned"}
+
+
 # ------------------------------------------------------ the reference arm ----
 
 def run_reference(args):
     """The reference's CPU path for this workload: the C oracle (ggml-cpu's arm64
     order restated; the reference's own ggml_ref cannot be built here), one
-    sample per step through all layers, rows split over every host thread."""
-    if int(os.environ.get("RANK", "0")) != 0:
+    sample of the same global batch per step through all layers, rows split
+    over every host thread. Rank 0 alone runs; the other ranks exit at once.
+    Nothing here maps the CUDA library: `shlo.denoiser` and `shlo.shard` are
+    host-only modules."""
+    rank = int(os.environ.get("RANK", "0"))
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
         return
     from oracle import model_oracle as MO
     from shlo import denoiser as D
 
     cfg = D.Config(layers=args.layers)
+    G, _, scaling = shard_of(args, ws, 0)
     w = D.init_weights(cfg, seed=1)
-    ins = D.inputs(cfg, 1, seed=1)
+    ins = [a[:1] for a in D.inputs(cfg, 1, seed=1)]
     cores = os.cpu_count() or 1
     for _ in range(args.warmup):
         MO.forward(cfg, w, ins, nthreads=cores)
@@ -510,13 +667,14 @@ def run_reference(args):
         MO.forward(cfg, w, ins, nthreads=cores)
     dt = time.perf_counter() - t
     v = args.steps / dt
-    line = {"metric": METRIC, "value": round(v, 4), "unit": UNIT, "impl": "reference", "n_gpus": 0,
+    line = {"metric": METRIC, "value": round(v, 4), "unit": UNIT, "impl": "reference", "n_gpus": ws,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 1),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic", "config": {"workload": WORKLOAD, "global_batch": 1, "seq_len": cfg.seq,
-                                            "layers": cfg.layers, "parallelism": "host threads"},
+            "higher_is_better": True, "scaling": scaling, "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic: seeded N(0,1) noisy inputs and host sinusoid timestep embeddings, N(0,0.02) random-init weights",
+            "config": config_of(cfg, G, ws, scaling),
             "cpu_baseline": {"value": round(v, 4), "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": "each step: one sample through all %d layers on the C oracle" % cfg.layers},
+                             "sample": "each step: one sample of the batch through all %d layers on the C oracle, "
+                                       "rows split over %d host threads (the rate is per sample)" % (cfg.layers, cores)},
             "e2e": {"value": round(v, 4), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -532,7 +690,7 @@ def profile_run(args):
     M.set_flavor("pinned")
     if args.profile_run == "step":
         cfg = D.Config(layers=args.layers)
-        B = args.batch_per_gpu
+        B = args.batch_per_gpu or 64
         w = D.init_weights(cfg, seed=1)
         W = [M.of_numpy(w[n]) for n, _ in D.weight_specs(cfg)]
         X = [M.of_numpy(a) for a in D.inputs(cfg, B, seed=1)]
@@ -555,7 +713,7 @@ def profile_run(args):
         M.eval_(outs)
         print("attention [%dx%dx%dx%d]: 3 launches" % (B, cfg.seq, cfg.heads, cfg.dh))
     elif args.profile_run == "kernels":
-        suite = kernel_suite(args.batch_per_gpu, D.Config(layers=args.layers), small=True)
+        suite = kernel_suite(args.batch_per_gpu or 64, D.Config(layers=args.layers), small=True)
         outs = [fn() for _, _, _, fn in suite]
         M.eval_(outs)
         print("kernels: %d launches: %s" % (len(suite), "; ".join(n for n, _, _, _ in suite)))

@@ -1469,6 +1469,20 @@ static int noalloc_scratch(int dev, float **out) {
   return 0;
 }
 
+// The kernel's dynamic shared-memory limit, raised once per device (with that
+// device current).
+static bool g_noalloc_attr[64];
+
+static int noalloc_smem_attr(int dev, int smem) {
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_attr[dev]) {
+    cudaError_t e = cudaFuncSetAttribute(k_mul_mat_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return cuda_check(e, "mul_mat_noalloc: shared-memory limit");
+    g_noalloc_attr[dev] = true;
+  }
+  return 0;
+}
+
 }  // namespace shlo
 
 extern "C" int shlo_mul_mat_noalloc(const float *w, const float *x, float *y, int64_t K, int64_t M, int64_t R,
@@ -1518,7 +1532,7 @@ extern "C" int shlo_mul_mat_noalloc(const float *w, const float *x, float *y, in
   SHLO_TRY(launch_check("mul_mat_noalloc pack"));
   launch_pack(x, (int)Nx, (int)K, Nx * K, (int)Bx, seg, segp, Np, 0.0f, xp, s);
   SHLO_TRY(launch_check("mul_mat_noalloc pack"));
-  MMArgs a;
+  MMArgs a{};  // the epilogue fields (bias, residual, park slabs) stay null: this kernel has none
   a.wp = wp;
   a.xp = xp;
   a.w = w;
@@ -1535,7 +1549,7 @@ extern "C" int shlo_mul_mat_noalloc(const float *w, const float *x, float *y, in
   a.r_tiles = Np / mm::BN;
   a.flavor = flavor;
   const size_t smem = (size_t)mm::NS * mm::STAGE_FLOATS * sizeof(float);
-  SHLO_CUDA(cudaFuncSetAttribute(k_mul_mat_fast, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+  SHLO_TRY(noalloc_smem_attr(devid, (int)smem));
   dim3 grid(Mp / mm::BM, (unsigned)(Bx * a.r_tiles));
   k_mul_mat_fast<<<grid, mm::THREADS, smem, s>>>(a);
   return launch_check("mul_mat_noalloc");

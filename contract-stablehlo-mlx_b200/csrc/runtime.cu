@@ -518,6 +518,15 @@ int shlo_launch_count(uint64_t *count) {
   return 0;
 }
 
+int shlo_device_ptr(shlo_arr a, void **ptr, int *device) {
+  if (!a) return fail("device_ptr: null array");
+  if (!a->buf) return fail("device_ptr: the array has no storage");
+  if (!is_row_contiguous(a)) return fail("device_ptr: the array is a strided view (make it contiguous first)");
+  *ptr = data_ptr(a);
+  if (device) *device = a->buf->dev->id;
+  return 0;
+}
+
 void shlo_retain(shlo_arr a) {
   if (a) a->rc.fetch_add(1);
 }

@@ -16,13 +16,27 @@
 
 #include "../../include/shlo_cuda.h"
 
-/* IO.Error.toString, exported by the Lean runtime. */
+/* Lean runtime functions this file calls that lean.h does not declare. */
 extern lean_object *lean_io_error_to_string(lean_object *err);
 
-static lean_obj_res io_err(const char *what) {
-	char b[4400];
-	snprintf(b, sizeof b, "%s: %s", what, shlo_last_error());
-	return lean_io_result_mk_error(lean_mk_io_user_error(lean_mk_string(b)));
+/* An IO error whose text is `msg`. */
+static lean_obj_res fail_with(const char *msg) {
+	return lean_io_result_mk_error(lean_mk_io_user_error(lean_mk_string(msg)));
+}
+
+/* A library call failed: the text names the operation and carries the
+   library's message for this thread. */
+static lean_obj_res lib_error(const char *op) {
+	const char *why = shlo_last_error();
+	size_t n = strlen(op) + strlen(why) + 3;
+	char *msg = (char *)malloc(n);
+	if (!msg) return fail_with(op);
+	memcpy(msg, op, strlen(op));
+	memcpy(msg + strlen(op), ": ", 2);
+	memcpy(msg + strlen(op) + 2, why, strlen(why) + 1);
+	lean_obj_res r = fail_with(msg);
+	free(msg);
+	return r;
 }
 
 /* ---- external classes: Arr, Kernel, Fn ---- */
@@ -39,15 +53,21 @@ static lean_object *box_arr(shlo_arr a) {
 }
 static shlo_arr unbox_arr(b_lean_obj_arg o) { return (shlo_arr)lean_get_external_data(o); }
 
-static int shape_of(b_lean_obj_arg arr, int64_t *out, int max) {
-	size_t n = lean_array_size(arr);
-	if ((int)n > max) return -1;
-	for (size_t i = 0; i < n; i++) out[i] = (int64_t)lean_unbox(lean_array_get_core(arr, i));
-	return (int)n;
+/* The entries of an `Array Nat` (a shape, permutation, start/stop/step or a
+   grid) as int64 values; false when there are more than `cap`. */
+static int read_dims(b_lean_obj_arg dims, int64_t *out, int cap, int *count) {
+	size_t len = lean_array_size(dims);
+	if (len > (size_t)cap) return 0;
+	for (size_t k = 0; k < len; k++) {
+		size_t v = lean_unbox(lean_array_get_core(dims, k));
+		out[k] = (int64_t)v;
+	}
+	*count = (int)len;
+	return 1;
 }
 
 static lean_obj_res ok_arr(int rc, shlo_arr r, const char *what) {
-	if (rc) return io_err(what);
+	if (rc) return lib_error(what);
 	return lean_io_result_mk_ok(box_arr(r));
 }
 
@@ -67,8 +87,8 @@ LEAN_EXPORT lean_obj_res smlx_empty(lean_obj_arg u) {
 LEAN_EXPORT lean_obj_res smlx_of_bytes(b_lean_obj_arg data, b_lean_obj_arg shape, uint8_t dt, lean_obj_arg w) {
 	(void)w;
 	int64_t s[SHLO_MAX_RANK];
-	int n = shape_of(shape, s, SHLO_MAX_RANK);
-	if (n < 0) return io_err("ofBytes: rank above 16");
+	int n = 0;
+	if (!read_dims(shape, s, SHLO_MAX_RANK, &n)) return fail_with("ofBytes: a shape of more than 16 dimensions");
 	shlo_arr r = NULL;
 	int rc = shlo_of_bytes(lean_sarray_cptr(data), lean_sarray_size(data), s, n, dt, &r);
 	return ok_arr(rc, r, "ofBytes");
@@ -77,11 +97,11 @@ LEAN_EXPORT lean_obj_res smlx_of_bytes(b_lean_obj_arg data, b_lean_obj_arg shape
 LEAN_EXPORT lean_obj_res smlx_to_bytes(b_lean_obj_arg a, lean_obj_arg w) {
 	(void)w;
 	size_t bytes = 0;
-	if (shlo_nbytes(unbox_arr(a), &bytes)) return io_err("toBytes");
+	if (shlo_nbytes(unbox_arr(a), &bytes)) return lib_error("toBytes");
 	lean_object *r = lean_alloc_sarray(1, bytes, bytes);
 	if (shlo_to_bytes(unbox_arr(a), lean_sarray_cptr(r), bytes)) {
 		lean_dec(r);
-		return io_err("toBytes");
+		return lib_error("toBytes");
 	}
 	return lean_io_result_mk_ok(r);
 }
@@ -90,14 +110,14 @@ LEAN_EXPORT lean_obj_res smlx_shape(b_lean_obj_arg a, lean_obj_arg w) {
 	(void)w;
 	int64_t s[SHLO_MAX_RANK];
 	int n = 0;
-	if (shlo_shape(unbox_arr(a), s, &n)) return io_err("shape");
+	if (shlo_shape(unbox_arr(a), s, &n)) return lib_error("shape");
 	return lean_io_result_mk_ok(shape_to_lean(s, n));
 }
 
 LEAN_EXPORT lean_obj_res smlx_dtype(b_lean_obj_arg a, lean_obj_arg w) {
 	(void)w;
 	uint8_t d = 0;
-	if (shlo_dtype(unbox_arr(a), &d)) return io_err("dtype");
+	if (shlo_dtype(unbox_arr(a), &d)) return lib_error("dtype");
 	return lean_io_result_mk_ok(lean_box((size_t)d));
 }
 
@@ -125,8 +145,9 @@ LEAN_EXPORT lean_obj_res smlx_where(b_lean_obj_arg c, b_lean_obj_arg a, b_lean_o
 	LEAN_EXPORT lean_obj_res NAME(b_lean_obj_arg a, b_lean_obj_arg shape, lean_obj_arg w) { \
 		(void)w;                                                                     \
 		int64_t s[SHLO_MAX_RANK];                                                    \
-		int n = shape_of(shape, s, SHLO_MAX_RANK);                                   \
-		if (n < 0) return io_err(WHAT ": rank above 16");                            \
+		int n = 0;                                                                   \
+		if (!read_dims(shape, s, SHLO_MAX_RANK, &n))                                 \
+			return fail_with(WHAT ": more than 16 dimensions");                      \
 		shlo_arr r = NULL;                                                           \
 		return ok_arr(CALL(unbox_arr(a), s, n, &r), r, WHAT);                        \
 	}
@@ -138,8 +159,10 @@ LEAN_EXPORT lean_obj_res smlx_slice(b_lean_obj_arg a, b_lean_obj_arg start, b_le
                                     lean_obj_arg w) {
 	(void)w;
 	int64_t s0[SHLO_MAX_RANK], s1[SHLO_MAX_RANK], s2[SHLO_MAX_RANK];
-	int n = shape_of(start, s0, SHLO_MAX_RANK), m = shape_of(stop, s1, SHLO_MAX_RANK), k = shape_of(step, s2, SHLO_MAX_RANK);
-	if (n < 0 || n != m || n != k) return io_err("slice");
+	int n = 0, m = 0, k = 0;
+	if (!read_dims(start, s0, SHLO_MAX_RANK, &n) || !read_dims(stop, s1, SHLO_MAX_RANK, &m) ||
+	    !read_dims(step, s2, SHLO_MAX_RANK, &k) || n != m || n != k)
+		return fail_with("slice: start, stop and step must have one entry per dimension (at most 16)");
 	shlo_arr r = NULL;
 	return ok_arr(shlo_slice(unbox_arr(a), s0, s1, s2, n, &r), r, "slice");
 }
@@ -192,7 +215,7 @@ LEAN_EXPORT lean_obj_res smlx_eval(b_lean_obj_arg xs, lean_obj_arg w) {
 	for (size_t i = 0; i < n; i++) v[i] = unbox_arr(lean_array_get_core(xs, i));
 	int rc = shlo_eval(v, (int)n);
 	free(v);
-	if (rc) return io_err("eval");
+	if (rc) return lib_error("eval");
 	return lean_io_result_mk_ok(lean_box(0));
 }
 
@@ -212,7 +235,7 @@ LEAN_EXPORT lean_obj_res smlx_kernel_new(b_lean_obj_arg name, b_lean_obj_arg ins
 	                         lean_string_cstr(hdr), &k);
 	free(vi);
 	free(vo);
-	if (rc) return io_err("kernel");
+	if (rc) return lib_error("kernel");
 	return lean_io_result_mk_ok(lean_alloc_external(kern_class, k));
 }
 
@@ -220,30 +243,31 @@ LEAN_EXPORT lean_obj_res smlx_kernel_apply(b_lean_obj_arg ko, b_lean_obj_arg ins
                                            b_lean_obj_arg dts, b_lean_obj_arg grid, b_lean_obj_arg tg, lean_obj_arg w) {
 	(void)w;
 	size_t ni = lean_array_size(ins), no = lean_array_size(shapes);
-	if (no > 8 || lean_sarray_size(dts) < no) return io_err("kernel apply: output shapes and dtypes");
+	if (no > 8) return fail_with("kernelApply: more than 8 outputs");
+	if (lean_sarray_size(dts) < no) return fail_with("kernelApply: fewer output dtypes than output shapes");
 	shlo_arr *vi = (shlo_arr *)malloc(sizeof(shlo_arr) * (ni ? ni : 1));
 	for (size_t i = 0; i < ni; i++) vi[i] = unbox_arr(lean_array_get_core(ins, i));
 	int64_t sh[8][SHLO_MAX_RANK];
 	const int64_t *shp[8];
 	int nd[8];
 	for (size_t i = 0; i < no; i++) {
-		nd[i] = shape_of(lean_array_get_core(shapes, i), sh[i], SHLO_MAX_RANK);
 		shp[i] = sh[i];
-		if (nd[i] < 0) {
+		if (!read_dims(lean_array_get_core(shapes, i), sh[i], SHLO_MAX_RANK, &nd[i])) {
 			free(vi);
-			return io_err("kernel apply: rank above 16");
+			return fail_with("kernelApply: an output shape of more than 16 dimensions");
 		}
 	}
 	int64_t g[3], t[3];
-	if (shape_of(grid, g, 3) != 3 || shape_of(tg, t, 3) != 3) {
+	int ng = 0, nt = 0;
+	if (!read_dims(grid, g, 3, &ng) || !read_dims(tg, t, 3, &nt) || ng != 3 || nt != 3) {
 		free(vi);
-		return io_err("kernel: grid and threadgroup need 3 entries");
+		return fail_with("kernelApply: the grid and the threadgroup are [x, y, z] triples");
 	}
 	shlo_arr outs[8] = {0};
 	int rc = shlo_kernel_apply((shlo_kernel)lean_get_external_data(ko), vi, (int)ni, shp, nd, lean_sarray_cptr(dts),
 	                           (int)no, g, t, outs);
 	free(vi);
-	if (rc) return io_err("kernel apply");
+	if (rc) return lib_error("kernel apply");
 	lean_object *r = lean_alloc_array(0, no);
 	for (size_t i = 0; i < no; i++) r = lean_array_push(r, box_arr(outs[i]));
 	return lean_io_result_mk_ok(r);
@@ -297,7 +321,7 @@ LEAN_EXPORT lean_obj_res smlx_compile(lean_obj_arg f, uint8_t enable, lean_obj_a
 	shlo_fn fn = NULL;
 	if (shlo_compile(trampoline, f, payload_free, enable, &fn)) {
 		lean_dec(f);
-		return io_err("compile");
+		return lib_error("compile");
 	}
 	return lean_io_result_mk_ok(lean_alloc_external(fn_class, fn));
 }
@@ -311,7 +335,7 @@ LEAN_EXPORT lean_obj_res smlx_apply(b_lean_obj_arg fo, b_lean_obj_arg ins, lean_
 	int n = 0;
 	int rc = shlo_apply((shlo_fn)lean_get_external_data(fo), vi, (int)ni, outs, &n, 64);
 	free(vi);
-	if (rc) return io_err("apply");
+	if (rc) return lib_error("apply");
 	lean_object *r = lean_alloc_array(0, (size_t)n);
 	for (int i = 0; i < n; i++) r = lean_array_push(r, box_arr(outs[i]));
 	return lean_io_result_mk_ok(r);
@@ -324,7 +348,7 @@ LEAN_EXPORT lean_obj_res smlx_libm_erff_range(uint32_t base, uint32_t count, lea
 	lean_object *r = lean_alloc_sarray(1, (size_t)count * 4, (size_t)count * 4);
 	if (shlo_libm_erff_range(base, count, (uint32_t *)lean_sarray_cptr(r))) {
 		lean_dec(r);
-		return io_err("libm_erff_range");
+		return lib_error("libm_erff_range");
 	}
 	return lean_io_result_mk_ok(r);
 }
@@ -332,6 +356,6 @@ LEAN_EXPORT lean_obj_res smlx_libm_erff_range(uint32_t base, uint32_t count, lea
 LEAN_EXPORT lean_obj_res smlx_count_nonzero(b_lean_obj_arg a, lean_obj_arg w) {
 	(void)w;
 	uint64_t n = 0;
-	if (shlo_count_nonzero(unbox_arr(a), &n)) return io_err("count_nonzero");
+	if (shlo_count_nonzero(unbox_arr(a), &n)) return lib_error("count_nonzero");
 	return lean_io_result_mk_ok(lean_uint64_to_nat(n));
 }

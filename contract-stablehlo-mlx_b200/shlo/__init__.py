@@ -10,11 +10,10 @@ the FFI boundary, one module each, with the reference's names:
   exec   StablehloMlx/Exec.lean         load / prepare / call, with a generic-form reader
 
 Every device operation goes through the C ABI of include/shlo_cuda.h. There
-is no CPU fallback: importing this package loads the CUDA library and fails if
-it is missing.
+is no CPU fallback: importing `mlx` (and so `run`, `lower`, `exec`, `fuse`)
+loads the CUDA library and fails if it is missing. Two modules are host-only
+and load nothing: `denoiser` (the benchmark workload as module text, weights
+and inputs) and `shard` (the partition rules and host collectives), so a
+CPU-only caller such as the CPU baseline can use them without mapping the
+CUDA library.
 """
-from . import _lib
-
-_lib.load()
-
-from . import mlx, run, lower, exec  # noqa: E402,F401

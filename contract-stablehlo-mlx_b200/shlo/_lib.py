@@ -15,7 +15,7 @@ SYMBOLS = [
     "shlo_transpose", "shlo_broadcast", "shlo_slice", "shlo_concat", "shlo_astype", "shlo_view", "shlo_take",
     "shlo_max_axis", "shlo_contiguous", "shlo_eval", "shlo_kernel_new", "shlo_kernel_free",
     "shlo_kernel_apply", "shlo_compile", "shlo_fn_free", "shlo_apply", "shlo_libm_erff_range",
-    "shlo_count_nonzero", "shlo_current_stream", "shlo_launch_count", "shlo_mul_mat_noalloc",
+    "shlo_count_nonzero", "shlo_current_stream", "shlo_launch_count", "shlo_device_ptr", "shlo_mul_mat_noalloc",
 ]
 
 
@@ -90,6 +90,7 @@ def load() -> ctypes.CDLL:
     L.shlo_count_nonzero.argtypes = [c_arr, ctypes.POINTER(ctypes.c_uint64)]
     L.shlo_current_stream.argtypes = [ctypes.POINTER(ctypes.c_void_p)]
     L.shlo_launch_count.argtypes = [ctypes.POINTER(ctypes.c_uint64)]
+    L.shlo_device_ptr.argtypes = [c_arr, ctypes.POINTER(ctypes.c_void_p), ctypes.POINTER(i)]
     L.shlo_mul_mat_noalloc.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int64,
                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
                                        ctypes.c_void_p]

@@ -14,6 +14,10 @@ import numpy as np
 
 from ._lib import FREE_FN, TRACE_FN, ShloError, c_arr, check, load
 
+# The library is mapped when this module is imported: a missing or unloadable
+# libshlo_cuda.so fails here, never later inside an op.
+load()
+
 # mlx_dtype codes (Mlx.lean:30-37)
 dtBool, dtU8, dtU16, dtU32, dtU64, dtI8, dtI16, dtI32, dtI64, dtF16, dtF32 = range(11)
 
@@ -318,6 +322,13 @@ def launch_count() -> int:
     c = ctypes.c_uint64()
     check(load().shlo_launch_count(ctypes.byref(c)))
     return c.value
+
+
+def device_ptr(a: Arr) -> tuple:
+    """(device address, device) of a row-contiguous array's first element."""
+    p, d = ctypes.c_void_p(), ctypes.c_int()
+    check(load().shlo_device_ptr(a.h, ctypes.byref(p), ctypes.byref(d)))
+    return p.value or 0, d.value
 
 
 def set_flavor(flavor: str) -> None:

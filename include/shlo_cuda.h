@@ -161,6 +161,15 @@ int shlo_apply(shlo_fn f, const shlo_arr *inputs, int n_inputs, shlo_arr *output
 int shlo_current_stream(void **stream);
 /* How many kernels this library has launched since it was loaded, all devices. */
 int shlo_launch_count(uint64_t *count);
+/* The device address of a row-contiguous array's first element and the device
+   it lives on, for handing a result to another library on the same GPU (a
+   collective's send buffer, say) without a copy; mlx-c's mlx_array_data_* play
+   this part on the reference's unified memory. The array's producing work is
+   queued on shlo_current_stream(): order the reader after it (an event on that
+   stream), and keep a reference to the array, with the compute stream ordered
+   after the reader, until the reader is done -- the storage returns to this
+   library's pool when the last reference goes. A strided view is an error. */
+int shlo_device_ptr(shlo_arr a, void **ptr, int *device);
 
 /* ---- mul_mat for callers that cannot allocate (no counterpart in the reference) ----
    The same product as the "smlx_mul_mat" kernel (ggml_vec_dot_f32 order, the

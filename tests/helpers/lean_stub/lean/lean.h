@@ -1,6 +1,8 @@
 /* A declaration-only stand-in for the subset of Lean 4's lean.h that
-   contract-stablehlo-mlx_b200/csrc/shlo_cuda_lean.c uses, so the CPU tests can
-   type-check the glue where Lean is not installed. Not linked or run. */
+   contract-stablehlo-mlx_b200/csrc/shlo_cuda_lean.c uses, so the tests can
+   compile the glue where Lean is not installed. tests/helpers/lean_model/
+   implements these declarations (a small model of the Lean runtime's objects)
+   so that the glue also links and runs. */
 #pragma once
 #include <stddef.h>
 #include <stdint.h>
