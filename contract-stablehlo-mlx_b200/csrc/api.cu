@@ -16,11 +16,6 @@ using namespace shlo;
 
 namespace {
 
-enum KernelKind {
-  KK_MUL_MAT, KK_SOFT_MAX, KK_NORM, KK_SILU, KK_GELU_ERF, KK_ERFF_MAP, KK_DIVIDE, KK_SQRT, KK_F64_EW,
-  KK_F64_OF_F32, KK_F32_OF_F64, KK_MUL_MAT_EP, KK_NORM_AFFINE, KK_ATTENTION
-};
-
 struct KernelInfo {
   const char *name;
   KernelKind kind;
@@ -76,6 +71,7 @@ struct Captured {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t exec = nullptr;
   uint64_t launches = 0;  // kernel launches recorded in the graph
+  int fused = 0;          // chains run as one fused launch each (fusion.cu)
 };
 
 std::string signature(Device *dev, const shlo_arr *inputs, int n) {
@@ -171,12 +167,21 @@ int record(shlo_fn f, Device *dev, const shlo_arr *inputs, int n_inputs, int max
     SHLO_TRY(refresh_slot(c, i, in));
   }
   // One eager call first: it derives every cached layout of the inputs (the
-  // packed weights of mul_mat) outside the graph, and checks f.
+  // packed weights of mul_mat) outside the graph, and checks f. Its ops are
+  // logged; the fused chains found in the log run as one launch each in the
+  // capture call (fusion.cu).
+  std::unique_ptr<Tracer, void (*)(Tracer *)> tr(fusion_enabled() ? tracer_new(dev) : nullptr, tracer_free);
   {
     std::vector<shlo_arr> tmp(max_outputs > 0 ? max_outputs : 1, nullptr);
     int n = 0;
-    SHLO_TRY(call_traced(f, c->staging.data(), n_inputs, tmp.data(), &n, max_outputs));
+    Tracer *outer = t_tracer;  // a recording in progress around this one (a nested compiled function)
+    t_tracer = tr.get();
+    const int frc = call_traced(f, c->staging.data(), n_inputs, tmp.data(), &n, max_outputs);
+    t_tracer = outer;
+    SHLO_TRY(frc);
+    if (tr) c->fused = tracer_plan(tr.get(), tmp.data(), n);
     release_all(tmp.data(), n);
+    if (tr && c->fused == 0) tr.reset();
   }
   // Nothing queued may still use a pooled block once the recording claims it.
   SHLO_TRY(device_wait(dev, "compile"));
@@ -196,8 +201,16 @@ int record(shlo_fn f, Device *dev, const shlo_arr *inputs, int n_inputs, int max
     dev->capture_owner = c;
     dev->capture_allocs = &c->allocs;
   }
+  Tracer *outer = t_tracer;
+  t_tracer = tr.get();
   int frc = call_traced(f, c->staging.data(), n_inputs, outs.data(), &n_out, max_outputs);
+  t_tracer = outer;
   std::string ferr = frc ? shlo_last_error() : "";
+  std::string unfused;
+  if (!frc && tr && !tracer_complete(tr.get(), &unfused)) {
+    frc = 1;  // the capture call departed from the eager call: record nothing, run unfused
+    ferr = "fusion: " + unfused;
+  }
   cudaGraph_t g = nullptr;
   e = cudaStreamEndCapture(dev->stream, &g);
   c->launches = g_launches.load() - l0;
@@ -261,6 +274,10 @@ int shlo_kernel_apply(shlo_kernel k, const shlo_arr *inputs, int n_inputs, const
     return fail("kernel %s: output dtype %s, %s expected", ki.name, dtype_name(out_dtypes[0]), dtype_name(ki.out_dtype));
   uint32_t p[8] = {0};
   SHLO_TRY(read_words(inputs[ki.param_index], p, ki.n_params));
+  // The op log of a compiled function's recording (fusion.cu): in the capture
+  // call an op of a fused chain returns its substitute here.
+  TraceScope ts(TK_KERNEL, (int)ki.kind, p, ki.n_params, inputs, n_inputs);
+  if (ts.substituted()) return ts.take(&outs[0]);
   Device *dev;
   SHLO_TRY(arr_device(inputs[0], &dev));
   // The kernels index flat row-major buffers (c/smlx_shim.c:292-293).
@@ -321,6 +338,7 @@ int shlo_kernel_apply(shlo_kernel k, const shlo_arr *inputs, int n_inputs, const
   }
   rc = shlo_reshape(o, out_shapes[0], out_ndims[0], &outs[0]);
   shlo_release(o);
+  if (!rc) ts.done(outs[0]);
   return rc;
 }
 
@@ -366,7 +384,13 @@ int shlo_apply(shlo_fn f, const shlo_arr *inputs, int n_inputs, shlo_arr *output
       return fail("%s", msg.c_str());
     }
     f->graphs[key] = c;
-    if (c->eager && getenv("SHLO_GRAPH_VERBOSE")) fprintf(stderr, "shlo: compiled function runs eagerly: %s\n", c->why.c_str());
+    if (getenv("SHLO_GRAPH_VERBOSE")) {
+      if (c->eager)
+        fprintf(stderr, "shlo: compiled function runs eagerly: %s\n", c->why.c_str());
+      else
+        fprintf(stderr, "shlo: compiled function recorded: %llu launches, %d fused chains\n",
+                (unsigned long long)c->launches, c->fused);
+    }
   }
   if (c->eager) return call_traced(f, inputs, n_inputs, outputs, n_outputs, max_outputs);
   if ((int)c->outs.size() > max_outputs) return fail("apply: %d outputs, room for %d", (int)c->outs.size(), max_outputs);

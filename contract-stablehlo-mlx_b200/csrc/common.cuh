@@ -77,6 +77,7 @@ int current_flavor();
 // ---- storage ----
 struct Buffer {
   std::atomic<int> rc{1};
+  uint64_t serial = 0;  // unique per storage block made (the op log's identity of data)
   Device *dev = nullptr;
   void *ptr = nullptr;
   size_t bytes = 0;
@@ -179,6 +180,55 @@ int launch_check(const char *what);
 extern std::atomic<uint64_t> g_launches;
 // Wait for all queued work of a device (bounded by SHLO_EVAL_TIMEOUT_S).
 int device_wait(Device *dev, const char *what);
+
+// The kernels of shlo_kernel_apply, by name (api.cu's table).
+enum KernelKind {
+  KK_MUL_MAT, KK_SOFT_MAX, KK_NORM, KK_SILU, KK_GELU_ERF, KK_ERFF_MAP, KK_DIVIDE, KK_SQRT, KK_F64_EW,
+  KK_F64_OF_F32, KK_F32_OF_F64, KK_MUL_MAT_EP, KK_NORM_AFFINE, KK_ATTENTION
+};
+// mul_mat's fused epilogue (k_mul_mat_ep): + bias[m] (its own operand order),
+// then + res[r][m].
+enum { EP_BIAS = 1, EP_BIAS_LHS = 2, EP_RES = 4, EP_RES_LHS = 8 };
+
+// ---- recording a compiled function: the op log and its fusions (fusion.cu) ----
+// Entry points that read array data open a TraceScope. While the recorder logs
+// the eager call of a compiled function (shlo_apply's first call of a
+// signature), the outermost scope on the thread logs the op; in the capture
+// call that follows, an op of a fusable chain is substituted: the scope then
+// holds the op's result (a placeholder, or the fused kernel's result at the
+// chain's end) and the entry point returns it without running the op.
+enum TraceKind { TK_KERNEL = 1, TK_BINARY, TK_COPY, TK_OTHER };
+struct Tracer;
+extern thread_local Tracer *t_tracer;
+bool fusion_enabled();
+Tracer *tracer_new(Device *dev);
+void tracer_free(Tracer *t);
+// After the eager call: mark its outputs, find the chains, switch to the capture
+// call's mode. Returns the number of chains found.
+int tracer_plan(Tracer *t, shlo_arr_s *const *outs, int n);
+// After the capture call: whether it matched the log and ended every chain.
+bool tracer_complete(Tracer *t, std::string *why);
+
+class TraceScope {
+ public:
+  TraceScope(int kind, int sub, const uint32_t *p, int np, shlo_arr_s *const *ins, int n);
+  ~TraceScope();
+  TraceScope(const TraceScope &) = delete;
+  TraceScope &operator=(const TraceScope &) = delete;
+  bool substituted() const { return substituted_; }
+  // The substituted op's status, with its result in *out on success.
+  int take(shlo_arr_s **out) {
+    *out = result_;
+    return status_;
+  }
+  // The op ran: log its result (nullptr when it returns no array).
+  void done(shlo_arr_s *out);
+
+ private:
+  int depth_ = 0, idx_ = -1, status_ = 0;
+  bool logging_ = false, substituted_ = false;
+  shlo_arr_s *result_ = nullptr;
+};
 
 // ---- ggml kernels (ggml_kernels.cu) ----
 int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out);

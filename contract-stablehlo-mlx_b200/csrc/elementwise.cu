@@ -1195,40 +1195,59 @@ static int builtin_matmul(Arr *a, Arr *b, Arr **out) {
 
 using namespace shlo;
 
+// Each entry point below reads array data, so it opens a TraceScope (the op
+// log of a compiled function's recording; see fusion.cu). Only the binary ops
+// take part in fusions; the others are logged as uses of their inputs.
+namespace {
+enum OtherOp { OT_UNARY = 1, OT_WHERE, OT_ASTYPE, OT_TAKE, OT_MAX_AXIS, OT_CONCAT, OT_COUNT_NONZERO };
+
+int traced(int kind, int sub, Arr *const *ins, int n, Arr **out, const std::function<int()> &run) {
+  TraceScope ts(kind, sub, nullptr, 0, ins, n);
+  if (ts.substituted()) return out ? ts.take(out) : fail("internal: a substituted op without a result");
+  const int rc = run();
+  if (!rc) ts.done(out ? *out : nullptr);
+  return rc;
+}
+}  // namespace
+
 extern "C" {
 
 int shlo_unary(uint32_t op, shlo_arr a, shlo_arr *out) {
   if (!a) return fail("unary: null array");
-  return op_unary(op, a, out);
+  return traced(TK_OTHER, OT_UNARY, &a, 1, out, [&] { return op_unary(op, a, out); });
 }
 int shlo_binary(uint32_t op, shlo_arr a, shlo_arr b, shlo_arr *out) {
   if (!a || !b) return fail("binary: null array");
-  return op_binary(op, a, b, out);
+  Arr *ins[2] = {a, b};
+  return traced(TK_BINARY, (int)op, ins, 2, out, [&] { return op_binary(op, a, b, out); });
 }
 int shlo_where(shlo_arr c, shlo_arr a, shlo_arr b, shlo_arr *out) {
   if (!c || !a || !b) return fail("where: null array");
-  return op_where(c, a, b, out);
+  Arr *ins[3] = {c, a, b};
+  return traced(TK_OTHER, OT_WHERE, ins, 3, out, [&] { return op_where(c, a, b, out); });
 }
 int shlo_astype(shlo_arr a, uint8_t dtype, shlo_arr *out) {
   if (!a) return fail("astype: null array");
-  return op_astype(a, dtype, out);
+  return traced(TK_OTHER, OT_ASTYPE, &a, 1, out, [&] { return op_astype(a, dtype, out); });
 }
 int shlo_take(shlo_arr a, shlo_arr idx, uint32_t axis, shlo_arr *out) {
   if (!a || !idx) return fail("take: null array");
-  return op_take(a, idx, (int)axis, out);
+  Arr *ins[2] = {a, idx};
+  return traced(TK_OTHER, OT_TAKE, ins, 2, out, [&] { return op_take(a, idx, (int)axis, out); });
 }
 int shlo_max_axis(shlo_arr a, uint32_t axis, shlo_arr *out) {
   if (!a) return fail("max_axis: null array");
-  return op_max_axis(a, (int)axis, out);
+  return traced(TK_OTHER, OT_MAX_AXIS, &a, 1, out, [&] { return op_max_axis(a, (int)axis, out); });
 }
 int shlo_concat(const shlo_arr *xs, int n, uint32_t axis, shlo_arr *out) {
   for (int i = 0; i < n; i++)
     if (!xs[i]) return fail("concatenate: null array");
-  return op_concat(const_cast<Arr *const *>(xs), n, (int)axis, out);
+  Arr *const *ins = const_cast<Arr *const *>(xs);
+  return traced(TK_OTHER, OT_CONCAT, ins, n, out, [&] { return op_concat(ins, n, (int)axis, out); });
 }
 int shlo_count_nonzero(shlo_arr a, uint64_t *count) {
   if (!a) return fail("count_nonzero: null array");
-  return op_count_nonzero(a, count);
+  return traced(TK_OTHER, OT_COUNT_NONZERO, &a, 1, nullptr, [&] { return op_count_nonzero(a, count); });
 }
 
 }  // extern "C"

@@ -89,7 +89,6 @@ struct MMArgs {
   int *ctr;           // k_mul_mat_tm split over CTAs: arrivals per tile (0 between launches)
 };
 
-enum { EP_BIAS = 1, EP_BIAS_LHS = 2, EP_RES = 4, EP_RES_LHS = 8 };
 
 // y (the dot product, NaN already canonical) + bias[m], then + res[r][m]: the
 // same __fadd_rn the built-in add runs, in the same operand order.

@@ -142,6 +142,9 @@ static size_t round_bytes(size_t n) {
   return (n + 511) & ~(size_t)511;
 }
 
+static std::atomic<uint64_t> g_serial{0};
+static uint64_t next_serial() { return g_serial.fetch_add(1) + 1; }
+
 static int take_block(Device *dev, size_t want, bool from_capture, void **p, size_t *got) {
   *p = nullptr;
   *got = want;
@@ -194,6 +197,7 @@ static int alloc_block(Device *dev, size_t bytes, bool constant, Buffer **out) {
     }
   }
   Buffer *b = new Buffer();
+  b->serial = next_serial();
   b->dev = dev;
   b->ptr = p;
   b->bytes = got;
@@ -244,6 +248,7 @@ static int alloc_upload(Device *dev, size_t bytes, Buffer **out) {
     SHLO_CUDA(cudaMalloc(&p, want));
   }
   Buffer *b = new Buffer();
+  b->serial = next_serial();
   b->dev = dev;
   b->ptr = p;
   b->bytes = got;
@@ -520,6 +525,8 @@ int shlo_launch_count(uint64_t *count) {
 
 int shlo_device_ptr(shlo_arr a, void **ptr, int *device) {
   if (!a) return fail("device_ptr: null array");
+  TraceScope ts(TK_OTHER, 21, nullptr, 0, &a, 1);  // the data escapes to the caller
+  ts.done(nullptr);
   if (!a->buf) return fail("device_ptr: the array has no storage");
   if (!is_row_contiguous(a)) return fail("device_ptr: the array is a strided view (make it contiguous first)");
   *ptr = data_ptr(a);
@@ -626,6 +633,8 @@ int shlo_nbytes(shlo_arr a, size_t *nbytes) {
 
 int shlo_to_bytes(shlo_arr a, void *dst, size_t cap) {
   if (!a) return fail("toBytes: null array");
+  TraceScope ts(TK_OTHER, 20, nullptr, 0, &a, 1);  // a read of the array's data
+  ts.done(nullptr);
   size_t bytes = (size_t)numel(a) * dtype_size(a->dtype);
   if (cap < bytes) return fail("toBytes: %zu bytes needed, %zu given", bytes, cap);
   if (bytes == 0) return 0;
@@ -734,6 +743,11 @@ int shlo_reshape(shlo_arr a, const int64_t *shape, int ndim, shlo_arr *out) {
     *out = v;
     return 0;
   }
+  // A row-contiguous array keeps its storage; any other is copied first (a
+  // read of its data: logged while a compiled function is recorded).
+  const bool copies = !is_row_contiguous(a) && a->buf;
+  TraceScope ts(copies ? TK_COPY : 0, 1, nullptr, 0, &a, copies ? 1 : 0);
+  if (copies && ts.substituted()) return ts.take(out);
   Arr *c;
   SHLO_TRY(make_contiguous(a, &c));
   Arr *v = new_view(c);
@@ -746,6 +760,7 @@ int shlo_reshape(shlo_arr a, const int64_t *shape, int ndim, shlo_arr *out) {
   }
   release_arr(c);
   *out = v;
+  if (copies) ts.done(v);
   return 0;
 }
 
@@ -813,6 +828,8 @@ int shlo_view(shlo_arr a, uint8_t dtype, shlo_arr *out) {
   if (a->ndim == 0) return fail("view: a scalar cannot change its element size");
   int64_t last = a->shape[a->ndim - 1] * (int64_t)from;
   if (last % (int64_t)to) return fail("view: last axis of %lld bytes is not a multiple of %zu", (long long)last, to);
+  TraceScope ts(TK_OTHER, 22, nullptr, 0, &a, 1);  // may copy: logged as a read
+  ts.done(nullptr);
   Arr *c;
   SHLO_TRY(make_contiguous(a, &c));
   Arr *v = new_view(c);
@@ -832,7 +849,12 @@ int shlo_view(shlo_arr a, uint8_t dtype, shlo_arr *out) {
 
 int shlo_contiguous(shlo_arr a, shlo_arr *out) {
   if (!a) return fail("contiguous: null array");
-  return make_contiguous(a, out);
+  const bool copies = !is_row_contiguous(a) && a->buf;
+  TraceScope ts(copies ? TK_COPY : 0, 2, nullptr, 0, &a, copies ? 1 : 0);
+  if (copies && ts.substituted()) return ts.take(out);
+  const int rc = make_contiguous(a, out);
+  if (copies && !rc) ts.done(*out);
+  return rc;
 }
 
 int shlo_eval(const shlo_arr *xs, int n) {

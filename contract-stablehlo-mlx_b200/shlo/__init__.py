@@ -10,7 +10,7 @@ the FFI boundary, one module each, with the reference's names:
   exec   StablehloMlx/Exec.lean         load / prepare / call, with a generic-form reader
 
 Every device operation goes through the C ABI of include/shlo_cuda.h. There
-is no CPU fallback: importing `mlx` (and so `run`, `lower`, `exec`, `fuse`)
+is no CPU fallback: importing `mlx` (and so `run`, `lower`, `exec`)
 loads the CUDA library and fails if it is missing. Two modules are host-only
 and load nothing: `denoiser` (the benchmark workload as module text, weights
 and inputs) and `shard` (the partition rules and host collectives), so a

@@ -7,15 +7,17 @@ one op per line, `"stablehlo.x"(%a, %b) {attrs} : (types) -> type`),
 
 The reader carries single-block functions; region ops (`while`, `reduce`) are
 refused as not carried by this reader.
+
+Ops run one at a time, as Lower.lean issues them; the fused launches of a
+compiled function are chosen below the boundary, by libshlo_cuda's recorder
+(csrc/fusion.cu), so this mirror and the unchanged Lean host get the same ones.
 """
 from __future__ import annotations
 
-import os
 import re
 from dataclasses import dataclass, field
 from typing import Dict, List
 
-from . import fuse as F
 from . import lower as L
 from . import mlx as M
 
@@ -70,26 +72,12 @@ class Func:
 class Module:
     funcs: Dict[str, Func] = field(default_factory=dict)
 
-    fuse: bool = True  # run fuse.plan's fused launches (off with $SHLO_FUSE=0 or any fault)
-    _plans: Dict[str, dict] = field(default_factory=dict)
-
     def run_func(self, f: L.Faults, fn: Func, args: List[M.Arr]) -> List[M.Arr]:
         """Lower.lean:521-526 (one block, no trace-time scalars)."""
         if len(args) != len(fn.args):
             raise M.ShloError("@%s takes %d arguments, got %d" % (fn.name, len(fn.args), len(args)))
         env = {n: a for (n, _), a in zip(fn.args, args)}
-        fused, skip = {}, set()
-        if self.fuse and os.environ.get("SHLO_FUSE", "1") != "0" and not F.any_fault(f):
-            if fn.name not in self._plans:
-                self._plans[fn.name] = F.plan(fn)
-            fused = self._plans[fn.name]
-            skip = {j for fz in fused.values() for j in fz.skip}
-        for i, o in enumerate(fn.ops):
-            if i in skip:
-                continue
-            if i in fused:
-                env[fused[i].result] = F.run_fused(fused[i], o, env)
-                continue
+        for o in fn.ops:
             try:
                 xs = [env[n] for n in o.operands]
             except KeyError as e:

@@ -1,15 +1,24 @@
-"""The executor's fused launches (shlo/fuse.py) against the unfused sequence
-they replace, bit for bit: the fused kernels alone on random data with
-specials, and whole modules (the encoder layer and the denoiser) fused and
-unfused."""
+"""The fused launches against the unfused sequences they replace, bit for bit.
+
+The fusions are chosen below the boundary, by the recorder of compiled
+functions (csrc/fusion.cu): a compiled call (shlo_compile with enable = 1)
+runs the fused kernels, an uncompiled call runs the ops one at a time as
+Lower.lean issues them. Checked here: the fused kernels alone on random data
+with specials; whole modules (the encoder layer, the denoiser, the attention
+block) compiled against uncompiled, with the number of fused chains the
+recorder reports; chains it must leave alone (an intermediate read elsewhere,
+a planted fault); and a traced function whose capture call departs from its
+eager call, which must run unfused with the eager result."""
 from __future__ import annotations
+
+import re
 
 import numpy as np
 import pytest
 
-import shlo  # noqa: F401
 from shlo import denoiser as D
 from shlo import exec as E
+from shlo import lower as L
 from shlo import mlx as M
 from shlo import run as Run
 
@@ -68,24 +77,114 @@ def test_norm_affine_matches_unfused(cols, rows):
     assert np.array_equal(bits(got).reshape(-1), bits(want).reshape(-1))
 
 
+def run_counted(capfd, monkeypatch, fn, args):
+    """Call a compiled function once (recording it) and return its output and
+    the fused chains the recorder reported."""
+    monkeypatch.setenv("SHLO_GRAPH_VERBOSE", "1")
+    capfd.readouterr()
+    out = M.to_numpy(E.call(fn, args)[0])
+    err = capfd.readouterr().err
+    monkeypatch.delenv("SHLO_GRAPH_VERBOSE")
+    m = re.search(r"recorded: (\d+) launches, (\d+) fused chains", err)
+    return out, (int(m.group(2)) if m else None), err
+
+
 @pytest.mark.parametrize("cfg,B", [(D.ENCODER, 2), (D.Config(layers=2), 3)])
-def test_modules_fused_equal_unfused(cfg, B):
+def test_modules_fused_equal_unfused(cfg, B, capfd, monkeypatch):
     w = D.init_weights(cfg, seed=9)
     W = [M.of_numpy(w[n]) for n, _ in D.weight_specs(cfg)]
     X = [M.of_numpy(a) for a in D.inputs(cfg, B, seed=4)]
-    text = D.module_text(cfg, B)
-    fused = E.load(text)
-    plain = E.load(text)
-    plain.module.fuse = False
-    for compile_ in (False, True):
-        got = M.to_numpy(E.call(E.prepare(fused, None, compile_), X + W)[0])
-        want = M.to_numpy(E.call(E.prepare(plain, None, compile_), X + W)[0])
-        assert np.array_equal(bits(got), bits(want))
+    l = E.load(D.module_text(cfg, B))
+    want = M.to_numpy(E.call(E.prepare(l, None, False), X + W)[0])
+    fn = E.prepare(l, None, True)
+    got, chains, err = run_counted(capfd, monkeypatch, fn, X + W)
+    # per layer: qkv, output (+ residual), ffn1, ffn2 (+ residual) dense chains, two
+    # layer norms, and the attention block where the fused kernel carries its
+    # positions (128 or 256: not the encoder's 196); two timestep dense chains
+    per_layer = 6 + (1 if cfg.seq in (128, 256) else 0)
+    assert chains == per_layer * cfg.layers + (2 if cfg.timestep else 0), err
+    assert np.array_equal(bits(got), bits(want))
+    again = M.to_numpy(E.call(fn, X + W)[0])  # the replay
+    assert np.array_equal(bits(again), bits(want))
 
 
-def attn_text(B, S, H, W, scale_bits):
+def test_planted_faults_are_not_fused_away(capfd, monkeypatch):
+    """A planted wrong lowering changes the ops, so the chain no longer matches
+    and the compiled result keeps the fault's bits (differing from the exact ones)."""
+    cfg = D.Config(layers=1)
+    w = D.init_weights(cfg, seed=2)
+    W = [M.of_numpy(w[n]) for n, _ in D.weight_specs(cfg)]
+    X = [M.of_numpy(a) for a in D.inputs(cfg, 1, seed=2)]
+    l = E.load(D.module_text(cfg, 1))
+    exact = M.to_numpy(E.call(E.prepare(l, None, False), X + W)[0])
+    for fault in (L.Faults(dotPlain=True), L.Faults(normGpuOps=True), L.Faults(softMaxFloatSum=True),
+                  L.Faults(broadcastFirst=True)):
+        eager = M.to_numpy(E.call(E.prepare(l, fault, False), X + W)[0])
+        got, chains, err = run_counted(capfd, monkeypatch, E.prepare(l, fault, True), X + W)
+        assert np.array_equal(bits(got), bits(eager)), fault
+        assert not np.array_equal(bits(got), bits(exact)), fault
+
+
+def test_intermediate_read_elsewhere_is_not_fused(capfd, monkeypatch):
+    """The dense chain's product is also a function output: it must be computed
+    on its own, so nothing is fused."""
+    text = """module {
+  func.func public @main(%x: tensor<64x512xf32>, %w: tensor<256x512xf32>, %b: tensor<256xf32>) -> (tensor<64x256xf32>, tensor<64x256xf32>) {
+    %y = "stablehlo.dot_general"(%x, %w) {dot_dimension_numbers = #stablehlo.dot<lhs_contracting_dimensions = [1], rhs_contracting_dimensions = [1]>} : (tensor<64x512xf32>, tensor<256x512xf32>) -> tensor<64x256xf32>
+    %bb = "stablehlo.broadcast_in_dim"(%b) {broadcast_dimensions = array<i64: 1>} : (tensor<256xf32>) -> tensor<64x256xf32>
+    %z = "stablehlo.add"(%y, %bb) : (tensor<64x256xf32>, tensor<64x256xf32>) -> tensor<64x256xf32>
+    func.return %z, %y : tensor<64x256xf32>, tensor<64x256xf32>
+  }
+}
+"""
+    rng = np.random.default_rng(1)
+    args = [M.of_numpy(rng.standard_normal(s).astype(np.float32)) for s in ((64, 512), (256, 512), (256,))]
+    l = E.load(text)
+    want = [M.to_numpy(a) for a in E.call(E.prepare(l, None, False), args)]
+    got, chains, err = run_counted(capfd, monkeypatch, E.prepare(l, None, True), args)
+    assert chains == 0, err
+    assert np.array_equal(bits(got), bits(want[0]))
+
+
+def test_capture_call_departing_from_eager_call_runs_unfused(capfd, monkeypatch):
+    """The recorder matches the capture call to the eager call op by op; a
+    traced function that does something else the second time must not get the
+    first call's fused chain: the recording is dropped and the function runs
+    eagerly (unfused) from then on, with its own results."""
+    rng = np.random.default_rng(3)
+    K, Mm, R = 512, 256, 64
+    w = M.of_numpy(rng.standard_normal((Mm, K)).astype(np.float32))
+    x = M.of_numpy(rng.standard_normal((R, K)).astype(np.float32))
+    b = M.of_numpy(rng.standard_normal((Mm,)).astype(np.float32))
+    b2 = M.of_numpy(rng.standard_normal((R, Mm)).astype(np.float32))
+    calls = [0]
+
+    def f(args):
+        calls[0] += 1
+        y = M.reshape(Run.mul_mat(args[0], args[1], K, Mm, R, R, 0), [R, Mm])
+        other = M.broadcast(M.reshape(args[2], [1, Mm]), [R, Mm]) if calls[0] != 2 else args[3]
+        return [M.binary(M.opAdd, y, other)]
+
+    monkeypatch.setenv("SHLO_GRAPH_VERBOSE", "1")
+    capfd.readouterr()
+    fn = M.compile_(f, True)
+    got = M.to_numpy(M.apply(fn, [w, x, b, b2])[0])
+    err = capfd.readouterr().err
+    monkeypatch.delenv("SHLO_GRAPH_VERBOSE")
+    assert "runs eagerly" in err and "fusion" in err, err
+    y = M.reshape(Run.mul_mat(w, x, K, Mm, R, R, 0), [R, Mm])
+    want = M.to_numpy(M.binary(M.opAdd, y, M.broadcast(M.reshape(b, [1, Mm]), [R, Mm])))
+    assert np.array_equal(bits(got), bits(want))
+
+
+def attn_text(B, S, H, W, scale_bits, merged=True):
+    """q k^T -> soft_max -> p v -> transpose, as the encoder layer writes it;
+    `merged`: then the reshape to [B, S, H*W] that ends the fused chain."""
     T = lambda *d: "tensor<" + "".join("%dx" % x for x in d) + "f32>"
     q, s_, o, qkv = T(B, S, H, W), T(B, H, S, S), T(B, H, S, W), T(B, S, 3, H, W)
+    m = T(B, S, H * W)
+    tail = (f'    %r = "stablehlo.reshape"(%t) : ({q}) -> {m}\n    func.return %r : {m}\n' if merged
+            else f"    func.return %t : {q}\n")
     sl = T(B, S, 1, H, W)
     parts = []
     for i in range(3):
@@ -94,13 +193,12 @@ def attn_text(B, S, H, W, scale_bits):
             f'array<i64: {B}, {S}, {i + 1}, {H}, {W}>, strides = array<i64: 1, 1, 1, 1, 1>}} : ({qkv}) -> {sl}\n'
             f'    %x{i} = "stablehlo.reshape"(%sl{i}) : ({sl}) -> {q}\n')
     return f"""module {{
-  func.func public @main(%qkv: {qkv}) -> ({q}) {{
+  func.func public @main(%qkv: {qkv}) -> ({m if merged else q}) {{
 {''.join(parts)}    %s = "stablehlo.dot_general"(%x0, %x1) {{dot_dimension_numbers = #stablehlo.dot<lhs_batching_dimensions = [0, 2], rhs_batching_dimensions = [0, 2], lhs_contracting_dimensions = [3], rhs_contracting_dimensions = [3]>}} : ({q}, {q}) -> {s_}
     %p = "stablehlo.custom_call"(%s) {{call_target_name = "ggml.soft_max", backend_config = "scale = 0x{scale_bits:08X} : f32"}} : ({s_}) -> {s_}
     %o = "stablehlo.dot_general"(%p, %x2) {{dot_dimension_numbers = #stablehlo.dot<lhs_batching_dimensions = [0, 1], rhs_batching_dimensions = [0, 2], lhs_contracting_dimensions = [3], rhs_contracting_dimensions = [1]>}} : ({s_}, {q}) -> {o}
     %t = "stablehlo.transpose"(%o) {{permutation = array<i64: 0, 2, 1, 3>}} : ({o}) -> {q}
-    func.return %t : {q}
-  }}
+{tail}  }}
 }}
 """
 
@@ -109,7 +207,7 @@ def attn_text(B, S, H, W, scale_bits):
                                                      (3, 256, 2, 0x3F800000, True, 4.0), (1, 256, 1, 0x41000000, False, 4.0),
                                                      (2, 256, 4, 0x3E000000, False, 0.05), (1, 128, 2, 0x3E000000, False, 0.3),
                                                      (2, 256, 2, 0x3E000000, False, 1.0)])
-def test_attention_matches_unfused(B, S, H, scale, special, amp):
+def test_attention_matches_unfused(B, S, H, scale, special, amp, capfd, monkeypatch):
     # q, k, v as the strided slices of one projection, as in the encoder layer;
     # specials give NaN and infinite score rows (the soft_max's sequential scan);
     # small amplitudes keep every row's exponentials within a few binades (the
@@ -117,11 +215,11 @@ def test_attention_matches_unfused(B, S, H, scale, special, amp):
     rng = np.random.default_rng(B * 1000 + S + H)
     a = specials(rng, (B, S, 3, H, 64)) if special else rng.standard_normal((B, S, 3, H, 64)).astype(np.float32)
     x = [M.of_numpy(a * np.float32(amp))]
-    text = attn_text(B, S, H, 64, scale)
-    fused = E.load(text)
-    plain = E.load(text)
-    plain.module.fuse = False
-    for compile_ in (False, True):
-        got = M.to_numpy(E.call(E.prepare(fused, None, compile_), x)[0])
-        want = M.to_numpy(E.call(E.prepare(plain, None, compile_), x)[0])
+    for merged in (True, False):
+        l = E.load(attn_text(B, S, H, 64, scale, merged))
+        want = M.to_numpy(E.call(E.prepare(l, None, False), x)[0])
+        got, chains, err = run_counted(capfd, monkeypatch, E.prepare(l, None, True), x)
+        # without the final reshape the chain has no end to fuse into -- except
+        # with one head, where the value product already is the [B, S, H*64] layout
+        assert chains == (1 if merged or H == 1 else 0), err
         assert np.array_equal(bits(got), bits(want))
