@@ -128,7 +128,7 @@ def dist_init():
     if ws <= 1:
         return 0, 0, 1, None
     import torch.distributed as dist
-    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=600))
+    dist.init_process_group("gloo", timeout=datetime.timedelta(seconds=300))
     return dist.get_rank(), int(os.environ.get("LOCAL_RANK", "0")), ws, dist
 
 
@@ -412,7 +412,7 @@ def run_shlo(args):
     timer = EventTimer(M.current_stream(), local_rank)
     nccl = None
     if dist is not None:
-        nccl = dist.new_group(backend="nccl")
+        nccl = dist.new_group(backend="nccl", timeout=datetime.timedelta(seconds=300))
         z = torch.zeros(1, device="cuda")
         dist.all_reduce(z, group=nccl)  # the communicator is set up here, outside any timing
         torch.cuda.synchronize()
@@ -694,12 +694,14 @@ def profile_run(args):
         w = D.init_weights(cfg, seed=1)
         W = [M.of_numpy(w[n]) for n, _ in D.weight_specs(cfg)]
         X = [M.of_numpy(a) for a in D.inputs(cfg, B, seed=1)]
-        # called eagerly, so every kernel is a launch of its own in the list
-        fn = E.prepare(E.load(D.module_text(cfg, B)), None, False)
+        # compiled, as the executor prepares it: the first call runs the trace
+        # eagerly and records the fused graph, the second replays it (the graph's
+        # kernels are the last launches of the run)
+        fn = E.prepare(E.load(D.module_text(cfg, B)), None, True)
         c0 = M.launch_count()
-        M.eval_([M.apply(fn, X + W)[0]])  # warm-up step
+        M.eval_([M.apply(fn, X + W)[0]])  # warm-up step (eager trace + recording)
         c1 = M.launch_count()
-        M.eval_([M.apply(fn, X + W)[0]])  # the captured step
+        M.eval_([M.apply(fn, X + W)[0]])  # the replayed step
         print("launches: warm-up %d, step %d" % (c1 - c0, M.launch_count() - c1))
     elif args.profile_run == "attention":
         # the fused attention at batch 16 of the denoiser's shape, three launches

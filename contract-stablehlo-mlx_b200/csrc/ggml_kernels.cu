@@ -444,7 +444,9 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   if (!attr_done[dev->id]) {
     const int rc = cuda_check(mul_mat_tm_attributes<1>(), "mul_mat attribute") ||
          cuda_check(mul_mat_tm_attributes<2>(), "mul_mat attribute") ||
-         cuda_check(mul_mat_tm_attributes<4>(), "mul_mat attribute");
+         cuda_check(mul_mat_tm_attributes<4>(), "mul_mat attribute") ||
+         cuda_check(mul_mat_tm_attributes<8>(), "mul_mat attribute") ||
+         cuda_check(mul_mat_tm_attributes<16>(), "mul_mat attribute");
     if (rc) {
       buffer_release(wpk);
       buffer_release(xpk);
@@ -464,10 +466,21 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   // the grid no fuller in its last wave than halved. Quarters for tiny grids (below).
   int split = 1;
   if (segp / 2 >= 16 && (segp >= 128 || M <= 512) && wave_fill(2 * tiles) + 0.01 >= wave_fill(tiles)) split = 2;
-  // A grid of a few tiles (the timestep MLP) leaves most SMs
-  // idle: quarters make each CTA's K four times shorter.
+  // A grid of a few tiles (the timestep MLP, BASELINE config 1, a batch of one)
+  // leaves most SMs idle: quarters, eighths or sixteenths of the tree make each
+  // CTA's K that much shorter, as long as the grid stays within one CTA an SM
+  // and every CTA keeps whole stages of 16 packed k (2 or 1 segments a CTA:
+  // segp a multiple of 8 or 16).
+  auto valid = [&](int s) { return s <= 4 ? segp % 4 == 0 : segp % s == 0; };
   if (4 * tiles <= slots / 2 && segp >= 8) split = 4;
-  if (const char *e = getenv("SHLO_MM_SPLIT")) split = atoi(e) == 4 ? 4 : atoi(e) == 2 ? 2 : 1;
+  if (split == 4 && 8 * tiles <= slots / 2 && valid(8)) split = 8;
+  if (split == 8 && 16 * tiles <= slots / 2 && valid(16)) split = 16;
+  if (const char *e = getenv("SHLO_MM_SPLIT")) {
+    // a forced form; the largest valid one at or below it
+    split = 1;
+    for (int s : {2, 4, 8, 16})
+      if (s <= atoi(e) && valid(s)) split = s;
+  }
   const bool shared_tile = split > 1;
   const unsigned grid = (unsigned)(split * tiles);
   Buffer *park, *ctr = nullptr;
@@ -484,7 +497,9 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   a.park = (float *)park->ptr;
   a.ctr = shared_tile ? (int *)ctr->ptr : nullptr;
   const bool stage_fold = segp % 16 == 0;
-  if (split == 4) launch_mul_mat_tm<4>(WM, stage_fold, ep != 0, grid, dev->stream, a);
+  if (split == 16) launch_mul_mat_tm<16>(WM, stage_fold, ep != 0, grid, dev->stream, a);
+  else if (split == 8) launch_mul_mat_tm<8>(WM, stage_fold, ep != 0, grid, dev->stream, a);
+  else if (split == 4) launch_mul_mat_tm<4>(WM, stage_fold, ep != 0, grid, dev->stream, a);
   else if (split == 2) launch_mul_mat_tm<2>(WM, stage_fold, ep != 0, grid, dev->stream, a);
   else launch_mul_mat_tm<1>(WM, stage_fold, ep != 0, grid, dev->stream, a);
   int rc = launch_check("mul_mat");

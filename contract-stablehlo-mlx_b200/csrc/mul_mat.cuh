@@ -196,9 +196,12 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
 // popped only at S = 15 (depth 4); the caller parks it in global memory, so
 // here depth 3 leaves the value in acc and depth 4 stops after level 2.
 // PAIR: the adds as paired FP32 adds (fewer issue slots, more register pressure).
+// last_pops >= 0: the last fold of a CTA that computes a subtree of 2^last_pops
+// segments (a quarter: 2, an eighth: 1): pop that many levels, push nothing.
 template <bool PAIR>
-__device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, float4 *lv2, int S, bool last = false) {
-  const int depth = last ? 2 : __ffs(~S) - 1;  // trailing one bits: 0..4 (a quarter's last: pop 0 and 1)
+__device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, float4 *lv2, int S, int last_pops = -1) {
+  const bool last = last_pops >= 0;
+  const int depth = last ? last_pops : __ffs(~S) - 1;  // trailing one bits: 0..4
   const int pops = depth < 3 ? depth : 3;
 #pragma unroll
   for (int c = 0; c < 4; c++) {
@@ -231,7 +234,7 @@ __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, floa
         for (int i = 0; i < 16; i++) v[i] = __fadd_rn(t[i], v[i]);
       }
     }
-    if (depth < 2) {
+    if (depth < 2 && !last) {
       tmem_st16(tcol + 64 * depth + 16 * c, v);
     } else if (depth == 2 && !last) {
 #pragma unroll
@@ -246,23 +249,28 @@ __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, floa
 // tile in L2).
 // STAGE_FOLD: every segment spans whole stages (segp a multiple of 16), so the
 // fold check runs once per stage; otherwise after every group of 4 k.
-// SPLIT = 2 or 4: the grid has SPLIT CTAs a tile, CTA q computing the subtree
-// of segments [q 16/SPLIT, (q + 1) 16/SPLIT) (4 segments: a 2-level stack, all
-// in TMEM; 8: levels 0-1 in TMEM and 2 in the slab); each writes its partial to
-// a per-tile slice of a.park, and the last of the tile's CTAs to arrive (an
-// atomic count, no waiting) adds the top of ggml's tree -- T0 + T1, or
-// ((T0 + T1) + (T2 + T3)) -- and runs the epilogue. More, shorter CTAs fill the
-// last wave of a grid that would leave SMs idle. SPLIT = 1: one CTA a tile,
-// T(0..7) parked in a.park until the root add.
+// SPLIT = 2, 4, 8 or 16: the grid has SPLIT CTAs a tile, CTA q computing the
+// subtree of segments [q 16/SPLIT, (q + 1) 16/SPLIT) (1 segment: one chain, no
+// stack; 2 or 4 segments: a 1- or 2-level stack, all in TMEM; 8: levels 0-1 in
+// TMEM and 2 in the slab); each writes its partial to a per-tile slice of
+// a.park, and the last of the tile's CTAs to arrive (an atomic count, no
+// waiting) adds the top of ggml's tree over the SPLIT partials -- T0 + T1,
+// ((T0 + T1) + (T2 + T3)), ... -- and runs the epilogue. More, shorter CTAs
+// fill a grid that would leave SMs idle (small products: few rows or few
+// tiles). SPLIT = 1: one CTA a tile, T(0..7) parked in a.park until the root
+// add.
 // EPI: the fused bias / residual adds in the epilogue (a separate instance, so
 // the plain product compiles without them).
 template <int WM, bool STAGE_FOLD, int SPLIT, bool EPI>
 __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMArgs a) {
   using namespace mt;
   constexpr int BM = Tile<WM>::BM, BN = Tile<WM>::BN, STAGE_FLOATS = Tile<WM>::STAGE_FLOATS;
-  constexpr bool QUARTER = SPLIT == 4;
   constexpr int SEGS = 16 / SPLIT;  // segments a CTA
-  constexpr int NS = QUARTER ? Pipe<WM>::NS_QUARTER : Pipe<WM>::NS;
+  // At most 4 segments a CTA: a stack of levels 0-1 only (TMEM), so the level-2
+  // slab's shared memory holds more stages.
+  constexpr bool NO_SLAB = SPLIT >= 4;
+  constexpr int LAST_POPS = SPLIT == 4 ? 2 : SPLIT == 8 ? 1 : -1;
+  constexpr int NS = NO_SLAB ? Pipe<WM>::NS_QUARTER : Pipe<WM>::NS;
   extern __shared__ __align__(16) float smem[];
   __shared__ uint32_t tmem_base;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -355,7 +363,8 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
   float4 *lv2 = reinterpret_cast<float4 *>(smem + NS * STAGE_FLOATS) + tid;
   int S = 0, gleft = a.segp / 4;
   auto fold_segment = [&]() {
-    tfold_rt<STAGE_FOLD>(acc2, tcol, lv2, S, QUARTER && S == 3);
+    // A CTA of one segment has no stack: its chain is its partial.
+    if constexpr (SPLIT < 16) tfold_rt<STAGE_FOLD>(acc2, tcol, lv2, S, (LAST_POPS >= 0 && S == SEGS - 1) ? LAST_POPS : -1);
     // After S = 7 the fold left T(0..7) in acc (depth 3 pushes nothing).
     if (SPLIT == 1 && S == 7) park(false);
     if (++S < SEGS) {
@@ -444,17 +453,26 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
     };
 #pragma unroll
     for (int i = 0; i < 16; i++) {
-      // every partial from L2 (this CTA's own too: it wrote it above)
-      float4 r;
-      if constexpr (SPLIT == 4) {
-        const float4 p0 = __ldcg(base + i * THREADS), p1 = __ldcg(base + 16 * THREADS + i * THREADS);
-        const float4 p2 = __ldcg(base + 32 * THREADS + i * THREADS), p3 = __ldcg(base + 48 * THREADS + i * THREADS);
-        r = add4(add4(p0, p1), add4(p2, p3));
-      } else {
-        r = add4(__ldcg(base + i * THREADS), __ldcg(base + 16 * THREADS + i * THREADS));
+      // every partial from L2 (this CTA's own too: it wrote it above), then the
+      // top of the tree: neighbours first, as the perfect binary tree pairs them
+      // (partial q pushes at level ctz(~q) after adding the levels below it,
+      // the older value on the left: the binary-counter form of that tree)
+      constexpr int TOP = SPLIT == 2 ? 1 : SPLIT == 4 ? 2 : SPLIT == 8 ? 3 : 4;
+      float4 lv[TOP + 1];
+#pragma unroll
+      for (int q = 0; q < SPLIT; q++) {
+        float4 v = __ldcg(base + q * 16 * THREADS + i * THREADS);
+#pragma unroll
+        for (int L = 0; L <= TOP; L++) {
+          if (((q >> L) & 1) == 0 || L == TOP) {
+            lv[L] = v;
+            break;
+          }
+          v = add4(lv[L], v);
+        }
       }
-      acc2[2 * i] = make_float2(r.x, r.y);
-      acc2[2 * i + 1] = make_float2(r.z, r.w);
+      acc2[2 * i] = make_float2(lv[TOP].x, lv[TOP].y);
+      acc2[2 * i + 1] = make_float2(lv[TOP].z, lv[TOP].w);
     }
   } else {
     // The root of the tree: T(0..7) + T(8..15).

@@ -1,0 +1,9 @@
+// The TMEM-stack mul_mat's instances for tiles split over 8 CTAs (SPLIT 8), in a
+// translation unit of their own so that the kernel instances compile in parallel.
+#define SHLO_MUL_MAT_INSTANCES
+#include "mul_mat.cuh"
+
+namespace shlo {
+template cudaError_t mul_mat_tm_attributes<8>();
+template void launch_mul_mat_tm<8>(int, bool, bool, unsigned, cudaStream_t, const MMArgs &);
+}  // namespace shlo

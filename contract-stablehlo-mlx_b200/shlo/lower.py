@@ -263,6 +263,65 @@ def convert_op(a, src: Ty, out: Ty):
     return M.astype(a, el_dtype(e))
 
 
+INT_ELS = ("i1", "i8", "ui8", "i32", "si32", "ui32", "i64", "si64", "ui64")
+
+
+def const_eval(known: Dict[str, int], o) -> Optional[int]:
+    """Lower.lean:225-251: the value of a scalar integer that is a constant, or
+    arithmetic on such scalars -- what `while` conditions and `dynamic_slice`
+    starts are made of (None when it depends on data)."""
+    if not o.out_tys or o.out_tys[0].dims != () or o.out_tys[0].el not in INT_ELS:
+        return None
+
+    def k(i):
+        return known.get(o.operands[i]) if i < len(o.operands) else None
+    n = o.name
+    if n == "stablehlo.constant":
+        v = o.attr("value")
+        if v is None:
+            return None
+        t = (v.split("dense<")[1] if "dense<" in v else "").split(">")[0].strip()
+        if t == "true":
+            return 1
+        if t == "false":
+            return 0
+        try:
+            return int(t)
+        except ValueError:
+            return None
+    if n in ("stablehlo.add", "stablehlo.subtract", "stablehlo.multiply"):
+        a, b = k(0), k(1)
+        if a is None or b is None:
+            return None
+        return a + b if n.endswith("add") else a - b if n.endswith("subtract") else a * b
+    if n == "stablehlo.convert":
+        return k(0)
+    if n == "stablehlo.compare":
+        a, b = k(0), k(1)
+        if a is None or b is None:
+            return None
+        d = direction(o.attr("comparison_direction") or "")
+        r = {"EQ": a == b, "NE": a != b, "LT": a < b, "LE": a <= b, "GT": a > b}.get(d[-2:], a >= b)
+        return 1 if r else 0
+    return None
+
+
+def gather1d(o, table: M.Arr, idx: M.Arr) -> M.Arr:
+    """Lower.lean:317-331: `stablehlo.gather` of a 1-D table indexed elementwise,
+    out[i] = table[clamp(idx[i])] -- the form contract-ggml-stablehlo emits;
+    any other form is refused."""
+    dn = o.attr("dimension_numbers") or ""
+    t, it = o.in_tys[0], o.in_tys[1]
+    if not (len(t.dims) == 1 and field_(dn, "collapsed_slice_dims") == "[0]" and field_(dn, "start_index_map") == "[0]"
+            and ("index_vector_dim = %d" % len(it.dims)) in dn and ints(o.attr("slice_sizes") or "") == [1]):
+        err("gather: only a 1-D table indexed elementwise is carried (%s)" % dn)
+    ix = M.astype(idx, M.dtI64)
+    lo = M.astype(M.u32_arr([0]), M.dtI64)
+    hi = M.astype(M.u32_arr([t.dims[0] - 1]), M.dtI64)
+    ix = M.binary(M.opMin, M.binary(M.opMax, ix, M.reshape(lo, [])), M.reshape(hi, []))
+    return M.take(table, ix, 0)
+
+
 @dataclass
 class Op:
     """One StableHLO op as the Lean AST holds it (StablehloMlx/Ast.lean)."""
@@ -278,8 +337,12 @@ class Op:
         return self.attrs.get(k)
 
 
-def run_op(f: Faults, o: Op, args: List[M.Arr], module=None) -> List[M.Arr]:
-    """Lower.lean:334-473 (regions and trace-time scalars are handled by the caller)."""
+def run_op(f: Faults, o: Op, args: List[M.Arr], module=None, env=None, known=None) -> List[M.Arr]:
+    """Lower.lean:334-473. `env` and `known` are the enclosing values and the
+    trace-time integer scalars among them (a region reads the values defined
+    around it; `while` and `dynamic_slice` need the scalars)."""
+    env = env if env is not None else {}
+    known = known if known is not None else {}
     out = o.out_tys[0] if o.out_tys else Ty((), "")
     n = o.name
     el0 = o.in_tys[0].el if o.in_tys else ""
@@ -389,6 +452,53 @@ def run_op(f: Faults, o: Op, args: List[M.Arr], module=None) -> List[M.Arr]:
     if n == "stablehlo.dot_general":
         return [dot_general(f, o.attr("dot_dimension_numbers") or "", args[0], args[1], o.in_tys[0], o.in_tys[1],
                             out)]
+    if n == "stablehlo.dynamic_slice":
+        # Lower.lean:417-428: the starts must be known at trace time
+        src = o.in_tys[0]
+        sizes = ints(o.attr("slice_sizes") or "")
+        st = []
+        for d, nm in enumerate(o.operands[1:]):
+            v = known.get(nm)
+            if v is None:
+                err("dynamic_slice: start %d (%s) depends on data, which is not carried" % (d, nm))
+            # StableHLO clamps each start to [0, dim - size]
+            st.append(max(0, min(v, src.dims[d] - sizes[d])))
+        return [M.slice_(args[0], st, [a + b for a, b in zip(st, sizes)], [1] * len(st))]
+    if n == "stablehlo.gather":
+        return [gather1d(o, args[0], args[1])]
+    if n == "stablehlo.reduce":
+        # Lower.lean:430-440: a single-operand maximum; exact and order-free, the
+        # init value takes part like any element
+        dims = ints(o.attr("dimensions") or "")
+        if not o.regions:
+            err("reduce without a body")
+        body = o.regions[0]
+        if not (len(body.ops) == 1 and body.ops[0].name == "stablehlo.maximum" and len(o.operands) == 2):
+            err("reduce: only a single-operand maximum is carried")
+        if el0 == "f64":
+            err("reduce on f64 is not carried")
+        r = args[0]
+        for d in sorted(dims, reverse=True):
+            r = M.max_axis(r, d)
+        return [M.binary(M.opMax, r, args[1])]
+    if n == "stablehlo.while":
+        # Lower.lean:454-470: unrolled while the trace runs; the condition must be known
+        if len(o.regions) < 2:
+            err("while without its two regions")
+        cond, body = o.regions[0], o.regions[1]
+        st = list(args)
+        st_k = [known.get(nm) for nm in o.operands]
+        prev = st
+        while True:
+            _, ck = run_region(module, f, env, known, cond, st, st_k)
+            c = ck[0] if ck else None
+            if c is None:
+                err("while: the condition depends on data, which is not carried (the loop is unrolled when traced)")
+            if c == 0:
+                break
+            br, bk = run_region(module, f, env, known, body, st, st_k)
+            prev, st, st_k = st, br, bk
+        return prev if f.whileShort else st
     if n in ("stablehlo.composite", "stablehlo.custom_call"):
         return run_composite(f, o, args, module)
     err("op %s is not in the lowering table" % n)
@@ -421,5 +531,46 @@ def run_composite(f: Faults, o: Op, args: List[M.Arr], module=None) -> List[M.Ar
         fn = module.funcs.get(dec)
         if fn is None:
             err("composite %s: no decomposition @%s" % (name, dec))
-        return module.run_func(f, fn, args)
+        return run_func(module, f, fn, args)
     err("composite %s: no decomposition" % name)
+
+
+def run_region(module, f: Faults, env, known, block, args, arg_known):
+    """Lower.lean:503-519: run a block whose arguments are `args`, seeing the
+    enclosing values; returns its results and which of them are known integer
+    scalars."""
+    env = dict(env)
+    known = dict(known)
+    for (n, _), a, k in zip(block.args, args, arg_known):
+        env[n] = a
+        if k is None:
+            known.pop(n, None)
+        else:
+            known[n] = k
+    for o in block.ops:
+        try:
+            xs = [env[nm] for nm in o.operands]
+        except KeyError as e:
+            raise M.ShloError("undefined value %s" % e)
+        rs = run_op(f, o, xs, module, env, known)
+        if len(rs) != len(o.results):
+            raise M.ShloError("%s: %d results for %d names" % (o.name, len(rs), len(o.results)))
+        env.update(zip(o.results, rs))
+        if len(o.results) == 1:
+            v = const_eval(known, o)
+            if v is None:
+                known.pop(o.results[0], None)
+            else:
+                known[o.results[0]] = v
+    try:
+        outs = [env[nm] for nm in block.ret]
+    except KeyError as e:
+        raise M.ShloError("undefined value %s" % e)
+    return outs, [known.get(nm) for nm in block.ret]
+
+
+def run_func(module, f: Faults, fn, args):
+    """Lower.lean:521-526."""
+    if len(args) != len(fn.args):
+        raise M.ShloError("@%s takes %d arguments, got %d" % (fn.name, len(fn.args), len(args)))
+    return run_region(module, f, {}, {}, fn.body, args, [None] * len(args))[0]
