@@ -537,6 +537,31 @@ def run_shlo(args):
             2.0 * K * Mm * Rr / (t / n) / 1e12, 2)
         del wa, xa, y
     mm_tflops = mm_flops / mm_time / 1e12
+    weight_tflops = weight_flops / weight_time / 1e12
+    # Small products, timed on the device: n calls recorded as one CUDA graph
+    # (a compiled function) and replayed, so the host's per-call overhead is
+    # not in the figure. Config 1, the timestep MLP's products at this rank's
+    # batch, and a layer's products at batch 1 (the latency case).
+    small = {}
+    for name, (K, Mm, Rr) in (("config1 64x256x128", (256, 128, 64)),
+                              ("timestep %dx512x512" % B, (cfg.d, cfg.d, B)),
+                              ("batch1 qkv 256x1536x512", (cfg.d, 3 * cfg.d, cfg.seq)),
+                              ("batch1 ffn2 256x512x2048", (cfg.ffn, cfg.d, cfg.seq))):
+        wa = M.of_numpy(rng.standard_normal((Mm, K)).astype(np.float32))
+        xa = M.of_numpy(rng.standard_normal((Rr, K)).astype(np.float32))
+        reps = 50
+
+        def many(args, K=K, Mm=Mm, Rr=Rr):
+            y = None
+            for _ in range(reps):
+                y = Run.mul_mat(args[0], args[1], K, Mm, Rr, Rr, 0)
+            return [y]
+        fm = M.compile_(many, True)
+        M.eval_(M.apply(fm, [wa, xa]))  # records the graph
+        t = timer.time(lambda: M.apply(fm, [wa, xa]), 5)
+        small[name] = {"us_per_call": round(t / (5 * reps) * 1e6, 2),
+                       "tflops": round(2.0 * K * Mm * Rr * 5 * reps / t / 1e12, 3)}
+        del fm, wa, xa
     # dot_general config 1: [64,256] x [256,128]
     w1 = M.of_numpy(rng.standard_normal((128, 256)).astype(np.float32))
     x1 = M.of_numpy(rng.standard_normal((64, 256)).astype(np.float32))
@@ -595,14 +620,18 @@ def run_shlo(args):
         "config": config_of(cfg, G, ws, scaling),
         "batch_per_gpu": B,
         "model_tflops": round(flops_step * args.steps / dt_max / 1e12, 2),
-        "roofline": {"bound": "fp32-cuda-core", "kernel": "mul_mat (k_mm_pack of x + k_mul_mat_tm)",
-                     "achieved": round(mm_tflops, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
-                     "frac": round(mm_tflops / peak, 3),
+        "roofline": {"bound": "fp32-cuda-core",
+                     "kernel": "mul_mat (k_mm_pack of x + k_mul_mat_tm) at the step's four weight products of a layer "
+                               "(QKV, output, FFN1, FFN2; attention's products run inside k_attention)",
+                     "achieved": round(weight_tflops, 2), "peak": round(peak, 2), "unit": "TFLOP/s",
+                     "frac": round(weight_tflops / peak, 3),
                      "peak_source": "FP32 CUDA-core peak: %d SMs x 128 FFMA lanes x 2 flop x %.0f MHz (median SM clock "
                                     "sampled during the timed region; MEASURED_PEAKS.json has no FP32 figure)"
                                     % (sm_count, sm_mhz),
-                     "peak_at_max_clock": round(peak_max, 2), "frac_at_max_clock": round(mm_tflops / peak_max, 3),
-                     "weight_products_tflops": round(weight_flops / weight_time / 1e12, 2),
+                     "peak_at_max_clock": round(peak_max, 2), "frac_at_max_clock": round(weight_tflops / peak_max, 3),
+                     "six_shapes_tflops": round(mm_tflops, 2),
+                     "six_shapes_note": "the four weight products and, as standalone mul_mat calls, attention's scores "
+                                        "and value shapes (the unfused path's)",
                      "sgemm_tflops": round(sgemm, 2),
                      "sgemm_note": "cuBLAS SGEMM (TF32 off) 8192^3 on this GPU in this run, a side note: not the peak",
                      "per_shape": per_shape,
@@ -610,7 +639,10 @@ def run_shlo(args):
         "kernels": kernels,
         "dot_general": {"config1_64x256x128_tflops": round(cfg1_tflops, 4),
                         "config1_us_per_call": round(t1 / n1 * 1e6, 2),
-                        "denoiser_shapes_tflops": round(mm_tflops, 2)},
+                        "config1_note": "eager calls from Python through the C ABI, host overhead included; "
+                                        "small_products has the device time",
+                        "denoiser_shapes_tflops": round(mm_tflops, 2),
+                        "small_products": small},
         "cpu_baseline": cpu,
         "cpu_baseline_single_thread": cpu1,
         "e2e": {"value": round(G * args.steps / e2e_dt, 3), "unit": UNIT, "h2d_bytes_per_step": h2d,

@@ -22,7 +22,7 @@ LIB = os.path.join(LIB_DIR, "libshlo_cuda.so")
 # The mul_mat kernel instances sit in six units of their own, compiled in
 # parallel with the rest (the longest compiles of the library).
 SOURCES = ["mul_mat_tm_split1.cu", "mul_mat_tm_split2.cu", "mul_mat_tm_split4.cu", "mul_mat_tm_split8.cu",
-           "mul_mat_tm_split16.cu", "mul_mat_short.cu",
+           "mul_mat_tm_split16.cu", "mul_mat_short.cu", "mul_mat_seg.cu",
            "ggml_kernels.cu", "attention.cu", "runtime.cu", "elementwise.cu", "api.cu", "fusion.cu"]
 
 NVCC_FLAGS = [

@@ -295,11 +295,14 @@ static int mm_path() {
   const char *e = getenv("SHLO_MUL_MAT_PATH");
   if (e && !strcmp(e, "naive")) return 1;
   if (e && !strcmp(e, "fast")) return 2;
+  if (e && !strcmp(e, "seg")) return 3;
   return 0;
 }
 
 static int pack_operand(Device *dev, const float *src, int rows, int K, int64_t src_batch, int batches, int seg,
                         int segp, int rows_p, float pad, Buffer **out) {
+  // k_mm_pack writes whole blocks of 64 rows
+  if (rows_p % 64) return fail("mul_mat pack: %d padded rows, not a multiple of 64", rows_p);
   size_t bytes = (size_t)batches * 16 * segp * rows_p * sizeof(float);
   SHLO_TRY(buffer_alloc(dev, bytes, out));
   launch_pack(src, rows, K, src_batch, batches, seg, segp, rows_p, pad, (float *)(*out)->ptr, dev->stream);
@@ -337,7 +340,7 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   const int flavor = current_flavor();
   const int64_t np = K & ~(int64_t)15;
   int path = mm_path();
-  bool fast = !plain && np >= 16 && (path == 2 || (path == 0 && R * M >= 4096));
+  bool fast = !plain && np >= 16 && (path >= 2 || (path == 0 && R * M >= 4096));
   if (R * M == 0) {
     *out = o;
     return 0;
@@ -364,14 +367,20 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   const int segp = (seg + 3) & ~3;
   // k_mul_mat_short (register stack, 64 x 64 tiles): every segment 4 packed k,
   // or up to 16 when M <= 64 (attention's value product).
-  const bool short_k = segp == 4 || (M <= 64 && segp <= 16);
-  const int WM = M <= 64 ? 1 : 2;
-  const int BM = short_k ? ms::BM : WM == 1 ? mt::Tile<1>::BM : mt::Tile<2>::BM;
-  const int BN = short_k ? ms::BN : WM == 1 ? mt::Tile<1>::BN : mt::Tile<2>::BN;
-  const int Mp = (int)((M + BM - 1) / BM * BM);
   const int64_t Bx = wbs ? nb : 1;
   const int64_t Nx = wbs ? N : R;
-  const int Np = (int)((Nx + BN - 1) / BN * BN);
+  // k_mul_mat_seg (32 x 32 tiles, the sixteen chains side by side in a CTA):
+  // products of up to 2^21 outputs, where 128 x 128 tiles would leave most of
+  // the GPU idle; $SHLO_MUL_MAT_PATH=seg forces it.
+  const bool short_k = path != 3 && (segp == 4 || (M <= 64 && segp <= 16));
+  const bool seg_k = path == 3 || (path == 0 && !short_k && Bx * Nx * M <= ((int64_t)1 << 21));
+  const int WM = M <= 64 ? 1 : 2;
+  const int BM = seg_k ? sg::TM : short_k ? ms::BM : WM == 1 ? mt::Tile<1>::BM : mt::Tile<2>::BM;
+  const int BN = seg_k ? sg::TR : short_k ? ms::BN : WM == 1 ? mt::Tile<1>::BN : mt::Tile<2>::BN;
+  // padded to whole tiles, and to the pack's blocks of 64 rows
+  const int PM = BM < 64 ? 64 : BM, PN = BN < 64 ? 64 : BN;
+  const int Mp = (int)((M + PM - 1) / PM * PM);
+  const int Np = (int)((Nx + PN - 1) / PN * PN);
   const int Wb = wbs ? (int)nb : 1;
   // The packed w is derived from w's storage, which never changes: keep it.
   Buffer *wpk = nullptr;
@@ -427,9 +436,12 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   a.r_tiles = Np / BN;
   a.flavor = flavor;
   a.bx_count = (int)Bx;
-  if (short_k) {
+  if (seg_k || short_k) {
     const unsigned grid = (unsigned)((int64_t)(Mp / BM) * Bx * a.r_tiles);
-    launch_mul_mat_short(segp / 4, ep != 0, grid, dev->stream, a);
+    if (seg_k)
+      launch_mul_mat_seg(ep != 0, grid, dev->stream, a);
+    else
+      launch_mul_mat_short(segp / 4, ep != 0, grid, dev->stream, a);
     int rc = launch_check("mul_mat");
     buffer_release(wpk);
     buffer_release(xpk);
@@ -462,10 +474,15 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   const int64_t slots = (int64_t)mt::CTAS_PER_SM * dev->sm_count;
   auto wave_fill = [&](int64_t t) { return (double)t / (double)(((t + slots - 1) / slots) * slots); };
   // Halves where measured faster (B200, the denoiser's shapes): long K
-  // (>= 2048) or narrow M (<= 512), each half at least 16 stages of 16 k and
-  // the grid no fuller in its last wave than halved. Quarters for tiny grids (below).
+  // (>= 2048) or narrow M (<= 512), each half at least 16 stages of 16 k, the
+  // grid no fuller in its last wave than halved, and fewer than four waves of
+  // tiles (with more, one CTA a tile measured as fast or faster: the output
+  // projection at 131072 rows 44.7 against 43.5 TFLOP/s). Smaller splits for
+  // tiny grids (below).
   int split = 1;
-  if (segp / 2 >= 16 && (segp >= 128 || M <= 512) && wave_fill(2 * tiles) + 0.01 >= wave_fill(tiles)) split = 2;
+  if (segp / 2 >= 16 && (segp >= 128 || M <= 512) && tiles < 4 * slots &&
+      wave_fill(2 * tiles) + 0.01 >= wave_fill(tiles))
+    split = 2;
   // A grid of a few tiles (the timestep MLP, BASELINE config 1, a batch of one)
   // leaves most SMs idle: quarters, eighths or sixteenths of the tree make each
   // CTA's K that much shorter, as long as the grid stays within one CTA an SM

@@ -727,6 +727,11 @@ template <int SPLIT>
 void launch_mul_mat_tm(int WM, bool stage_fold, bool epi, unsigned grid, cudaStream_t stream, const MMArgs &a);
 // k_mul_mat_short<EPI, NG> with NG = ng (1..4).
 void launch_mul_mat_short(int ng, bool epi, unsigned grid, cudaStream_t stream, const MMArgs &a);
+// k_mul_mat_seg<EPI> (mul_mat_seg.cu): small products, 32 m x 32 r tiles.
+namespace sg {
+constexpr int TM = 32, TR = 32, THREADS = 256;
+}
+void launch_mul_mat_seg(bool epi, unsigned grid, cudaStream_t stream, const MMArgs &a);
 
 #ifdef SHLO_MUL_MAT_INSTANCES
 template <int SPLIT>

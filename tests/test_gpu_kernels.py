@@ -35,11 +35,15 @@ MM_SHAPES = [  # K, M, R, N, batched
     (64, 256, 256, 256, True), (100, 64, 33, 11, True), (196, 196, 392, 196, True), (256, 64, 512, 256, True),
     (352, 128, 352, 352, False), (512, 1536, 300, 300, False), (737, 1024, 40, 40, False), (2048, 512, 129, 129, False),
     (4096, 64, 16, 16, False), (80, 33, 200, 50, True), (64, 40, 700, 700, False), (192, 64, 1300, 650, True),
+    # segments that do not span whole stages (the fold after groups of 4 k) in
+    # eighths, and a batched narrow-M product in sixteenths
+    (389, 200, 96, 96, False), (643, 130, 64, 64, False), (1024, 64, 128, 64, True),
 ]
 
 
 @pytest.mark.parametrize("flavor", ["pinned", "stock"])
-@pytest.mark.parametrize("path", ["fast", "naive", "fast-split1", "fast-split2", "fast-split4"])
+@pytest.mark.parametrize("path", ["fast", "naive", "seg", "fast-split1", "fast-split2", "fast-split4", "fast-split8",
+                                  "fast-split16"])
 @pytest.mark.parametrize("K,Mm,R,N,batched", MM_SHAPES)
 def test_mul_mat_random(K, Mm, R, N, batched, path, flavor, monkeypatch):
     # the fast path in one CTA a tile, or in two or four (halves, quarters of the fold tree)
@@ -58,7 +62,7 @@ def test_mul_mat_random(K, Mm, R, N, batched, path, flavor, monkeypatch):
     assert_bits(got, want, "mul_mat K=%d M=%d R=%d N=%d" % (K, Mm, R, N))
 
 
-@pytest.mark.parametrize("path", ["fast", "naive"])
+@pytest.mark.parametrize("path", ["fast", "naive", "seg"])
 def test_mul_mat_signed_zeros_and_specials(path, monkeypatch):
     """Chains that end at -0, products that underflow, infinities: the padded
     segments and the tree must keep every sign and special value."""
