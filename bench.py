@@ -281,9 +281,30 @@ def kernel_suite(B: int, cfg, small: bool = False):
     return out
 
 
+def graph_time(timer, fn, reps: int) -> float:
+    """Device seconds per call of `fn`: `reps` calls recorded as one compiled
+    function (a CUDA graph) and replayed, so no host work is inside the timing
+    (the data stays in L2 between calls where it fits)."""
+    from shlo import mlx as M
+
+    def many(args):
+        y = None
+        for _ in range(reps):
+            y = fn()
+        return [y]
+    fm = M.compile_(many, True)
+    M.eval_(M.apply(fm, []))  # records the graph
+    M.eval_(M.apply(fm, []))
+    t = timer.time(lambda: M.apply(fm, []), 3)
+    del fm
+    return t / (3 * reps)
+
+
 def time_kernels(timer, suite, n: int, hbm_gbs: float) -> dict:
     """Per-launch CUDA-event durations on the library's stream, with L2 flushed
-    (a 256 MiB fill on the same stream) before every launch."""
+    (a 256 MiB fill on the same stream) before every launch; for short kernels
+    this includes the host's call overhead. `graph_us`: the device time per
+    call, the kernel recorded in a CUDA graph and replayed (graph_time)."""
     torch = timer.torch
     flush = torch.empty(64 << 20, dtype=torch.float32, device=timer.stream.device)
     res = {}
@@ -304,6 +325,8 @@ def time_kernels(timer, suite, n: int, hbm_gbs: float) -> dict:
         total = sum(s.elapsed_time(e) for s, e in evs) / 1e3
         us = total / n * 1e6
         row = {"us": round(us, 2), "gbs": round(nbytes / (total / n) / 1e9, 1)}
+        gt = graph_time(timer, fn, 20 if us < 100 else 5)
+        row["graph_us"] = round(gt * 1e6, 2)
         if hbm_gbs:
             row["frac_hbm"] = round(row["gbs"] / hbm_gbs, 3)
         if flop:
