@@ -529,6 +529,23 @@ def run_shlo(args):
         del f1
     del X1
 
+    # ---- config 5's batch sweep on one GPU: the step rate at global batches
+    # 1, 16 and 64 beside the headline's (compiled, device-resident inputs)
+    sweep = {}
+    if ws == 1:
+        for gb in (1, 16, 64):
+            if gb == G:
+                continue
+            Xb = [M.of_numpy(a) for a in D.inputs(cfg, gb, seed=1)]
+            fb = E.prepare(E.load(D.module_text(cfg, gb)), None, True)
+            for _ in range(3):
+                M.apply(fb, Xb + W)
+            nb = 20 if gb <= 16 else 10
+            tb = timer.time(lambda: M.apply(fb, Xb + W), nb)
+            sweep[str(gb)] = {"sample_steps_per_s": round(gb * nb / tb, 2), "ms_per_step": round(tb / nb * 1e3, 3)}
+            del fb, Xb
+        sweep[str(G)] = {"sample_steps_per_s": round(G * args.steps / dt, 2), "ms_per_step": round(dt / args.steps * 1e3, 3)}
+
     # ---- the dominant kernel: mul_mat at a layer's six shapes for this rank's
     # batch (four weight products, then attention's scores and value products,
     # batched per head), each launch with its activation pack
@@ -676,6 +693,7 @@ def run_shlo(args):
                                                       "gathered_equals_ranks_results": gather_ok}},
         "gpu_launches": int(launches),
         "latency_b1_ms": latency,
+        "batch_sweep_1gpu": sweep or None,
         "clocks": clocks,
         "bit_exact": {"sample0_vs_oracle": exact0, "deterministic_across_steps": deterministic},
         "hbm_gbs_measured": measured_peaks().get("hbm_gbs"),
