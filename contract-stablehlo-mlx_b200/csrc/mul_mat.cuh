@@ -68,6 +68,15 @@ __device__ __forceinline__ void cp_async_wait() {
 }
 
 
+// Invalidate the L2 lines of n floats at p (a multiple of 32 floats from a
+// 128-byte boundary) without writing them back: for scratch that was written
+// and read within one launch and is never read again. The CTA's threads share
+// the lines; call after every thread's last read of them.
+__device__ __forceinline__ void discard_l2(float *p, size_t n) {
+  for (size_t l = threadIdx.x; l < n / 32; l += blockDim.x)
+    asm volatile("discard.global.L2 [%0], 128;\n" ::"l"(p + 32 * l) : "memory");
+}
+
 struct MMArgs {
   const float *wp;  // packed w [Wb][Kq][Mp]
   const float *xp;  // packed x [Bx][Kq][Np]
@@ -474,9 +483,15 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
       acc2[2 * i] = make_float2(lv[TOP].x, lv[TOP].y);
       acc2[2 * i + 1] = make_float2(lv[TOP].z, lv[TOP].w);
     }
+    // The partials are spent: drop their L2 lines instead of writing them back.
+    __syncthreads();
+    discard_l2(a.park + (size_t)tile * SPLIT * (THREADS * 64), SPLIT * THREADS * 64);
   } else {
     // The root of the tree: T(0..7) + T(8..15).
     park(true);
+    // The parked slice is spent: drop its L2 lines instead of writing them back.
+    __syncthreads();
+    discard_l2(a.park + (size_t)blockIdx.x * (THREADS * 64), THREADS * 64);
   }
   // Epilogue: the tail (K mod 16 elements, in order) and the store.
   int m0, bx;
