@@ -86,3 +86,46 @@ def test_two_gloo_ranks():
     want = int(np.count_nonzero((sample >> np.uint64(16)) & np.uint64(0xFF) == 0x5A))
     assert res[0][2] == res[1][2] == want
     assert res[0][3] == res[1][3] == 2.5
+
+
+def _leaving_worker(rank, world, port, q):
+    """Rank 1 leaves before the job's collective (a host-side failure: the
+    process returns between steps, nothing of it in flight); rank 0's collective
+    must end with an error within its short timeout instead of waiting for good."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import datetime
+    import time
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        q.put((1, "left"))
+        q.close()
+        q.join_thread()  # the message is out before the process goes
+        os._exit(0)  # gone without the collective or the group's teardown
+    t0 = time.monotonic()
+    try:
+        S.sum_over_ranks(dist, 3)
+        q.put((0, "no error", time.monotonic() - t0))
+    except Exception as e:  # the collective's timeout or the peer's closed connection
+        q.put((0, type(e).__name__, time.monotonic() - t0))
+
+
+def test_a_rank_that_leaves_is_detected_not_waited_for():
+    world = 2
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_leaving_worker, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = {}
+    for _ in range(world):
+        r = q.get(timeout=120)
+        res[r[0]] = r
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert res[1][1] == "left"
+    assert res[0][1] != "no error", res[0]
+    assert res[0][2] < 60, res[0]  # ended by the group's 5 s limit (or at once), not the test's
