@@ -69,8 +69,9 @@ def sweep(rank, ws, dist, M, Run, O, S, chunk_log=24):
                 bad += k
                 first_bad = b if first_bad is None else min(first_bad, b)
     dt = time.perf_counter() - t0
-    # the planted fault: the CPU side one input late must differ
-    b0, n0 = chunks[len(chunks) // 2]
+    # the planted fault: the CPU side one input late must differ, on a window
+    # where erff varies (a rank's own share may lie where it is +-1 throughout)
+    b0, n0 = 0x3F000000, 1 << 20
     planted = M.count_nonzero(M.binary(M.opNe, Run.erff_map(b0, n0), M.of_numpy(O.erff_range(b0 + 1, n0), M.dtU32)))
     total = S.sum_over_ranks(dist, bad)
     caught = S.sum_over_ranks(dist, 1 if planted else 0)
