@@ -5,6 +5,7 @@
 // StablehloMlx/Kernels/Run.lean:62-104. Built with -fmad=false: every fused
 // multiply-add below is an explicit __fmaf_rn where ggml uses vfmaq_f32, and
 // every other product and sum is rounded on its own.
+#include <atomic>
 #include <cmath>
 
 #include "common.cuh"
@@ -1190,33 +1191,83 @@ __global__ void g_silu(const float *__restrict__ x, float *__restrict__ y, int64
 // gelu_erf: Shaders.lean:186-199 (ggml_vec_gelu_erf_f32):
 // y = (0.5f*x) * (1.0f + erff(x*SQRT_2_INV)) with the correctly rounded erff; a
 // NaN input returns itself quieted, as every arm64 step does.
-__device__ __forceinline__ float gelu_one(float v, int gpu_erf, const shlo_erf::ErfSmem *t) {
-  float ev;
-  if (gpu_erf) {
-    // The planted fault: GELU's tanh form (SQRT_2_OVER_PI, GELU_COEF_A of vec.h).
-    ev = tanhf(__fmul_rn(__fmul_rn(bitsf(0x3F4C422Au), v),
-                         __fadd_rn(1.0f, __fmul_rn(__fmul_rn(bitsf(0x3D372713u), v), v))));
-  } else {
-    ev = shlo_erf::erff_cr_smem(__fmul_rn(v, bitsf(0x3F3504F3u)), t);
-  }
-  float r = __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, ev));
+__device__ __forceinline__ float gelu_nan(float v, float r) {
   const uint32_t b = fbits(v);
-  if ((b & 0x7FFFFFFFu) > 0x7F800000u) r = bitsf(b | 0x00400000u);
-  else if (r != r) r = bitsf(0x7FC00000u);  // -inf * 0: arm64's default NaN
+  if ((b & 0x7FFFFFFFu) > 0x7F800000u) return bitsf(b | 0x00400000u);
+  if (r != r) return bitsf(0x7FC00000u);  // -inf * 0: arm64's default NaN
   return r;
 }
 
-__global__ void g_gelu_erf(const float *__restrict__ x, float *__restrict__ y, int64_t n, int gpu_erf) {
+__device__ __forceinline__ float gelu_of(float v, float ev) {
+  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, ev));
+}
+
+// The planted fault: GELU's tanh form (SQRT_2_OVER_PI, GELU_COEF_A of vec.h).
+__device__ __forceinline__ float gelu_tanh_one(float v) {
+  const float ev = tanhf(__fmul_rn(__fmul_rn(bitsf(0x3F4C422Au), v),
+                                   __fadd_rn(1.0f, __fmul_rn(__fmul_rn(bitsf(0x3D372713u), v), v))));
+  return gelu_nan(v, gelu_of(v, ev));
+}
+
+// Four values: erff's Taylor path as straight-line code for the four, then the
+// NaN rules for the values erff took out of that path (an infinite or NaN input
+// is out of its range; for the rest the product is finite). The binary32 steps
+// run two values a packed instruction, each lane the scalar operation.
+__device__ __forceinline__ float4 gelu4(float4 v4, const shlo_erf::ErfSmem *t) {
+  const float2 v01 = make_float2(v4.x, v4.y), v23 = make_float2(v4.z, v4.w);
+  const float2 k = make_float2(bitsf(0x3F3504F3u), bitsf(0x3F3504F3u));
+  const float2 x01 = __fmul2_rn(v01, k), x23 = __fmul2_rn(v23, k);
+  const float x[4] = {x01.x, x01.y, x23.x, x23.y};
+  float ev[4];
+  const unsigned rare = shlo_erf::erff4_smem(x, ev, t);
+  const float2 h = make_float2(0.5f, 0.5f), one = make_float2(1.0f, 1.0f);
+  const float2 r01 = __fmul2_rn(__fmul2_rn(h, v01), __fadd2_rn(one, make_float2(ev[0], ev[1])));
+  const float2 r23 = __fmul2_rn(__fmul2_rn(h, v23), __fadd2_rn(one, make_float2(ev[2], ev[3])));
+  float r[4] = {r01.x, r01.y, r23.x, r23.y};
+  if (rare) {
+    const float v[4] = {v4.x, v4.y, v4.z, v4.w};
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+      if (rare & (1u << i)) r[i] = gelu_nan(v[i], r[i]);
+  }
+  return make_float4(r[0], r[1], r[2], r[3]);
+}
+
+// A grid-stride loop over 16-byte vectors, the next vector's load issued before
+// the current one is computed; 64 registers a thread, so that four blocks of 256
+// threads stay resident on a multiprocessor (a few spills, on the rare path).
+__global__ void __launch_bounds__(256, 4) g_gelu_erf(const float *__restrict__ x, float *__restrict__ y, int64_t n, int gpu_erf) {
   __shared__ shlo_erf::ErfSmem tab;
   shlo_erf::erf_smem_load(&tab);
   __syncthreads();
   const shlo_erf::ErfSmem *t = &tab;
-  map_f32(x, y, n, [gpu_erf, t](float v) { return gelu_one(v, gpu_erf, t); });
+  if (gpu_erf) {
+    map_f32(x, y, n, [](float v) { return gelu_tanh_one(v); });
+    return;
+  }
+  const int64_t nv = n >> 2;
+  const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
+  const float4 *xv = reinterpret_cast<const float4 *>(x);
+  float4 *yv = reinterpret_cast<float4 *>(y);
+  int64_t i = t0;
+  if (i < nv) {
+    float4 cur = __ldg(xv + i);
+    for (; i + stride < nv; i += stride) {
+      const float4 nxt = __ldg(xv + i + stride);
+      yv[i] = gelu4(cur, t);
+      cur = nxt;
+    }
+    yv[i] = gelu4(cur, t);
+  }
+  for (int64_t j = 4 * nv + t0; j < n; j += stride) {
+    const float v = x[j];
+    y[j] = gelu_nan(v, gelu_of(v, shlo_erf::erff_cr_smem(__fmul_rn(v, bitsf(0x3F3504F3u)), t)));
+  }
 }
 
 // erff_map: Shaders.lean:204-208: y[t] = bits(erff(bits^-1(base + t))), four
 // consecutive patterns per thread and trip, stored as one 16-byte vector.
-__global__ void g_erff_map(uint32_t base, int64_t n, uint32_t *__restrict__ y) {
+__global__ void __launch_bounds__(256, 4) g_erff_map(uint32_t base, int64_t n, uint32_t *__restrict__ y) {
   __shared__ shlo_erf::ErfSmem tab;
   shlo_erf::erf_smem_load(&tab);
   __syncthreads();
@@ -1225,9 +1276,10 @@ __global__ void g_erff_map(uint32_t base, int64_t n, uint32_t *__restrict__ y) {
   const int64_t t0 = (int64_t)blockIdx.x * blockDim.x + threadIdx.x, stride = (int64_t)gridDim.x * blockDim.x;
   for (int64_t i = t0; i < nv; i += stride) {
     const uint32_t p = base + (uint32_t)(4 * i);
-    reinterpret_cast<uint4 *>(y)[i] =
-        make_uint4(fbits(shlo_erf::erff_cr_smem(bitsf(p), t)), fbits(shlo_erf::erff_cr_smem(bitsf(p + 1u), t)),
-                   fbits(shlo_erf::erff_cr_smem(bitsf(p + 2u), t)), fbits(shlo_erf::erff_cr_smem(bitsf(p + 3u), t)));
+    const float x[4] = {bitsf(p), bitsf(p + 1u), bitsf(p + 2u), bitsf(p + 3u)};
+    float r[4];
+    shlo_erf::erff4_smem(x, r, t);
+    reinterpret_cast<uint4 *>(y)[i] = make_uint4(fbits(r[0]), fbits(r[1]), fbits(r[2]), fbits(r[3]));
   }
   for (int64_t j = 4 * nv + t0; j < n; j += stride) y[j] = fbits(shlo_erf::erff_cr_smem(bitsf(base + (uint32_t)j), t));
 }
@@ -1349,6 +1401,21 @@ static int launch_ew(Device *dev, int64_t n, K kernel, const char *what, Args...
   return launch_check(what);
 }
 
+// The erf kernels stage a 16 KB table in every block, so they run one resident
+// wave of blocks over a grid-stride loop rather than launch_ew's 16 a
+// multiprocessor.
+template <typename K, typename... Args>
+static int launch_erf(Device *dev, int64_t n, K kernel, std::atomic<int> *per_sm, const char *what, Args... args) {
+  if (n <= 0) return 0;
+  int b = per_sm->load();
+  if (b == 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&b, kernel, 256, 0) != cudaSuccess || b < 1) b = 1;
+    per_sm->store(b);
+  }
+  kernel<<<grid_for(n, 256, dev, b), 256, 0, dev->stream>>>(args...);
+  return launch_check(what);
+}
+
 static int simple_out(Device *dev, int dt, int64_t n, Arr **o) {
   int64_t shape[1] = {n};
   return new_array(dev, (uint8_t)dt, shape, 1, o);
@@ -1375,7 +1442,10 @@ int k_gelu_erf(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
                 "(this backend carries the correctly rounded erff of the pinned build)");
   Arr *o;
   SHLO_TRY(simple_out(dev, kF32, n, &o));
-  if (launch_ew(dev, n, g_gelu_erf, "gelu_erf", (const float *)data_ptr(x), (float *)o->buf->ptr, n, (int)(p[1] != 0))) {
+  static std::atomic<int> per_sm{0};
+  const int rc = launch_erf(dev, n, g_gelu_erf, &per_sm, "gelu_erf", (const float *)data_ptr(x), (float *)o->buf->ptr,
+                            n, (int)(p[1] != 0));
+  if (rc) {
     shlo_release(o);
     return 1;
   }
@@ -1387,7 +1457,9 @@ int k_erff_map(Device *dev, const uint32_t *p, Arr **out) {
   int64_t n = p[1];
   Arr *o;
   SHLO_TRY(simple_out(dev, kU32, n, &o));
-  if (launch_ew(dev, n, g_erff_map, "erff_map", p[0], n, (uint32_t *)o->buf->ptr)) {
+  static std::atomic<int> per_sm{0};
+  const int rc = launch_erf(dev, n, g_erff_map, &per_sm, "erff_map", p[0], n, (uint32_t *)o->buf->ptr);
+  if (rc) {
     shlo_release(o);
     return 1;
   }
