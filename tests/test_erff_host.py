@@ -2,9 +2,10 @@
 the oracle (erfl with binary128 hard cases) -- no GPU needed.
 
 Both paths of contract-stablehlo-mlx_b200/csrc/erff_cr.cuh are checked: the
-fast path (piecewise binary64 polynomials + rounding test), exhaustively below
-4, and the double-double series alone, which the fast path falls back to near
-rounding midpoints. The host build runs the same arithmetic as the device.
+fast path (the binary64 Taylor expansion about the table's row centres + the
+rounding test), exhaustively below 4, and the double-double series alone, which
+the fast path falls back to near rounding midpoints. The host build runs the
+same arithmetic as the device.
 """
 import ctypes
 import os
@@ -86,7 +87,7 @@ def test_nan_inf_zero(host):
 @pytest.mark.slow
 def test_exhaustive_below_4(host):
     """Every non-negative binary32 input below 4 (the rest is +-1, NaN or a sign
-    flip), in chunks of 2^24: the polynomial fast path with its rounding test,
+    flip), in chunks of 2^24: the Taylor fast path with its rounding test,
     and the series behind it, against the oracle's erfl/binary128 rounding."""
     n_threads = max(1, os.cpu_count() or 1)
     chunk = 1 << 24

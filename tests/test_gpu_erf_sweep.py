@@ -4,7 +4,7 @@ all 2^32 binary32 inputs, NaN, infinities and subnormals included.
 Chunk by chunk (2^24 inputs), the GPU kernel erff_map is compared on the
 device with the oracle's correctly rounded erff computed on the host cores
 (erfl, with binary128 re-evaluation near rounding midpoints: a method
-independent of the kernel's piecewise binary64 polynomials): `binary ne` then
+independent of the kernel's binary64 Taylor expansion): `binary ne` then
 `count_nonzero`, as the reference does. Then the planted fault: the CPU side
 shifted by one input must differ.
 """
