@@ -64,6 +64,10 @@ struct Device {
   // listed in `capture_allocs`; blocks the capture frees go to `capture_free`
   // and are reused only by later allocations of the same capture (the graph is
   // one linear chain of nodes, so stream order makes that reuse safe).
+  // Set by a kernel that gave up a bounded wait (mul_mat's stage pipeline): a
+  // word of mapped pinned host memory, read after the device's stream drains.
+  int *pipe_err_host = nullptr;
+  int *pipe_err_dev = nullptr;
   bool capturing = false;
   void *capture_owner = nullptr;
   std::vector<std::pair<void *, size_t>> *capture_allocs = nullptr;

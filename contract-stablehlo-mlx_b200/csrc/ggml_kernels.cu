@@ -300,6 +300,36 @@ static int mm_path() {
   return 0;
 }
 
+// A 2-D tensor map of a packed operand ([outer][inner] floats, rows of `inner`),
+// box box_inner x 16 rows, no swizzle, zero fill outside (never reached: the
+// packed operands are padded to whole tiles). cuTensorMapEncodeTiled is reached
+// through the runtime, so the library links no driver library.
+using EncodeTiledFn = CUresult (*)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                   const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static int tensor_map_2d(CUtensorMap *map, const float *base, uint64_t inner, uint64_t outer, uint32_t box_inner) {
+  static const EncodeTiledFn fn = [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &f, 12000, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess)
+      f = nullptr;
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  if (!fn) return fail("mul_mat: the driver's cuTensorMapEncodeTiled is not available");
+  const cuuint64_t dims[2] = {inner, outer};
+  const cuuint64_t strides[1] = {inner * sizeof(float)};
+  const cuuint32_t box[2] = {box_inner, (cuuint32_t)mt::BK};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float *>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail("mul_mat: tensor map of %llu x %llu floats (box %u x %d): driver error %d", (unsigned long long)outer,
+                (unsigned long long)inner, box_inner, mt::BK, (int)r);
+  return 0;
+}
+
 static int pack_operand(Device *dev, const float *src, int rows, int K, int64_t src_batch, int batches, int seg,
                         int segp, int rows_p, float pad, Buffer **out) {
   // k_mm_pack writes whole blocks of 64 rows
@@ -514,12 +544,23 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
   }
   a.park = (float *)park->ptr;
   a.ctr = shared_tile ? (int *)ctr->ptr : nullptr;
+  a.err = dev->pipe_err_dev;
+  CUtensorMap tw, tx;
+  if (tensor_map_2d(&tw, a.wp, (uint64_t)Mp, (uint64_t)Wb * 16 * segp, (uint32_t)BM) ||
+      tensor_map_2d(&tx, a.xp, (uint64_t)Np, (uint64_t)Bx * 16 * segp, (uint32_t)BN)) {
+    buffer_release(park);
+    buffer_release(ctr);
+    buffer_release(wpk);
+    buffer_release(xpk);
+    shlo_release(o);
+    return 1;
+  }
   const bool stage_fold = segp % 16 == 0;
-  if (split == 16) launch_mul_mat_tm<16>(WM, stage_fold, ep != 0, grid, dev->stream, a);
-  else if (split == 8) launch_mul_mat_tm<8>(WM, stage_fold, ep != 0, grid, dev->stream, a);
-  else if (split == 4) launch_mul_mat_tm<4>(WM, stage_fold, ep != 0, grid, dev->stream, a);
-  else if (split == 2) launch_mul_mat_tm<2>(WM, stage_fold, ep != 0, grid, dev->stream, a);
-  else launch_mul_mat_tm<1>(WM, stage_fold, ep != 0, grid, dev->stream, a);
+  if (split == 16) launch_mul_mat_tm<16>(WM, stage_fold, ep != 0, grid, dev->stream, a, tw, tx);
+  else if (split == 8) launch_mul_mat_tm<8>(WM, stage_fold, ep != 0, grid, dev->stream, a, tw, tx);
+  else if (split == 4) launch_mul_mat_tm<4>(WM, stage_fold, ep != 0, grid, dev->stream, a, tw, tx);
+  else if (split == 2) launch_mul_mat_tm<2>(WM, stage_fold, ep != 0, grid, dev->stream, a, tw, tx);
+  else launch_mul_mat_tm<1>(WM, stage_fold, ep != 0, grid, dev->stream, a, tw, tx);
   int rc = launch_check("mul_mat");
   buffer_release(park);
   buffer_release(ctr);

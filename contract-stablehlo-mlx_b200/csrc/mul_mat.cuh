@@ -5,6 +5,8 @@
 // SHLO_MUL_MAT_INSTANCES; ggml_kernels.cu calls them through the launchers
 // declared at the end.
 #pragma once
+#include <cuda.h>  // CUtensorMap (the type only; the encoder is reached through the runtime)
+
 #include <utility>
 
 #include "common.cuh"
@@ -67,6 +69,50 @@ __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
+// mbarriers and TMA tile copies (k_mul_mat_tm's stage pipeline).
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+__device__ __forceinline__ void mbar_init(uint64_t *b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *b, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+__device__ __forceinline__ uint64_t global_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;\n" : "=l"(t));
+  return t;
+}
+// Wait for the phase of parity `parity` of barrier b, for at most about two
+// seconds, or until *abort is set (by another thread that gave up): false then.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *b, uint32_t parity, volatile int *abort) {
+  if (mbar_try_wait(b, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t i = 1;; i++) {
+    if (mbar_try_wait(b, parity)) return true;
+    if ((i & 255) == 0 && (*abort || global_ns() - t0 > 2000000000ull)) return false;
+  }
+}
+// A 2-D tile of the tensor map to shared memory, completing on barrier b.
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *b) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];\n" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(b))
+      : "memory");
+}
+
 
 // Invalidate the L2 lines of n floats at p (a multiple of 32 floats from a
 // 128-byte boundary) without writing them back: for scratch that was written
@@ -96,6 +142,7 @@ struct MMArgs {
   const float *res;   // [R][M]
   int ep;
   int *ctr;           // k_mul_mat_tm split over CTAs: arrivals per tile (0 between launches)
+  int *err;           // k_mul_mat_tm: set when a stage's copies did not arrive within the wait limit
 };
 
 
@@ -158,10 +205,11 @@ constexpr int LEVEL_FLOATS = THREADS * 64;
 template <int WM>
 struct Pipe {
   static constexpr int NS = WM == 2 ? 3 : 2;  // stages of BK k
-  static constexpr size_t SMEM = (size_t)NS * Tile<WM>::STAGE_FLOATS * 4 + (size_t)LEVEL_FLOATS * 4;
+  // + 128: the stages start on a 128-byte boundary (TMA destinations)
+  static constexpr size_t SMEM = (size_t)NS * Tile<WM>::STAGE_FLOATS * 4 + (size_t)LEVEL_FLOATS * 4 + 128;
   // A CTA that computes a quarter of the tree needs no level-2 slab: the same
   // shared memory holds more stages.
-  static constexpr int NS_QUARTER = (int)(SMEM / (Tile<WM>::STAGE_FLOATS * 4));
+  static constexpr int NS_QUARTER = (int)((SMEM - 128) / (Tile<WM>::STAGE_FLOATS * 4));
 };
 // Dynamic shared memory above a third of an SM's: at most two CTAs per SM, so
 // their TMEM columns (2 x 256) always fit the SM's 512.
@@ -270,8 +318,19 @@ __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, floa
 // add.
 // EPI: the fused bias / residual adds in the epilogue (a separate instance, so
 // the plain product compiles without them).
+//
+// The stages arrive by TMA: thread 0 copies stage st's w tile (BM x 16 k) and x
+// tile (BN x 16 k) from the tensor maps tw, tx of the packed operands into slot
+// st % NS, completing on the slot's full barrier; every warp waits on that
+// barrier, reads the stage, and arrives on the slot's empty barrier; once all
+// eight warps have, thread 0 refills the slot with stage st + NS. So no CTA-wide
+// barrier runs in the k-loop (a warp runs ahead while its stages are in), and no
+// thread computes copy addresses. Every wait is bounded: a stage that never
+// arrives (about two seconds) sets *a.err, the CTA waits (bounded) for its own
+// copies in flight, frees its TMEM and returns without writing.
 template <int WM, bool STAGE_FOLD, int SPLIT, bool EPI>
-__global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMArgs a) {
+__global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM)
+    k_mul_mat_tm(MMArgs a, const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx) {
   using namespace mt;
   constexpr int BM = Tile<WM>::BM, BN = Tile<WM>::BN, STAGE_FLOATS = Tile<WM>::STAGE_FLOATS;
   constexpr int SEGS = 16 / SPLIT;  // segments a CTA
@@ -280,8 +339,11 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
   constexpr bool NO_SLAB = SPLIT >= 4;
   constexpr int LAST_POPS = SPLIT == 4 ? 2 : SPLIT == 8 ? 1 : -1;
   constexpr int NS = NO_SLAB ? Pipe<WM>::NS_QUARTER : Pipe<WM>::NS;
-  extern __shared__ __align__(16) float smem[];
+  extern __shared__ __align__(128) float smem_raw[];
+  float *smem = reinterpret_cast<float *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~(uintptr_t)127);
   __shared__ uint32_t tmem_base;
+  __shared__ __align__(8) uint64_t full_bar[NS], empty_bar[NS];
+  __shared__ int abort_flag;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   // Warps WM (m) x 8/WM (r), lanes 8 (m) x 4 (r); a thread's m are mo + [0,4)
   // and mo + 32 + [0,4), its r are ro + [0,4) and ro + 16 + [0,4).
@@ -296,18 +358,31 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
     rl0 = (int64_t)((tile / mtiles) % a.r_tiles) * BN;
   };
   const int Kq = 16 * a.segp;
-  // CTA q of a tile reads packed k rows [q SEGS segp, (q + 1) SEGS segp).
+  // CTA q of a tile reads packed k rows [q SEGS segp, (q + 1) SEGS segp): the
+  // tile's rows in the tensor maps (w [Wb Kq][Mp], x [Bx Kq][Np]).
   const int kq0 = (int)(blockIdx.x % SPLIT) * SEGS * a.segp;
-  const float *wp, *xp;
+  int tm0, wrow0, tr0, xrow0;
   {
     int m0, bx;
     int64_t rl0;
     pos(m0, bx, rl0);
-    wp = a.wp + (a.wbs ? (int64_t)bx * Kq * a.Mp : 0) + (int64_t)kq0 * a.Mp + m0;
-    xp = a.xp + (int64_t)bx * Kq * a.Np + (int64_t)kq0 * a.Np + rl0;
+    tm0 = m0;
+    tr0 = (int)rl0;
+    wrow0 = (a.wbs ? bx * Kq : 0) + kq0;
+    xrow0 = bx * Kq + kq0;
   }
   const int nstages = Kq / SPLIT / BK;
 
+  if (tid == 0) {
+#pragma unroll
+    for (int q = 0; q < NS; q++) {
+      mbar_init(&full_bar[q], 1);
+      mbar_init(&empty_bar[q], THREADS / 32);
+    }
+    abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+  }
   if (warp == 0) {
     uint32_t slot = (uint32_t)__cvta_generic_to_shared(&tmem_base);
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(slot),
@@ -319,29 +394,19 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
   asm volatile("tcgen05.fence::after_thread_sync;\n");
   const uint32_t tcol = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(128 * (warp >> 2));
 
-  // Stage copies: this thread moves w rows tid / (BM/4) + j (1024/BM), x rows
-  // tid / (BN/4) + j (1024/BN), 16 bytes at column 4 (tid % (BM/4 or BN/4)).
-  // The addresses are rebuilt at every stage (once per 16 k) rather than kept
-  // live through the k-loop.
-  constexpr int WCP = BM / 64, XCP = BN / 64;  // 16-byte copies a thread a stage
-  auto issue = [&](int st) {
-    const int t = threadIdx.x;
-    float *sb = smem + (st % NS) * STAGE_FLOATS;
-    const int64_t k0 = (int64_t)st * BK;
-    const float *gw = wp + (k0 + t / (BM / 4)) * a.Mp + (t % (BM / 4)) * 4;
-    const float *gx = xp + (k0 + t / (BN / 4)) * a.Np + (t % (BN / 4)) * 4;
-    float *dw = sb + (t / (BM / 4)) * BM + (t % (BM / 4)) * 4;
-    float *dx = sb + BK * BM + (t / (BN / 4)) * BN + (t % (BN / 4)) * 4;
-#pragma unroll
-    for (int j = 0; j < WCP; j++) cp_async16(dw + j * (1024 / BM) * BM, gw + (int64_t)j * (1024 / BM) * a.Mp);
-#pragma unroll
-    for (int j = 0; j < XCP; j++) cp_async16(dx + j * (1024 / BN) * BN, gx + (int64_t)j * (1024 / BN) * a.Np);
+  // Thread 0's copies of stage st into slot q (both tiles on the slot's full
+  // barrier, which then expects their bytes).
+  auto issue = [&](int st, int q) {
+    float *sb = smem + q * STAGE_FLOATS;
+    mbar_expect_tx(&full_bar[q], STAGE_FLOATS * 4);
+    tma_load_2d(sb, &tw, tm0, wrow0 + st * BK, &full_bar[q]);
+    tma_load_2d(sb + BK * BM, &tx, tr0, xrow0 + st * BK, &full_bar[q]);
   };
-
-#pragma unroll
-  for (int s = 0; s < NS - 1; s++) {
-    if (s < nstages) issue(s);
-    cp_async_commit();
+  int nissued = 0;  // thread 0's count of stages copied
+  if (tid == 0) {
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tw) : "memory");
+    asm volatile("prefetch.tensormap [%0];\n" ::"l"(&tx) : "memory");
+    for (; nissued < NS && nissued < nstages; nissued++) issue(nissued, nissued);
   }
 
   // acc[j][i] (r index j, m index i) lives in pairs along m: acc2[4 j + i / 2].
@@ -381,16 +446,22 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
       for (int i = 0; i < 32; i++) acc2[i] = make_float2(0.0f, 0.0f);
     }
   };
-  int so = 0;  // offset of stage st % NS
-  // One stage: wait for its copies, start the copies NS - 1 stages ahead, and
-  // run its 16 k (after each group of 4 k, group_end()).
-  auto stage = [&](int st, auto group_end) {
-    cp_async_wait<NS - 2>();
-    __syncthreads();
-    if (st + NS - 1 < nstages) issue(st + NS - 1);
-    cp_async_commit();
-    const float *ws = smem + so + mo;
-    const float *xs = smem + so + BK * BM + ro;
+  int slot = 0;        // stage st's slot, st % NS
+  uint32_t phase = 0;  // the parity of st / NS
+  int next_wait = 0;   // the first stage this thread has not yet waited for
+  auto give_up = [&]() {
+    abort_flag = 1;
+    if (a.err) atomicExch(a.err, 1);
+    return false;
+  };
+  // One stage: wait for its copies, run its 16 k (after each group of 4 k,
+  // group_end()), release the slot, and (thread 0) refill it NS stages ahead.
+  auto stage = [&](int st, auto group_end) -> bool {
+    if (!mbar_wait_bounded(&full_bar[slot], phase, &abort_flag)) return give_up();
+    __syncwarp();  // the lanes left their waits apart; the folds' tcgen05 accesses need the warp whole
+    next_wait = st + 1;
+    const float *ws = smem + slot * STAGE_FLOATS + mo;
+    const float *xs = smem + slot * STAGE_FLOATS + BK * BM + ro;
 #pragma unroll
     for (int q = 0; q < GPS; q++) {
 #pragma unroll
@@ -412,25 +483,44 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
       }
       group_end();
     }
-    so = so + STAGE_FLOATS == NS * STAGE_FLOATS ? 0 : so + STAGE_FLOATS;
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty_bar[slot]);
+    if (tid == 0 && st + NS < nstages) {
+      if (!mbar_wait_bounded(&empty_bar[slot], phase, &abort_flag)) return give_up();
+      issue(st + NS, slot);
+      nissued++;
+    }
+    __syncwarp();
+    if (++slot == NS) {
+      slot = 0;
+      phase ^= 1;
+    }
+    return true;
   };
+  bool ok = true;
   if constexpr (STAGE_FOLD) {
     // Segments of whole stages: the fold between the segments' stage loops.
     const int sps = a.segp / BK;
-    for (int st = 0; S < SEGS;) {
-      for (int e = st + sps; st < e; st++) stage(st, [] {});
-      fold_segment();
+    for (int st = 0; ok && S < SEGS;) {
+      for (int e = st + sps; ok && st < e; st++) ok = stage(st, [] {});
+      if (ok) fold_segment();
     }
   } else {
-    for (int st = 0; st < nstages; st++)
-      stage(st, [&] {
+    for (int st = 0; ok && st < nstages; st++)
+      ok = stage(st, [&] {
         if (--gleft == 0) {
           gleft = a.segp / 4;
           fold_segment();
         }
       });
   }
-  cp_async_wait<0>();
+  if (!ok && tid == 0) {
+    // Gave up: wait (bounded) for this CTA's copies still in flight before its
+    // shared memory is released.
+    __shared__ int never;
+    never = 0;
+    for (int q = next_wait; q < nissued; q++) mbar_wait_bounded(&full_bar[q % NS], (q / NS) & 1, &never);
+  }
 
   // Every TMEM access of this CTA is complete (each waited): free the columns.
   asm volatile("tcgen05.fence::before_thread_sync;\n");
@@ -438,6 +528,7 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM) k_mul_mat_tm(MMA
   asm volatile("tcgen05.fence::after_thread_sync;\n");
   if (warp == 0)
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_base), "n"(TMEM_COLS));
+  if (abort_flag) return;  // read after the barrier: the same for every thread
 
   if (SPLIT > 1) {
     // This CTA's subtree to its slice; the last of the tile's CTAs adds the top
@@ -738,8 +829,11 @@ __global__ void __launch_bounds__(ms::THREADS, 2) k_mul_mat_short(MMArgs a) {
 // mul_mat_tm_attributes<SPLIT>(). Errors are left for cudaGetLastError.
 template <int SPLIT>
 cudaError_t mul_mat_tm_attributes();
+// tw, tx: the tensor maps of the packed w ([Wb Kq][Mp], box Tile<WM>::BM x 16)
+// and x ([Bx Kq][Np], box Tile<WM>::BN x 16).
 template <int SPLIT>
-void launch_mul_mat_tm(int WM, bool stage_fold, bool epi, unsigned grid, cudaStream_t stream, const MMArgs &a);
+void launch_mul_mat_tm(int WM, bool stage_fold, bool epi, unsigned grid, cudaStream_t stream, const MMArgs &a,
+                       const CUtensorMap &tw, const CUtensorMap &tx);
 // k_mul_mat_short<EPI, NG> with NG = ng (1..4).
 void launch_mul_mat_short(int ng, bool epi, unsigned grid, cudaStream_t stream, const MMArgs &a);
 // k_mul_mat_seg<EPI> (mul_mat_seg.cu): small products, 32 m x 32 r tiles.
@@ -767,11 +861,12 @@ cudaError_t mul_mat_tm_attributes() {
 }
 
 template <int SPLIT>
-void launch_mul_mat_tm(int WM, bool stage_fold, bool epi, unsigned grid, cudaStream_t stream, const MMArgs &a) {
+void launch_mul_mat_tm(int WM, bool stage_fold, bool epi, unsigned grid, cudaStream_t stream, const MMArgs &a,
+                       const CUtensorMap &tw, const CUtensorMap &tx) {
   const size_t smem = WM == 1 ? mt::Pipe<1>::SMEM : mt::Pipe<2>::SMEM;
-#define SHLO_TM(WMv, SF)                                                             \
-  (epi ? k_mul_mat_tm<WMv, SF, SPLIT, true><<<grid, mt::THREADS, smem, stream>>>(a) \
-       : k_mul_mat_tm<WMv, SF, SPLIT, false><<<grid, mt::THREADS, smem, stream>>>(a))
+#define SHLO_TM(WMv, SF)                                                                     \
+  (epi ? k_mul_mat_tm<WMv, SF, SPLIT, true><<<grid, mt::THREADS, smem, stream>>>(a, tw, tx) \
+       : k_mul_mat_tm<WMv, SF, SPLIT, false><<<grid, mt::THREADS, smem, stream>>>(a, tw, tx))
   if (WM == 1) {
     if (stage_fold) SHLO_TM(1, true);
     else SHLO_TM(1, false);

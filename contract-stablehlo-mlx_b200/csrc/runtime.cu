@@ -98,6 +98,9 @@ static int init_device(int id, Device **out) {
     SHLO_CUDA(cudaDeviceGetAttribute(&d->sm_count, cudaDevAttrMultiProcessorCount, id));
     SHLO_CUDA(cudaStreamCreateWithFlags(&d->stream, cudaStreamNonBlocking));
     SHLO_CUDA(cudaStreamCreateWithFlags(&d->copy, cudaStreamNonBlocking));
+    SHLO_CUDA(cudaHostAlloc((void **)&d->pipe_err_host, sizeof(int), cudaHostAllocMapped));
+    *d->pipe_err_host = 0;
+    SHLO_CUDA(cudaHostGetDevicePointer((void **)&d->pipe_err_dev, d->pipe_err_host, 0));
     g_devs[id] = d;
   }
   *out = g_devs[id];
@@ -400,7 +403,15 @@ static int wait_stream(Device *dev, cudaStream_t stream, const char *what) {
   auto t0 = std::chrono::steady_clock::now();
   for (int spins = 0;; spins++) {
     cudaError_t e = cudaStreamQuery(stream);
-    if (e == cudaSuccess) return 0;
+    if (e == cudaSuccess) {
+      volatile int *perr = dev->pipe_err_host;
+      if (perr && *perr) {
+        *perr = 0;
+        return fail("%s: a mul_mat launch on device %d gave up waiting for its stage copies (the results are "
+                    "not valid)", what, dev->id);
+      }
+      return 0;
+    }
     if (e != cudaErrorNotReady) return cuda_check(e, what);
     double dt = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     if (dt > limit) return fail("%s: device %d did not finish within %.0f s", what, dev->id, limit);
