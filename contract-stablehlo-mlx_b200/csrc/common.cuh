@@ -191,8 +191,8 @@ enum KernelKind {
   KK_F64_OF_F32, KK_F32_OF_F64, KK_MUL_MAT_EP, KK_NORM_AFFINE, KK_ATTENTION
 };
 // mul_mat's fused epilogue (k_mul_mat_ep): + bias[m] (its own operand order),
-// then + res[r][m].
-enum { EP_BIAS = 1, EP_BIAS_LHS = 2, EP_RES = 4, EP_RES_LHS = 8 };
+// then + res[r][m], then gelu_erf (the pinned build's).
+enum { EP_BIAS = 1, EP_BIAS_LHS = 2, EP_RES = 4, EP_RES_LHS = 8, EP_GELU = 16 };
 
 // ---- recording a compiled function: the op log and its fusions (fusion.cu) ----
 // Entry points that read array data open a TraceScope. While the recorder logs

@@ -45,7 +45,7 @@ namespace {
 enum { ROLE_NONE = -1 };
 enum GroupKind { G_DENSE = 1, G_NORM, G_ATTN };
 // roles inside a chain
-enum { R_MM = 0, R_BIAS, R_RES, R_NORM = 0, R_GAIN, R_BETA, R_CQ = 0, R_CK, R_SCORES, R_SOFTMAX, R_CV, R_VALUE, R_COPY_OUT };
+enum { R_MM = 0, R_BIAS, R_RES, R_GELU, R_NORM = 0, R_GAIN, R_BETA, R_CQ = 0, R_CK, R_SCORES, R_SOFTMAX, R_CV, R_VALUE, R_COPY_OUT };
 
 struct TIn {
   uint64_t buf = 0;  // storage serial (0: no storage)
@@ -249,6 +249,7 @@ struct Tracer {
       g.flags = EP_BIAS | (y == 1 ? EP_BIAS_LHS : 0);
       for (int k = 0; k < 6; k++) g.p[k] = o.p[k];
       std::vector<std::pair<int, int>> mem = {{i, R_MM}, {j, R_BIAS}};
+      uint64_t result = a.out;  // the chain's result so far
       const int k = single(a.out);
       if (k >= 0 && ops[k].kind == TK_BINARY && ops[k].sub == 0 && ops[k].in.size() == 2 && ops[k].out_dtype == kF32) {
         const TOp &r = ops[k];
@@ -258,8 +259,18 @@ struct Tracer {
           if (h.buf != a.out && h.dtype == kF32 && row_major(h) && count_of(h) == R * M) {
             g.flags |= EP_RES | (t == 1 ? EP_RES_LHS : 0);
             mem.push_back({k, R_RES});
+            result = r.out;
           }
         }
+      }
+      // then gelu_erf of the whole result (the pinned build's: the stock one is
+      // refused, unfused, with its own message)
+      const int q = single(result);
+      if (q >= 0 && ops[q].kind == TK_KERNEL && ops[q].sub == KK_GELU_ERF && ops[q].np >= 2 &&
+          ops[q].p[0] == (uint32_t)(R * M) && ops[q].p[1] == 0 && current_flavor() == 0 && !ops[q].in.empty() &&
+          full_view(ops[q].in[0], result, R * M)) {
+        g.flags |= EP_GELU;
+        mem.push_back({q, R_GELU});
       }
       g.p[6] = (uint32_t)g.flags;
       take(g, mem);
@@ -492,10 +503,12 @@ struct Tracer {
           if (g.h[2]) shlo_release(g.h[2]);
           g.h[2] = b;
         }
-      } else {
+      } else if (role == R_RES) {
         const int t = chained(g, R_BIAS, ins[0]) ? 0 : chained(g, R_BIAS, ins[1]) ? 1 : -1;
         ok = t >= 0 && ((g.flags & EP_RES_LHS) != 0) == (t == 1);
         if (ok) keep(g, 3, ins[1 - t]);
+      } else {  // gelu_erf of the chain's result
+        ok = n >= 1 && chained(g, (g.flags & EP_RES) ? R_RES : R_BIAS, ins[0]);
       }
     } else if (g.kind == G_NORM) {
       if (role == R_NORM) {

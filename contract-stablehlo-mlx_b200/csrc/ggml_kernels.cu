@@ -12,6 +12,7 @@
 #include <utility>
 
 #include "erff_cr.cuh"
+#include "gelu.cuh"
 #include "ggml_math.cuh"
 #include "mul_mat.cuh"
 
@@ -348,7 +349,11 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
   return k_mul_mat_ep(dev, w, x, p, nullptr, nullptr, 0, out);
 }
 
-int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr *res, int ep, Arr **out) {
+// The product with its fused epilogue. *gelu_done (when EP_GELU is asked for)
+// is set when k_mul_mat_tm ran gelu_erf in its epilogue; the other paths leave
+// it to the caller.
+static int mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr *res, int ep, Arr **out,
+                      bool *gelu_done) {
   const int64_t K = p[0], M = p[1], R = p[2], wbs = p[3], N = p[4];
   const int plain = p[5] != 0;
   if ((ep & EP_BIAS) && (!bias || require_dtype(bias, kF32, "mul_mat bias") || check_elems(bias, M, "mul_mat bias")))
@@ -556,11 +561,16 @@ int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr 
     return 1;
   }
   const bool stage_fold = segp % 16 == 0;
-  if (split == 16) launch_mul_mat_tm<16>(WM, stage_fold, ep != 0, grid, dev->stream, a, tw, tx);
-  else if (split == 8) launch_mul_mat_tm<8>(WM, stage_fold, ep != 0, grid, dev->stream, a, tw, tx);
-  else if (split == 4) launch_mul_mat_tm<4>(WM, stage_fold, ep != 0, grid, dev->stream, a, tw, tx);
-  else if (split == 2) launch_mul_mat_tm<2>(WM, stage_fold, ep != 0, grid, dev->stream, a, tw, tx);
-  else launch_mul_mat_tm<1>(WM, stage_fold, ep != 0, grid, dev->stream, a, tw, tx);
+  int epi = ep != 0;
+  if ((ep & EP_GELU) && WM == 2) {
+    epi = 2;
+    *gelu_done = true;
+  }
+  if (split == 16) launch_mul_mat_tm<16>(WM, stage_fold, epi, grid, dev->stream, a, tw, tx);
+  else if (split == 8) launch_mul_mat_tm<8>(WM, stage_fold, epi, grid, dev->stream, a, tw, tx);
+  else if (split == 4) launch_mul_mat_tm<4>(WM, stage_fold, epi, grid, dev->stream, a, tw, tx);
+  else if (split == 2) launch_mul_mat_tm<2>(WM, stage_fold, epi, grid, dev->stream, a, tw, tx);
+  else launch_mul_mat_tm<1>(WM, stage_fold, epi, grid, dev->stream, a, tw, tx);
   int rc = launch_check("mul_mat");
   buffer_release(park);
   buffer_release(ctr);
@@ -740,6 +750,29 @@ __global__ void g_soft_max(const float *__restrict__ x, float *__restrict__ y, i
     }
     __syncwarp();
   }
+}
+
+
+static const char kGeluStockRefusal[] =
+    "gelu_erf: the stock build's erff is Apple libsystem_m's platform erff, which is not carried "
+    "(this backend carries the correctly rounded erff of the pinned build)";
+
+int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr *res, int ep, Arr **out) {
+  if (!(ep & EP_GELU)) return mul_mat_ep(dev, w, x, p, bias, res, ep, out, nullptr);
+  if (current_flavor() == 1) return fail("%s", kGeluStockRefusal);
+  bool done = false;
+  Arr *o;
+  SHLO_TRY(mul_mat_ep(dev, w, x, p, bias, res, ep, &o, &done));
+  if (done) {
+    *out = o;
+    return 0;
+  }
+  // The product (with its adds) by a kernel without the gelu epilogue: the
+  // gelu_erf kernel on its result, the same bits.
+  const uint32_t gp[2] = {(uint32_t)((int64_t)p[2] * p[1]), 0};
+  const int rc = k_gelu_erf(dev, o, gp, out);
+  shlo_release(o);
+  return rc;
 }
 
 int k_soft_max(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
@@ -1229,49 +1262,12 @@ __global__ void g_silu(const float *__restrict__ x, float *__restrict__ y, int64
   map_f32(x, y, n, [gpu_ops](float v) { return silu_one(v, gpu_ops); });
 }
 
-// gelu_erf: Shaders.lean:186-199 (ggml_vec_gelu_erf_f32):
-// y = (0.5f*x) * (1.0f + erff(x*SQRT_2_INV)) with the correctly rounded erff; a
-// NaN input returns itself quieted, as every arm64 step does.
-__device__ __forceinline__ float gelu_nan(float v, float r) {
-  const uint32_t b = fbits(v);
-  if ((b & 0x7FFFFFFFu) > 0x7F800000u) return bitsf(b | 0x00400000u);
-  if (r != r) return bitsf(0x7FC00000u);  // -inf * 0: arm64's default NaN
-  return r;
-}
-
-__device__ __forceinline__ float gelu_of(float v, float ev) {
-  return __fmul_rn(__fmul_rn(0.5f, v), __fadd_rn(1.0f, ev));
-}
-
+// gelu_erf: Shaders.lean:186-199 (gelu.cuh has the arithmetic).
 // The planted fault: GELU's tanh form (SQRT_2_OVER_PI, GELU_COEF_A of vec.h).
 __device__ __forceinline__ float gelu_tanh_one(float v) {
   const float ev = tanhf(__fmul_rn(__fmul_rn(bitsf(0x3F4C422Au), v),
                                    __fadd_rn(1.0f, __fmul_rn(__fmul_rn(bitsf(0x3D372713u), v), v))));
   return gelu_nan(v, gelu_of(v, ev));
-}
-
-// Four values: erff's Taylor path as straight-line code for the four, then the
-// NaN rules for the values erff took out of that path (an infinite or NaN input
-// is out of its range; for the rest the product is finite). The binary32 steps
-// run two values a packed instruction, each lane the scalar operation.
-__device__ __forceinline__ float4 gelu4(float4 v4, const shlo_erf::ErfSmem *t) {
-  const float2 v01 = make_float2(v4.x, v4.y), v23 = make_float2(v4.z, v4.w);
-  const float2 k = make_float2(bitsf(0x3F3504F3u), bitsf(0x3F3504F3u));
-  const float2 x01 = __fmul2_rn(v01, k), x23 = __fmul2_rn(v23, k);
-  const float x[4] = {x01.x, x01.y, x23.x, x23.y};
-  float ev[4];
-  const unsigned rare = shlo_erf::erff4_smem(x, ev, t);
-  const float2 h = make_float2(0.5f, 0.5f), one = make_float2(1.0f, 1.0f);
-  const float2 r01 = __fmul2_rn(__fmul2_rn(h, v01), __fadd2_rn(one, make_float2(ev[0], ev[1])));
-  const float2 r23 = __fmul2_rn(__fmul2_rn(h, v23), __fadd2_rn(one, make_float2(ev[2], ev[3])));
-  float r[4] = {r01.x, r01.y, r23.x, r23.y};
-  if (rare) {
-    const float v[4] = {v4.x, v4.y, v4.z, v4.w};
-#pragma unroll
-    for (int i = 0; i < 4; i++)
-      if (rare & (1u << i)) r[i] = gelu_nan(v[i], r[i]);
-  }
-  return make_float4(r[0], r[1], r[2], r[3]);
 }
 
 // A grid-stride loop over 16-byte vectors, the next vector's load issued before
@@ -1479,8 +1475,7 @@ int k_gelu_erf(Device *dev, Arr *x, const uint32_t *p, Arr **out) {
   int64_t n = p[0];
   SHLO_TRY(require_dtype(x, kF32, "gelu_erf") || check_elems(x, n, "gelu_erf"));
   if (current_flavor() == 1 && p[1] == 0)
-    return fail("gelu_erf: the stock build's erff is Apple libsystem_m's platform erff, which is not carried "
-                "(this backend carries the correctly rounded erff of the pinned build)");
+    return fail("%s", kGeluStockRefusal);
   Arr *o;
   SHLO_TRY(simple_out(dev, kF32, n, &o));
   static std::atomic<int> per_sm{0};

@@ -10,6 +10,7 @@
 #include <utility>
 
 #include "common.cuh"
+#include "gelu.cuh"
 #include "ggml_math.cuh"
 
 namespace shlo {
@@ -316,8 +317,10 @@ __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, floa
 // fill a grid that would leave SMs idle (small products: few rows or few
 // tiles). SPLIT = 1: one CTA a tile, T(0..7) parked in a.park until the root
 // add.
-// EPI: the fused bias / residual adds in the epilogue (a separate instance, so
-// the plain product compiles without them).
+// EPI: 0 the plain product; 1 the fused bias / residual adds in the epilogue;
+// 2 those adds and then gelu_erf (WM = 2), the tile passing through shared
+// memory so that each warp finishes whole rows (separate instances, so the
+// plain product compiles without them).
 //
 // The stages arrive by TMA: thread 0 copies stage st's w tile (BM x 16 k) and x
 // tile (BN x 16 k) from the tensor maps tw, tx of the packed operands into slot
@@ -328,7 +331,7 @@ __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, floa
 // thread computes copy addresses. Every wait is bounded: a stage that never
 // arrives (about two seconds) sets *a.err, the CTA waits (bounded) for its own
 // copies in flight, frees its TMEM and returns without writing.
-template <int WM, bool STAGE_FOLD, int SPLIT, bool EPI>
+template <int WM, bool STAGE_FOLD, int SPLIT, int EPI>
 __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM)
     k_mul_mat_tm(MMArgs a, const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx) {
   using namespace mt;
@@ -590,7 +593,62 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM)
   pos(m0, bx, rl0);
   const int64_t rbase = (int64_t)bx * a.Nx;
   const bool vec = (a.M & 3) == 0;
-  if constexpr (EPI) {
+  if constexpr (EPI == 2) {
+    // The tile through shared memory (the stages and the slab are spent):
+    // every thread stores its outputs (the tail added, NaN made arm64's), the
+    // erf table is staged beside them, then warp w runs rows w, w + 8, ...:
+    // lane l the outputs 4 l .. 4 l + 3, + bias (+ residual) in the module's
+    // order and gelu_erf, loaded and stored as 16-byte vectors.
+    static_assert(WM == 2 && BM == 128, "a row of the tile is 32 lanes x 4");
+    constexpr int TS = BM + 4;  // a tile row: 16-byte aligned, rows 4 banks apart
+    static_assert((size_t)BN * TS * 4 + sizeof(shlo_erf::ErfSmem) <= Pipe<WM>::SMEM - 128, "tile and table fit");
+    float *tile = smem;
+    shlo_erf::ErfSmem *tab = reinterpret_cast<shlo_erf::ErfSmem *>(smem + BN * TS);
+    __syncthreads();  // every read of the slab is done
+    shlo_erf::erf_smem_load(tab);
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const int rr = ro + (j & 3) + (j >> 2) * 16;
+      const int64_t r = rbase + rl0 + rr;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+          const float2 pr = acc2[j * 4 + 2 * h + (i >> 1)];
+          v[i] = (i & 1) ? pr.y : pr.x;
+          const int m = m0 + mo + 32 * h + i;
+          if (a.np < a.K && m < a.M && rl0 + rr < a.Nx) {
+            const float *wr = a.w + (a.wbs ? (int64_t)bx * a.wbs : 0) + (int64_t)m * a.K;
+            v[i] = dot_tail(wr, a.x + r * a.K, a.np, a.K, v[i], a.flavor);
+          }
+          v[i] = arm_nan(v[i]);
+        }
+        *reinterpret_cast<float4 *>(tile + rr * TS + mo + 32 * h) = make_float4(v[0], v[1], v[2], v[3]);
+      }
+    }
+    __syncthreads();
+    const int mb = m0 + 4 * lane;
+    const float4 bv = (a.ep & EP_BIAS) ? ep_load4(a.bias, 0, mb, a.M, vec) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    for (int rr = warp; rr < BN && rl0 + rr < a.Nx; rr += THREADS / 32) {
+      const int64_t r = rbase + rl0 + rr;
+      const float4 t = *reinterpret_cast<const float4 *>(tile + rr * TS + 4 * lane);
+      const float4 hv = (a.ep & EP_RES) ? ep_load4(a.res, r, mb, a.M, vec) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+      const float4 g = gelu4(make_float4(ep_add(a.ep, t.x, bv.x, hv.x), ep_add(a.ep, t.y, bv.y, hv.y),
+                                         ep_add(a.ep, t.z, bv.z, hv.z), ep_add(a.ep, t.w, bv.w, hv.w)),
+                             tab);
+      if (vec && mb + 3 < a.M) {
+        *reinterpret_cast<float4 *>(a.y + r * a.M + mb) = g;
+      } else {
+        const float gs[4] = {g.x, g.y, g.z, g.w};
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+          if (mb + i < a.M) a.y[r * a.M + mb + i] = gs[i];
+      }
+    }
+    return;
+  }
+  if constexpr (EPI == 1) {
     // Per half h: the bias and all eight rows' residuals loaded first (one
     // round trip), then the adds and the stores.
 #pragma unroll
@@ -831,8 +889,9 @@ template <int SPLIT>
 cudaError_t mul_mat_tm_attributes();
 // tw, tx: the tensor maps of the packed w ([Wb Kq][Mp], box Tile<WM>::BM x 16)
 // and x ([Bx Kq][Np], box Tile<WM>::BN x 16).
+// epi: 0 the plain product, 1 the fused adds, 2 the adds and gelu_erf (WM = 2).
 template <int SPLIT>
-void launch_mul_mat_tm(int WM, bool stage_fold, bool epi, unsigned grid, cudaStream_t stream, const MMArgs &a,
+void launch_mul_mat_tm(int WM, bool stage_fold, int epi, unsigned grid, cudaStream_t stream, const MMArgs &a,
                        const CUtensorMap &tw, const CUtensorMap &tx);
 // k_mul_mat_short<EPI, NG> with NG = ng (1..4).
 void launch_mul_mat_short(int ng, bool epi, unsigned grid, cudaStream_t stream, const MMArgs &a);
@@ -849,30 +908,33 @@ cudaError_t mul_mat_tm_attributes() {
   auto attr = [&](auto kern, size_t bytes) {
     if (e == cudaSuccess) e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
   };
-  attr(k_mul_mat_tm<1, false, SPLIT, false>, mt::Pipe<1>::SMEM);
-  attr(k_mul_mat_tm<1, false, SPLIT, true>, mt::Pipe<1>::SMEM);
-  attr(k_mul_mat_tm<1, true, SPLIT, false>, mt::Pipe<1>::SMEM);
-  attr(k_mul_mat_tm<1, true, SPLIT, true>, mt::Pipe<1>::SMEM);
-  attr(k_mul_mat_tm<2, false, SPLIT, false>, mt::Pipe<2>::SMEM);
-  attr(k_mul_mat_tm<2, false, SPLIT, true>, mt::Pipe<2>::SMEM);
-  attr(k_mul_mat_tm<2, true, SPLIT, false>, mt::Pipe<2>::SMEM);
-  attr(k_mul_mat_tm<2, true, SPLIT, true>, mt::Pipe<2>::SMEM);
+  attr(k_mul_mat_tm<1, false, SPLIT, 0>, mt::Pipe<1>::SMEM);
+  attr(k_mul_mat_tm<1, false, SPLIT, 1>, mt::Pipe<1>::SMEM);
+  attr(k_mul_mat_tm<1, true, SPLIT, 0>, mt::Pipe<1>::SMEM);
+  attr(k_mul_mat_tm<1, true, SPLIT, 1>, mt::Pipe<1>::SMEM);
+  attr(k_mul_mat_tm<2, false, SPLIT, 0>, mt::Pipe<2>::SMEM);
+  attr(k_mul_mat_tm<2, false, SPLIT, 1>, mt::Pipe<2>::SMEM);
+  attr(k_mul_mat_tm<2, false, SPLIT, 2>, mt::Pipe<2>::SMEM);
+  attr(k_mul_mat_tm<2, true, SPLIT, 0>, mt::Pipe<2>::SMEM);
+  attr(k_mul_mat_tm<2, true, SPLIT, 1>, mt::Pipe<2>::SMEM);
+  attr(k_mul_mat_tm<2, true, SPLIT, 2>, mt::Pipe<2>::SMEM);
   return e;
 }
 
 template <int SPLIT>
-void launch_mul_mat_tm(int WM, bool stage_fold, bool epi, unsigned grid, cudaStream_t stream, const MMArgs &a,
+void launch_mul_mat_tm(int WM, bool stage_fold, int epi, unsigned grid, cudaStream_t stream, const MMArgs &a,
                        const CUtensorMap &tw, const CUtensorMap &tx) {
   const size_t smem = WM == 1 ? mt::Pipe<1>::SMEM : mt::Pipe<2>::SMEM;
-#define SHLO_TM(WMv, SF)                                                                     \
-  (epi ? k_mul_mat_tm<WMv, SF, SPLIT, true><<<grid, mt::THREADS, smem, stream>>>(a, tw, tx) \
-       : k_mul_mat_tm<WMv, SF, SPLIT, false><<<grid, mt::THREADS, smem, stream>>>(a, tw, tx))
+#define SHLO_TM(WMv, SF, E) k_mul_mat_tm<WMv, SF, SPLIT, E><<<grid, mt::THREADS, smem, stream>>>(a, tw, tx)
   if (WM == 1) {
-    if (stage_fold) SHLO_TM(1, true);
-    else SHLO_TM(1, false);
+    if (stage_fold) (epi ? SHLO_TM(1, true, 1) : SHLO_TM(1, true, 0));
+    else (epi ? SHLO_TM(1, false, 1) : SHLO_TM(1, false, 0));
+  } else if (epi == 2) {
+    if (stage_fold) SHLO_TM(2, true, 2);
+    else SHLO_TM(2, false, 2);
   } else {
-    if (stage_fold) SHLO_TM(2, true);
-    else SHLO_TM(2, false);
+    if (stage_fold) (epi ? SHLO_TM(2, true, 1) : SHLO_TM(2, true, 0));
+    else (epi ? SHLO_TM(2, false, 1) : SHLO_TM(2, false, 0));
   }
 #undef SHLO_TM
 }

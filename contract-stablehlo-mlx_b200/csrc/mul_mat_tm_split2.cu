@@ -5,6 +5,6 @@
 
 namespace shlo {
 template cudaError_t mul_mat_tm_attributes<2>();
-template void launch_mul_mat_tm<2>(int, bool, bool, unsigned, cudaStream_t, const MMArgs &, const CUtensorMap &,
+template void launch_mul_mat_tm<2>(int, bool, int, unsigned, cudaStream_t, const MMArgs &, const CUtensorMap &,
                                       const CUtensorMap &);
 }  // namespace shlo

@@ -37,7 +37,7 @@ FUSED = {
     "norm_affine": (["x", "gamma", "beta", "p"], ["y"]),
     "attention": (["q", "k", "v", "p"], ["y"]),
 }
-EP_BIAS, EP_BIAS_LHS, EP_RES, EP_RES_LHS = 1, 2, 4, 8
+EP_BIAS, EP_BIAS_LHS, EP_RES, EP_RES_LHS, EP_GELU = 1, 2, 4, 8, 16
 
 _cache: dict = {}
 
@@ -146,7 +146,7 @@ def f32_of_f64(a, count):
 def mul_mat_bias(w, x, K, M_, R, N, w_batch_stride, bias, res=None, flags=EP_BIAS):
     """mul_mat, then + bias[m] (and + res[r][m] when EP_RES is in flags), each
     add rounded alone in the module's operand order (EP_*_LHS: the added
-    value is the add's left operand)."""
+    value is the add's left operand), then gelu_erf when EP_GELU is in flags."""
     return run("mul_mat_bias", [w, x, bias, res if res is not None else bias,
                                 params([K, M_, R, w_batch_stride, N, 0, flags])], [R * M_], M.dtF32, R * M_, 64)
 

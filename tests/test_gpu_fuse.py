@@ -64,6 +64,48 @@ def test_mul_mat_bias_matches_unfused(K, Mm, R, flags):
     assert np.array_equal(bits(got).reshape(-1), bits(want).reshape(-1))
 
 
+@pytest.mark.parametrize("K,Mm,R,split", [
+    (512, 2048, 1100, None),   # k_mul_mat_tm, whole stages a segment, a partial last row tile
+    (600, 1024, 2100, None),   # the fold after groups of 4 k, and a K tail of 8
+    (512, 1002, 2200, None),   # a partial column tile, M not a multiple of 4 (element stores)
+    (512, 2048, 1100, "2"),    # halves of the fold tree: the last CTA of a tile runs the epilogue
+    (512, 64, 40000, None),    # one warp along m: the product, then the gelu_erf kernel
+    (512, 1536, 300, None),    # a small product (k_mul_mat_seg): the same
+])
+@pytest.mark.parametrize("flags", [Run.EP_BIAS, Run.EP_BIAS | Run.EP_BIAS_LHS | Run.EP_RES])
+def test_mul_mat_bias_gelu_matches_unfused(K, Mm, R, split, flags, monkeypatch):
+    """The dense chain with gelu_erf in the product's epilogue (FFN1's form)
+    against the product, the adds and the gelu_erf kernel, bit for bit."""
+    if split:
+        monkeypatch.setenv("SHLO_MM_SPLIT", split)
+    rng = np.random.default_rng(K + Mm * 3 + R + flags)
+    w = M.of_numpy(specials(rng, (Mm, K)) * np.float32(0.05))
+    x = M.of_numpy(specials(rng, (R, K)))
+    b = M.of_numpy(specials(rng, (Mm,)))
+    h = M.of_numpy(specials(rng, (R, Mm)))
+    y = M.reshape(Run.mul_mat(w, x, K, Mm, R, R, 0), [R, Mm])
+    bb = M.broadcast(M.reshape(b, [1, Mm]), [R, Mm])
+    z = M.binary(M.opAdd, bb, y) if flags & Run.EP_BIAS_LHS else M.binary(M.opAdd, y, bb)
+    if flags & Run.EP_RES:
+        z = M.binary(M.opAdd, h, z) if flags & Run.EP_RES_LHS else M.binary(M.opAdd, z, h)
+    want = M.to_numpy(Run.gelu_erf(M.reshape(z, [R * Mm]), R * Mm))
+    got = M.to_numpy(Run.mul_mat_bias(w, x, K, Mm, R, R, 0, b, M.reshape(h, [R * Mm]) if flags & Run.EP_RES else None,
+                                      flags | Run.EP_GELU))
+    assert np.array_equal(bits(got).reshape(-1), bits(want).reshape(-1))
+
+
+def test_mul_mat_bias_gelu_refused_stock():
+    M.set_flavor("stock")
+    try:
+        w = M.of_numpy(np.ones((256, 64), np.float32))
+        x = M.of_numpy(np.ones((300, 64), np.float32))
+        b = M.of_numpy(np.zeros(256, np.float32))
+        with pytest.raises(M.ShloError, match="not carried"):
+            M.to_numpy(Run.mul_mat_bias(w, x, 64, 256, 300, 300, 0, b, None, Run.EP_BIAS | Run.EP_GELU))
+    finally:
+        M.set_flavor("pinned")
+
+
 @pytest.mark.parametrize("cols,rows", [(512, 300), (1024, 17), (36, 9), (1100, 5), (13, 4)])
 def test_norm_affine_matches_unfused(cols, rows):
     rng = np.random.default_rng(cols + rows)
