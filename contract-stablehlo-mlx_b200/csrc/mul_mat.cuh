@@ -245,6 +245,39 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float *v) {
   for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
 }
 
+// 32 consecutive TMEM columns of this thread's lane, stored / loaded as one
+// access with one wait (the fold moves two 16-column chunks at a time).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float *v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};\n"
+      "tcgen05.wait::st.sync.aligned;\n" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+      "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+      "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15])),
+      "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])), "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])),
+      "r"(__float_as_uint(v[20])), "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])), "r"(__float_as_uint(v[27])),
+      "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])), "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float *v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];\n"
+      "tcgen05.wait::ld.sync.aligned;\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
 // Fold the finished chain of leaf S into the stack: pop and add the levels
 // below the first zero bit of S (the left operand is the older value, as in the
 // tree), then push at that level. Levels 0 and 1 are TMEM columns tcol + 64 L;
@@ -261,45 +294,46 @@ __device__ __forceinline__ void tfold_rt(float2 (&acc2)[32], uint32_t tcol, floa
   const bool last = last_pops >= 0;
   const int depth = last ? last_pops : __ffs(~S) - 1;  // trailing one bits: 0..4
   const int pops = depth < 3 ? depth : 3;
+  // Two chunks of 16 values at a time: 32 adjacent TMEM columns, one access.
 #pragma unroll
-  for (int c = 0; c < 4; c++) {
-    float v[16];
+  for (int cp = 0; cp < 2; cp++) {
+    float v[32];
 #pragma unroll
-    for (int q = 0; q < 8; q++) {
-      v[2 * q] = acc2[8 * c + q].x;
-      v[2 * q + 1] = acc2[8 * c + q].y;
+    for (int q = 0; q < 16; q++) {
+      v[2 * q] = acc2[16 * cp + q].x;
+      v[2 * q + 1] = acc2[16 * cp + q].y;
     }
     for (int L = 0; L < pops; L++) {
-      float t[16];
+      float t[32];
       if (L < 2) {
-        tmem_ld16(tcol + 64 * L + 16 * c, t);
+        tmem_ld32(tcol + 64 * L + 32 * cp, t);
       } else {
 #pragma unroll
-        for (int j = 0; j < 4; j++) {
-          const float4 u = lv2[(c * 4 + j) * mt::THREADS];
+        for (int j = 0; j < 8; j++) {
+          const float4 u = lv2[(cp * 8 + j) * mt::THREADS];
           t[4 * j] = u.x; t[4 * j + 1] = u.y; t[4 * j + 2] = u.z; t[4 * j + 3] = u.w;
         }
       }
       if (PAIR) {
 #pragma unroll
-        for (int i = 0; i < 8; i++) {  // each component rounds as __fadd_rn
+        for (int i = 0; i < 16; i++) {  // each component rounds as __fadd_rn
           const float2 r = __fadd2_rn(make_float2(t[2 * i], t[2 * i + 1]), make_float2(v[2 * i], v[2 * i + 1]));
           v[2 * i] = r.x;
           v[2 * i + 1] = r.y;
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < 16; i++) v[i] = __fadd_rn(t[i], v[i]);
+        for (int i = 0; i < 32; i++) v[i] = __fadd_rn(t[i], v[i]);
       }
     }
     if (depth < 2 && !last) {
-      tmem_st16(tcol + 64 * depth + 16 * c, v);
+      tmem_st32(tcol + 64 * depth + 32 * cp, v);
     } else if (depth == 2 && !last) {
 #pragma unroll
-      for (int j = 0; j < 4; j++) lv2[(c * 4 + j) * mt::THREADS] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      for (int j = 0; j < 8; j++) lv2[(cp * 8 + j) * mt::THREADS] = make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
     }
 #pragma unroll
-    for (int q = 0; q < 8; q++) acc2[8 * c + q] = make_float2(v[2 * q], v[2 * q + 1]);
+    for (int q = 0; q < 16; q++) acc2[16 * cp + q] = make_float2(v[2 * q], v[2 * q + 1]);
   }
 }
 
