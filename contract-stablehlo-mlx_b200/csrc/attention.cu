@@ -124,7 +124,7 @@ __device__ __forceinline__ void value_seg(const float *Vs, const float *Ps, int 
   constexpr int SEGK = S / 16;
 #pragma unroll
   for (int i = 0; i < 8; i++) acc[i] = make_float2(0.0f, 0.0f);
-#pragma unroll 4
+#pragma unroll
   for (int kk = 0; kk < SEGK; kk++) {
     const int p = SG * SEGK + kk;
     const float4 w4 = *reinterpret_cast<const float4 *>(Vs + p * at::DH + mo);
