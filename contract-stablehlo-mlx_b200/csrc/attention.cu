@@ -101,7 +101,8 @@ __device__ __forceinline__ void score_segs(const float *Ks, const float *Qs, int
   (score_seg<SG, S>(Ks, Qs, key, qr, acc, st), ...);
 }
 
-// One pass of scores: keys key..key+3 by queries qr..qr+3 into the score rows
+// One pass of scores (S = 128: 4 keys x 4 queries a thread, the register stack
+// of k_mul_mat_short): keys key..key+3 by queries qr..qr+3 into the score rows
 // (NaN made arm64's). Not inlined, so that one pass's registers are all the
 // compiler allocates for it.
 template <int S>
@@ -112,6 +113,89 @@ __device__ __noinline__ void score_pass(const float *Ks, const float *Qs, float 
   for (int j = 0; j < 4; j++)
     *reinterpret_cast<float4 *>(Ss + (qr + j) * at::Smem<S>::SW + key) =
         make_float4(arm_nan(acc[2 * j].x), arm_nan(acc[2 * j].y), arm_nan(acc[2 * j + 1].x), arm_nan(acc[2 * j + 1].y));
+}
+
+// The scores' fold of segment S for a thread's 8 keys x 4 queries (16 paired
+// accumulators): pop and add the levels below the first zero bit of S (the
+// older value on the left, as in ggml's tree), then push at that level; level 0
+// in registers, levels 1, 2 and 3 in 32 TMEM columns each (tcol + 32 (L - 1)).
+// S is known at compile time.
+template <int S>
+__device__ __forceinline__ void fold8(float2 (&acc)[16], float2 (&st0)[16], uint32_t tcol) {
+  constexpr int depth = S == 15 ? 4 : (S & 1) == 0 ? 0 : (S & 3) == 1 ? 1 : (S & 7) == 3 ? 2 : 3;
+#pragma unroll
+  for (int L = 0; L < depth; L++) {
+    if (L == 0) {
+#pragma unroll
+      for (int i = 0; i < 16; i++) acc[i] = __fadd2_rn(st0[i], acc[i]);
+    } else {
+      float t[32];
+      tmem_ld32(tcol + 32u * (uint32_t)(L - 1), t);
+#pragma unroll
+      for (int i = 0; i < 16; i++) acc[i] = __fadd2_rn(make_float2(t[2 * i], t[2 * i + 1]), acc[i]);
+    }
+  }
+  if constexpr (depth == 0) {
+#pragma unroll
+    for (int i = 0; i < 16; i++) st0[i] = acc[i];
+  } else if constexpr (depth < 4) {
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      v[2 * i] = acc[i].x;
+      v[2 * i + 1] = acc[i].y;
+    }
+    tmem_st32(tcol + 32u * (uint32_t)(depth - 1), v);
+  }
+}
+
+// Score segment SG (packed d rows 4 SG .. 4 SG + 3): keys key..key+3 and
+// key+32..key+35 (w, m) by queries qr..qr+3 (x, r), then the fold.
+template <int SG, int S>
+__device__ __forceinline__ void score_seg8(const float *Ks, const float *Qs, int key, int qr, float2 (&acc)[16],
+                                           float2 (&st)[16], uint32_t tcol) {
+#pragma unroll
+  for (int i = 0; i < 16; i++) acc[i] = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int kk = 0; kk < 4; kk++) {
+    const int p = 4 * SG + kk;
+    const float4 w0 = *reinterpret_cast<const float4 *>(Ks + k_at<S>(p, key));
+    const float4 w1 = *reinterpret_cast<const float4 *>(Ks + k_at<S>(p, key + 32));
+    const float4 x4 = *reinterpret_cast<const float4 *>(Qs + q_at(p, qr));
+    const float2 wp2[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                           make_float2(w1.z, w1.w)};
+    const float xr[4] = {x4.x, x4.y, x4.z, x4.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float2 xj = make_float2(xr[j], xr[j]);
+#pragma unroll
+      for (int i = 0; i < 4; i++) acc[4 * j + i] = __ffma2_rn(wp2[i], xj, acc[4 * j + i]);
+    }
+  }
+  fold8<SG>(acc, st, tcol);
+}
+
+template <int S, int... SG>
+__device__ __forceinline__ void score_segs8(const float *Ks, const float *Qs, int key, int qr, float2 (&acc)[16],
+                                            float2 (&st)[16], uint32_t tcol, std::integer_sequence<int, SG...>) {
+  (score_seg8<SG, S>(Ks, Qs, key, qr, acc, st, tcol), ...);
+}
+
+// The scores: keys key..key+3 and key+32..key+35 by queries qr..qr+3 into the
+// score rows (NaN made arm64's). Not inlined, so that its registers are all the
+// compiler allocates for it.
+template <int S>
+__device__ __noinline__ void score_pass8(const float *Ks, const float *Qs, float *Ss, int key, int qr, uint32_t tcol) {
+  float2 acc[16], st[16];
+  score_segs8<S>(Ks, Qs, key, qr, acc, st, tcol, std::make_integer_sequence<int, 16>{});
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+#pragma unroll
+    for (int h = 0; h < 2; h++)
+      *reinterpret_cast<float4 *>(Ss + (qr + j) * at::Smem<S>::SW + key + 32 * h) =
+          make_float4(arm_nan(acc[4 * j + 2 * h].x), arm_nan(acc[4 * j + 2 * h].y), arm_nan(acc[4 * j + 2 * h + 1].x),
+                      arm_nan(acc[4 * j + 2 * h + 1].y));
+  }
 }
 
 // Value segment SG of a half (its packed key rows SG S/16 .. of Vs and Ps,
@@ -187,14 +271,35 @@ __global__ void __launch_bounds__(at::THREADS, 2) k_attention(AttnArgs a) {
   }
   __syncthreads();
 
-  // 2. Scores, 128 keys a pass: warps 4 (keys) x 2 (queries), lanes 8 x 4.
-  {
+  // 2. Scores: warps 4 (keys) x 2 (queries), lanes 8 (keys) x 4 (queries).
+  //    S = 256: a thread 8 keys x 4 queries in one pass, levels 1 to 3 of the
+  //    fold's stack in TMEM (256 columns a CTA, two CTAs an SM: warps w and
+  //    w + 4 share lanes 32 (w % 4) .. + 32 and take columns 128 (w / 4) ..).
+  //    S = 128: 4 keys x 4 queries, the whole stack in registers.
+  if constexpr (S == 256) {
+    __shared__ uint32_t tmem_base;
+    if (warp == 0) {
+      const uint32_t slot = (uint32_t)__cvta_generic_to_shared(&tmem_base);
+      asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;\n" ::"r"(slot));
+      asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n");
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;\n");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;\n");
+    const uint32_t tcol = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(128 * (warp >> 2));
+    score_pass8<S>(A, Qs, SP, (warp & 3) * 64 + (lane & 7) * 4, (warp >> 2) * 16 + (lane >> 3) * 4, tcol);
+    // every TMEM access waited inside the pass: free the columns
+    asm volatile("tcgen05.fence::before_thread_sync;\n");
+    __syncthreads();
+    asm volatile("tcgen05.fence::after_thread_sync;\n");
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\n" ::"r"(tmem_base));
+  } else {
     const int km = (warp & 3) * 32 + (lane & 7) * 4;
     const int qr = (warp >> 2) * 16 + (lane >> 3) * 4;
 #pragma unroll 1
     for (int kb = 0; kb < S; kb += 128) score_pass<S>(A, Qs, SP, kb + km, qr);
+    __syncthreads();
   }
-  __syncthreads();
 
   // 3. V's rows into A (now free) in packed key order, while soft_max runs.
   {
