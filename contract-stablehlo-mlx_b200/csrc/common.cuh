@@ -239,6 +239,15 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out);
 // mul_mat with the executor's fused epilogue: + bias[m] and/or + res[r][m]
 // (ep: 1 bias, 2 bias is the add's left operand, 4 residual, 8 residual left).
 int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr *res, int ep, Arr **out);
+// k_mul_mat_ep for chained dense products (fusion.cu): x_np > 0, x's storage
+// is this product's packed x already (mm_packed_x_layout's layout, x_np padded
+// rows); y_pack = {segp, Np}: the result is written in the packed layout of a
+// next product whose K is this one's M (its logical shape stays [R*M]).
+int k_mul_mat_fused(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr *res, int ep, int x_np,
+                    const int *y_pack, Arr **out);
+// The packed x a product of K x M over R rows (one weight) makes: false where
+// it packs none or its x needs segment padding or a tail.
+bool mm_packed_x_layout(int64_t K, int64_t M, int64_t R, int *segp, int *Np);
 int k_soft_max(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 // norm with the executor's fused affine: (y * gamma[c]) + beta[c].

@@ -11,8 +11,12 @@
 // roundings, in the same order:
 //
 //   dense      mul_mat (one weight, no batch) -> add of a broadcast 1-D bias over
-//              the last axis [-> add of a same-shape residual]: k_mul_mat_ep
-//              (Lower.lean:157-182's dot_general followed by the module's adds)
+//              the last axis [-> add of a same-shape residual] [-> gelu_erf]:
+//              k_mul_mat_fused (Lower.lean:157-182's dot_general followed by
+//              the module's adds). A chain ending in gelu_erf whose result only
+//              the next chain's product reads (a feed-forward block) hands it
+//              over in that product's packed x layout, so the second product
+//              skips its pack.
 //   layer norm norm -> multiply by a broadcast 1-D gain -> add a broadcast 1-D
 //              bias: k_norm_affine
 //   attention  the copies of q and k into [batch*head*position, 64], the scores
@@ -74,6 +78,12 @@ struct Group {
   int flags = 0;         // dense: the epilogue flags
   int direct = 0;        // attention: q (1), k (2), v (4) read directly, without a copy
   uint32_t p[8] = {0};   // the fused kernel's parameter words
+  // dense chains linked through a packed operand: y_pack (this chain's result
+  // is the next chain's x, written in its packed layout) and x_np (this
+  // chain's x is the previous chain's result, already packed; src is that chain)
+  int y_pack[2] = {0, 0};
+  int x_np = 0, src = -1;
+  uint64_t produced = 0;  // the capture call: the serial of the fused result's storage
   // the capture call's handles, retained until the fused launch
   Arr *h[4] = {nullptr, nullptr, nullptr, nullptr};
   std::map<int, Buffer *> placeholder;  // role -> its placeholder storage
@@ -398,6 +408,27 @@ struct Tracer {
       if (group_of[i] < 0) try_attention(i);
       if (group_of[i] < 0) try_norm(i);
     }
+
+    // dense -> gelu_erf -> dense: the first chain's result read by the second
+    // chain's product alone, as its whole x
+    for (int a = 0; a < (int)groups.size(); a++) {
+      Group &g1 = groups[a];
+      if (g1.kind != G_DENSE || !(g1.flags & EP_GELU)) continue;
+      const uint64_t r1 = ops[g1.last].out;
+      const int64_t M1 = g1.p[1], R1 = g1.p[2];
+      const int j = single(r1);
+      if (j < 0 || group_of[j] < 0 || role_of[j] != R_MM) continue;
+      Group &g2 = groups[group_of[j]];
+      if (g2.kind != G_DENSE || g2.x_np || g2.p[0] != (uint32_t)M1 || g2.p[2] != (uint32_t)R1 ||
+          !full_view(ops[j].in[1], r1, R1 * M1) || ops[j].in[0].buf == r1)
+        continue;
+      int segp, np;
+      if (!mm_packed_x_layout(M1, g2.p[1], R1, &segp, &np)) continue;
+      g1.y_pack[0] = segp;
+      g1.y_pack[1] = np;
+      g2.x_np = np;
+      g2.src = a;
+    }
   }
 
   // ---- the capture call ----
@@ -459,7 +490,9 @@ struct Tracer {
       // h: 0 w, 1 x, 2 bias (1-D view), 3 residual
       for (int s = 0; s < 4 && !rc; s++)
         if (g.h[s]) rc = prep(dev, g.h[s], &c[s]);
-      if (!rc) rc = k_mul_mat_ep(dev, c[0], c[1], g.p, c[2], c[3], g.flags, &o);
+      if (!rc)
+        rc = k_mul_mat_fused(dev, c[0], c[1], g.p, c[2], c[3], g.flags, g.x_np, g.y_pack[1] ? g.y_pack : nullptr, &o);
+      if (!rc) g.produced = o->buf->serial;
     } else if (g.kind == G_NORM) {
       // h: 0 x, 1 gain (1-D view), 2 bias (1-D view)
       for (int s = 0; s < 3 && !rc; s++) rc = prep(dev, g.h[s], &c[s]);
@@ -490,6 +523,9 @@ struct Tracer {
     bool ok = true;
     if (g.kind == G_DENSE) {
       if (role == R_MM) {
+        // a packed x must be the linked chain's fused result itself
+        ok = !g.x_np || (ins[1]->buf && groups[g.src].done && ins[1]->buf->serial == groups[g.src].produced &&
+                         ins[1]->offset == 0);
         keep(g, 0, ins[0]);
         keep(g, 1, ins[1]);
       } else if (role == R_BIAS) {
@@ -610,6 +646,11 @@ int tracer_plan(Tracer *t, Arr *const *outs, int n) {
   t->plan();
   const char *v = getenv("SHLO_GRAPH_VERBOSE");
   if (v && atoi(v) >= 2) dump_log(t);
+  if (v && atoi(v) >= 1) {
+    int links = 0;
+    for (const Group &g : t->groups) links += g.y_pack[1] != 0;
+    if (links) fprintf(stderr, "shlo: dense chains handing a packed operand on: %d\n", links);
+  }
   t->mode = 2;
   t->next = 0;
   return (int)t->groups.size();

@@ -349,11 +349,35 @@ int k_mul_mat(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr **out) {
   return k_mul_mat_ep(dev, w, x, p, nullptr, nullptr, 0, out);
 }
 
+// The packed x of a product of K x M over R rows (one weight, N = R): its
+// segments and padded rows, as mul_mat_ep would make them (the same choice of
+// kernel). False where the product packs no x (the one-thread-an-output path)
+// or its x needs segment padding or a tail (K not a multiple of 64): such an x
+// cannot be handed over packed.
+bool mm_packed_x_layout(int64_t K, int64_t M, int64_t R, int *segp, int *Np) {
+  const int path = mm_path();
+  if (K % 64 || K < 64 || R <= 0 || M <= 0) return false;
+  if (!(path >= 2 || (path == 0 && R * M >= 4096))) return false;
+  const int seg = (int)(K / 16);
+  const bool short_k = path != 3 && (seg == 4 || (M <= 64 && seg <= 16));
+  const bool seg_k = path == 3 || (path == 0 && !short_k && R * M <= ((int64_t)1 << 21));
+  const int WM = M <= 64 ? 1 : 2;
+  const int BN = seg_k ? sg::TR : short_k ? ms::BN : WM == 1 ? mt::Tile<1>::BN : mt::Tile<2>::BN;
+  const int PN = BN < 64 ? 64 : BN;
+  *segp = seg;
+  *Np = (int)((R + PN - 1) / PN * PN);
+  return true;
+}
+
 // The product with its fused epilogue. *gelu_done (when EP_GELU is asked for)
 // is set when k_mul_mat_tm ran gelu_erf in its epilogue; the other paths leave
-// it to the caller.
+// it to the caller. x_np > 0: x's storage already holds this product's packed
+// x (mm_packed_x_layout's, x_np rows). y_pack = {segp, Np}: the result is for a
+// product that takes it packed; *pack_done is set when the epilogue wrote it in
+// that layout (k_mul_mat_tm with gelu_erf), and the result's storage is sized
+// for it either way.
 static int mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr *res, int ep, Arr **out,
-                      bool *gelu_done) {
+                      bool *gelu_done, int x_np = 0, const int *y_pack = nullptr, bool *pack_done = nullptr) {
   const int64_t K = p[0], M = p[1], R = p[2], wbs = p[3], N = p[4];
   const int plain = p[5] != 0;
   if ((ep & EP_BIAS) && (!bias || require_dtype(bias, kF32, "mul_mat bias") || check_elems(bias, M, "mul_mat bias")))
@@ -370,9 +394,10 @@ static int mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias,
   SHLO_TRY(check_elems(x, R * K, "mul_mat x"));
   SHLO_TRY(check_elems(w, (wbs ? (nb - 1) * wbs : 0) + M * K, "mul_mat w"));
   if (wbs && wbs < M * K) return fail("mul_mat: w batch stride %lld below M*K", (long long)wbs);
-  int64_t shape[1] = {R * M};
+  int64_t shape[1] = {y_pack ? M * (int64_t)y_pack[1] : R * M};
   Arr *o;
   SHLO_TRY(new_array(dev, kF32, shape, 1, &o));
+  o->shape[0] = R * M;  // (a packed result's storage holds its padded rows too)
   const int flavor = current_flavor();
   const int64_t np = K & ~(int64_t)15;
   int path = mm_path();
@@ -380,6 +405,10 @@ static int mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias,
   if (R * M == 0) {
     *out = o;
     return 0;
+  }
+  if (!fast && x_np) {
+    shlo_release(o);
+    return fail("mul_mat: a packed x handed to the one-thread-an-output path");
   }
   if (!fast) {
     k_mul_mat_naive<<<grid_for(R * M, 256, dev), 256, 0, dev->stream>>>(
@@ -450,7 +479,18 @@ static int mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias,
     }
   }
   Buffer *xpk;
-  if (pack_operand(dev, (const float *)data_ptr(x), (int)Nx, (int)K, Nx * K, (int)Bx, seg, segp, Np, 0.0f, &xpk)) {
+  if (x_np) {
+    // x is this product's packed x already (the producer wrote it so)
+    if (K % 64 || segp != seg || Bx != 1 || Np != x_np || !x->buf || x->offset ||
+        x->buf->bytes < (size_t)16 * segp * Np * sizeof(float)) {
+      buffer_release(wpk);
+      shlo_release(o);
+      return fail("mul_mat: a packed x that does not match this product's layout");
+    }
+    xpk = x->buf;
+    buffer_retain(xpk);
+  } else if (pack_operand(dev, (const float *)data_ptr(x), (int)Nx, (int)K, Nx * K, (int)Bx, seg, segp, Np, 0.0f,
+                          &xpk)) {
     buffer_release(wpk);
     shlo_release(o);
     return 1;
@@ -565,6 +605,11 @@ static int mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias,
   if ((ep & EP_GELU) && WM == 2) {
     epi = 2;
     *gelu_done = true;
+    if (y_pack && y_pack[1] == Np && 16 * (int64_t)y_pack[0] == M && Bx == 1) {
+      a.ypk_segp = y_pack[0];
+      a.ypk_np = y_pack[1];
+      *pack_done = true;
+    }
   }
   if (split == 16) launch_mul_mat_tm<16>(WM, stage_fold, epi, grid, dev->stream, a, tw, tx);
   else if (split == 8) launch_mul_mat_tm<8>(WM, stage_fold, epi, grid, dev->stream, a, tw, tx);
@@ -757,22 +802,47 @@ static const char kGeluStockRefusal[] =
     "gelu_erf: the stock build's erff is Apple libsystem_m's platform erff, which is not carried "
     "(this backend carries the correctly rounded erff of the pinned build)";
 
-int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr *res, int ep, Arr **out) {
-  if (!(ep & EP_GELU)) return mul_mat_ep(dev, w, x, p, bias, res, ep, out, nullptr);
-  if (current_flavor() == 1) return fail("%s", kGeluStockRefusal);
-  bool done = false;
+int k_mul_mat_fused(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr *res, int ep, int x_np,
+                    const int *y_pack, Arr **out) {
+  if ((ep & EP_GELU) && current_flavor() == 1) return fail("%s", kGeluStockRefusal);
+  bool gelu_done = false, pack_done = false;
   Arr *o;
-  SHLO_TRY(mul_mat_ep(dev, w, x, p, bias, res, ep, &o, &done));
-  if (done) {
-    *out = o;
-    return 0;
+  SHLO_TRY(mul_mat_ep(dev, w, x, p, bias, res, ep, &o, &gelu_done, x_np, y_pack, &pack_done));
+  const int64_t R = p[2], M = p[1];
+  if ((ep & EP_GELU) && !gelu_done) {
+    // The product (with its adds) by a kernel without the gelu epilogue: the
+    // gelu_erf kernel on its result, the same bits.
+    const uint32_t gp[2] = {(uint32_t)(R * M), 0};
+    Arr *g;
+    const int rc = k_gelu_erf(dev, o, gp, &g);
+    shlo_release(o);
+    SHLO_TRY(rc);
+    o = g;
   }
-  // The product (with its adds) by a kernel without the gelu epilogue: the
-  // gelu_erf kernel on its result, the same bits.
-  const uint32_t gp[2] = {(uint32_t)((int64_t)p[2] * p[1]), 0};
-  const int rc = k_gelu_erf(dev, o, gp, out);
-  shlo_release(o);
-  return rc;
+  if (y_pack && !pack_done) {
+    // Packed for its consumer by the pack kernel (the rows padded to y_pack[1]).
+    int64_t shape[1] = {M * (int64_t)y_pack[1]};
+    Arr *q;
+    if (new_array(dev, kF32, shape, 1, &q)) {
+      shlo_release(o);
+      return 1;
+    }
+    q->shape[0] = R * M;
+    launch_pack((const float *)data_ptr(o), (int)R, (int)M, R * M, 1, (int)(M / 16), y_pack[0], y_pack[1], 0.0f,
+                (float *)q->buf->ptr, dev->stream);
+    shlo_release(o);
+    if (launch_check("mul_mat pack")) {
+      shlo_release(q);
+      return 1;
+    }
+    o = q;
+  }
+  *out = o;
+  return 0;
+}
+
+int k_mul_mat_ep(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, Arr *res, int ep, Arr **out) {
+  return k_mul_mat_fused(dev, w, x, p, bias, res, ep, 0, nullptr, out);
 }
 
 int k_soft_max(Device *dev, Arr *x, const uint32_t *p, Arr **out) {

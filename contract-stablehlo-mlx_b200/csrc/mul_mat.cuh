@@ -144,6 +144,10 @@ struct MMArgs {
   int ep;
   int *ctr;           // k_mul_mat_tm split over CTAs: arrivals per tile (0 between launches)
   int *err;           // k_mul_mat_tm: set when a stage's copies did not arrive within the wait limit
+  // k_mul_mat_tm with the gelu epilogue: ypk_np > 0 writes y as the packed x
+  // of a next product whose K is M (segments of ypk_segp packed k, ypk_np
+  // rows; (r, m) at (leaf_of_class(m % 16) * ypk_segp + m / 16) * ypk_np + r).
+  int ypk_segp, ypk_np;
 };
 
 
@@ -671,13 +675,29 @@ __global__ void __launch_bounds__(mt::THREADS, mt::CTAS_PER_SM)
       const float4 g = gelu4(make_float4(ep_add(a.ep, t.x, bv.x, hv.x), ep_add(a.ep, t.y, bv.y, hv.y),
                                          ep_add(a.ep, t.z, bv.z, hv.z), ep_add(a.ep, t.w, bv.w, hv.w)),
                              tab);
-      if (vec && mb + 3 < a.M) {
+      if (a.ypk_np) {
+        // back into the tile (this thread's own four values), stored packed below
+        *reinterpret_cast<float4 *>(tile + rr * TS + 4 * lane) = g;
+      } else if (vec && mb + 3 < a.M) {
         *reinterpret_cast<float4 *>(a.y + r * a.M + mb) = g;
       } else {
         const float gs[4] = {g.x, g.y, g.z, g.w};
 #pragma unroll
         for (int i = 0; i < 4; i++)
           if (mb + i < a.M) a.y[r * a.M + mb + i] = gs[i];
+      }
+    }
+    if (a.ypk_np) {
+      // The next product's packed x, a column of the tile at a time: warp w
+      // the columns w, w + 8, ...; lane l the rows l, l + 32, ... (128-byte
+      // stores). Rows past the operand's are zero, as the pack writes them.
+      __syncthreads();
+      for (int mm = warp; mm < BM && m0 + mm < a.M; mm += THREADS / 32) {
+        const int m = m0 + mm;
+        float *col = a.y + ((int64_t)leaf_of_class(m & 15) * a.ypk_segp + (m >> 4)) * a.ypk_np;
+#pragma unroll
+        for (int rr = lane; rr < BN; rr += 32)
+          if (rl0 + rr < a.ypk_np) col[rl0 + rr] = rl0 + rr < a.Nx ? tile[rr * TS + mm] : 0.0f;
       }
     }
     return;

@@ -6,9 +6,11 @@ runs the fused kernels, an uncompiled call runs the ops one at a time as
 Lower.lean issues them. Checked here: the fused kernels alone on random data
 with specials; whole modules (the encoder layer, the denoiser, the attention
 block) compiled against uncompiled, with the number of fused chains the
-recorder reports; chains it must leave alone (an intermediate read elsewhere,
-a planted fault); and a traced function whose capture call departs from its
-eager call, which must run unfused with the eager result."""
+recorder reports; the feed-forward block's two products, the first writing
+its result in the second's packed operand layout; chains it must leave alone
+(an intermediate read elsewhere, a planted fault); and a traced function whose
+capture call departs from its eager call, which must run unfused with the
+eager result."""
 from __future__ import annotations
 
 import re
@@ -147,6 +149,62 @@ def test_modules_fused_equal_unfused(cfg, B, capfd, monkeypatch):
     assert chains == per_layer * cfg.layers + (2 if cfg.timestep else 0), err
     assert np.array_equal(bits(got), bits(want))
     again = M.to_numpy(E.call(fn, X + W)[0])  # the replay
+    assert np.array_equal(bits(again), bits(want))
+
+
+def ffn_text(R, K1, F, D2, residual):
+    """x [R, K1] -> dense (w1 [F, K1], b1) -> gelu_erf -> dense (w2 [D2, F], b2)
+    [-> + r], the feed-forward block's chain of two dense products."""
+    T = lambda *d: "tensor<" + "".join("%dx" % x for x in d) + "f32>"
+    dn = ('{dot_dimension_numbers = #stablehlo.dot<lhs_contracting_dimensions = [1], '
+          'rhs_contracting_dimensions = [1]>}')
+    res_arg = ", %%r: %s" % T(R, D2) if residual else ""
+    tail = ('    %%o = "stablehlo.add"(%%r, %%z2) : (%s, %s) -> %s\n    func.return %%o : %s\n'
+            % (T(R, D2), T(R, D2), T(R, D2), T(R, D2)) if residual else "    func.return %%z2 : %s\n" % T(R, D2))
+    return f"""module {{
+  func.func public @main(%x: {T(R, K1)}, %w1: {T(F, K1)}, %b1: {T(F)}, %w2: {T(D2, F)}, %b2: {T(D2)}{res_arg}) -> {T(R, D2)} {{
+    %y1 = "stablehlo.dot_general"(%x, %w1) {dn} : ({T(R, K1)}, {T(F, K1)}) -> {T(R, F)}
+    %c1 = "stablehlo.broadcast_in_dim"(%b1) {{broadcast_dimensions = array<i64: 1>}} : ({T(F)}) -> {T(R, F)}
+    %z1 = "stablehlo.add"(%y1, %c1) : ({T(R, F)}, {T(R, F)}) -> {T(R, F)}
+    %g = "stablehlo.custom_call"(%z1) {{call_target_name = "ggml.gelu_erf", backend_config = ""}} : ({T(R, F)}) -> {T(R, F)}
+    %y2 = "stablehlo.dot_general"(%g, %w2) {dn} : ({T(R, F)}, {T(D2, F)}) -> {T(R, D2)}
+    %c2 = "stablehlo.broadcast_in_dim"(%b2) {{broadcast_dimensions = array<i64: 1>}} : ({T(D2)}) -> {T(R, D2)}
+    %z2 = "stablehlo.add"(%y2, %c2) : ({T(R, D2)}, {T(R, D2)}) -> {T(R, D2)}
+{tail}  }}
+}}
+"""
+
+
+@pytest.mark.parametrize("R,K1,F,D2,split,linked", [
+    (1100, 512, 2048, 512, None, True),    # gelu epilogue writes the packed x (a partial last row tile); seg consumer
+    (1100, 512, 2048, 2048, None, True),   # both products on k_mul_mat_tm
+    (1100, 512, 2048, 512, "2", True),     # halves of the fold tree: the last CTA writes the packed tile
+    (4000, 256, 576, 1024, None, True),    # F not a multiple of the 128-column tile
+    (4000, 256, 576, 512, None, True),     # the products' padded rows differ: the pack kernel packs it
+    (300, 512, 1024, 512, None, True),     # the first product on k_mul_mat_seg: packed by the pack kernel
+    (1100, 512, 1000, 512, None, False),   # F not a multiple of 64: no handoff, each packs its own
+])
+@pytest.mark.parametrize("residual", [False, True])
+def test_ffn_packed_handoff_matches_unfused(R, K1, F, D2, split, linked, residual, capfd, monkeypatch):
+    """Two dense chains joined by gelu_erf: compiled, the first writes its result
+    in the second's packed x layout (the second skips its pack); uncompiled, the
+    ops one at a time. Bit for bit, the recording and its replay."""
+    if split:
+        monkeypatch.setenv("SHLO_MM_SPLIT", split)
+    rng = np.random.default_rng(R + K1 + F + D2 + residual)
+    args = [specials(rng, (R, K1)), specials(rng, (F, K1)) * np.float32(0.05), specials(rng, (F,)),
+            specials(rng, (D2, F)) * np.float32(0.05), specials(rng, (D2,))]
+    if residual:
+        args.append(specials(rng, (R, D2)))
+    args = [M.of_numpy(a) for a in args]
+    l = E.load(ffn_text(R, K1, F, D2, residual))
+    want = M.to_numpy(E.call(E.prepare(l, None, False), args)[0])
+    fn = E.prepare(l, None, True)
+    got, chains, err = run_counted(capfd, monkeypatch, fn, args)
+    assert chains == 2, err
+    assert ("handing a packed operand on: 1" in err) == linked, err
+    assert np.array_equal(bits(got), bits(want))
+    again = M.to_numpy(E.call(fn, args)[0])
     assert np.array_equal(bits(again), bits(want))
 
 
