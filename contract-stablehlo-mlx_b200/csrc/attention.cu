@@ -5,23 +5,24 @@
 // dot_general / ggml.soft_max / dot_general / transpose chain, Lower.lean:157-182).
 //
 // One CTA of 8 warps per (batch, head, 32 queries), two CTAs an SM, so that one
-// CTA's loads and soft_max overlap the other's products (both products are
-// bound by shared-memory reads: a 4 x 4 tile a thread, the most the register
-// stack of the fold leaves room for):
+// CTA's loads and soft_max overlap the other's products:
 //   1. K (all S keys) and the CTA's 32 queries, loaded row-contiguously and
 //      stored transposed into shared memory with the head width in ggml's
 //      packed class-major order (K = 64: sixteen segments of 4);
-//   2. the 32 x S scores with ggml_vec_dot_f32's chains and tree (the
-//      register-stack fold of k_mul_mat_short), NaN made arm64's, into a
-//      row-major shared tile;
+//   2. the 32 x S scores with ggml_vec_dot_f32's chains and tree (S = 256:
+//      8 keys x 4 queries a thread, the fold stack's levels 1-3 in TMEM;
+//      S = 128: 4 x 4, the register-stack fold of k_mul_mat_short), NaN made
+//      arm64's, into a row-major shared tile;
 //   3. soft_max over each row exactly as g_soft_max (x * scale, the max,
 //      ggml_v_expf(x - max), the four-lane group sums added in order to a
 //      binary64 sum, y = e * (float)(1 / sum)), the rows held in registers so
 //      that the probabilities can replace the scores in packed key order, while
 //      V's rows are copied in;
-//   4. the value product, the 16 key segments split over two halves of the
-//      CTA (the left and right subtrees of ggml's tree, added as its root),
-//      written straight into the [B][S][H][64] layout of the merged heads.
+//   4. the value product (S = 256: a pair of the 16 key segments a warp, 8 x 8
+//      outputs a thread, the pairs' sums added up ggml's tree; S = 128: the
+//      segments split over two halves of the CTA, 4 x 4 a thread, added as the
+//      tree's root), written straight into the [B][S][H][64] layout of the
+//      merged heads.
 #include "common.cuh"
 #include "ggml_math.cuh"
 #include "mul_mat.cuh"
@@ -231,6 +232,76 @@ __device__ __forceinline__ void value_segs(const float *Vs, const float *Ps, int
   (value_seg<SG, S>(Vs, Ps, mo, ro, acc, st), ...);
 }
 
+// Key segment 2 w + LF of warp w's pair (S = 256): head-width indices mo..mo+3
+// and mo+32..mo+35 (w, m) by queries ro..ro+3 and ro+16..ro+19 (x, r), one
+// chain per output from zero. vo: V's element for (the pair's first packed
+// key row, mo). P's float4 group of (row p, queries q..q+3) is
+// (q/4) ^ (p % 16) ^ (p/16 % 8) (p_at); on the pair's rows p = 32 w + 16 LF + kk
+// that is ((q/4) ^ 2w ^ LF ^ kk) % 8. po: the pair's first row; bq4: 4 (the
+// class of this thread's first queries on that row, (ro/4 ^ 2w) % 8); the
+// second queries' class is the first's ^ 4.
+template <int LF, int S>
+__device__ __forceinline__ void value_leaf8(const float *A, const float *SP, int vo, int po, int bq4,
+                                            float2 (&acc)[32]) {
+  constexpr int SEGK = S / 16;
+#pragma unroll
+  for (int i = 0; i < 32; i++) acc[i] = make_float2(0.0f, 0.0f);
+#pragma unroll
+  for (int kk = 0; kk < SEGK; kk++) {
+    const int r = LF * SEGK + kk;  // the row within the pair
+    const int c4 = ((kk ^ LF) & 7) << 2;
+    const float4 w0 = *reinterpret_cast<const float4 *>(A + vo + r * at::DH);
+    const float4 w1 = *reinterpret_cast<const float4 *>(A + vo + r * at::DH + 32);
+    const float4 x0 = *reinterpret_cast<const float4 *>(SP + po + (bq4 ^ c4) + r * at::NQ);
+    const float4 x1 = *reinterpret_cast<const float4 *>(SP + po + (bq4 ^ c4 ^ 16) + r * at::NQ);
+    const float2 wp2[4] = {make_float2(w0.x, w0.y), make_float2(w0.z, w0.w), make_float2(w1.x, w1.y),
+                           make_float2(w1.z, w1.w)};
+    const float xr[8] = {x0.x, x0.y, x0.z, x0.w, x1.x, x1.y, x1.z, x1.w};
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+      const float2 xj = make_float2(xr[j], xr[j]);
+#pragma unroll
+      for (int i = 0; i < 4; i++) acc[4 * j + i] = __ffma2_rn(wp2[i], xj, acc[4 * j + i]);
+    }
+  }
+}
+
+// The value product's subtree of warp w (S = 256): T(2w) + T(2w + 1), the
+// older on the left as in ggml's tree, left in this thread's 64 TMEM columns
+// (tcol), where T(2w) waits for T(2w + 1). Not inlined, so that its registers
+// are all the compiler allocates for it.
+template <int S>
+__device__ __noinline__ void value_pair8(const float *A, const float *SP, int warp, int mo, int ro, uint32_t tcol) {
+  float2 acc[32];
+  const int bq4 = (((ro >> 2) ^ (2 * warp)) & 7) << 2;
+  const int po = warp * 32 * at::NQ;
+  const int vo = warp * 32 * at::DH + mo;
+  value_leaf8<0, S>(A, SP, vo, po, bq4, acc);
+#pragma unroll
+  for (int hf = 0; hf < 2; hf++) {
+    float v[32];
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      v[2 * i] = acc[16 * hf + i].x;
+      v[2 * i + 1] = acc[16 * hf + i].y;
+    }
+    tmem_st32(tcol + 32u * (uint32_t)hf, v);
+  }
+  value_leaf8<1, S>(A, SP, vo, po, bq4, acc);
+#pragma unroll
+  for (int hf = 0; hf < 2; hf++) {
+    float t[32];
+    tmem_ld32(tcol + 32u * (uint32_t)hf, t);
+#pragma unroll
+    for (int i = 0; i < 16; i++) {
+      const float2 r = __fadd2_rn(make_float2(t[2 * i], t[2 * i + 1]), acc[16 * hf + i]);
+      t[2 * i] = r.x;
+      t[2 * i + 1] = r.y;
+    }
+    tmem_st32(tcol + 32u * (uint32_t)hf, t);
+  }
+}
+
 template <int S>
 __global__ void __launch_bounds__(at::THREADS, 2) k_attention(AttnArgs a) {
   using namespace at;
@@ -276,8 +347,9 @@ __global__ void __launch_bounds__(at::THREADS, 2) k_attention(AttnArgs a) {
   //    fold's stack in TMEM (256 columns a CTA, two CTAs an SM: warps w and
   //    w + 4 share lanes 32 (w % 4) .. + 32 and take columns 128 (w / 4) ..).
   //    S = 128: 4 keys x 4 queries, the whole stack in registers.
+  __shared__ uint32_t tmem_base;
+  uint32_t tcol = 0;
   if constexpr (S == 256) {
-    __shared__ uint32_t tmem_base;
     if (warp == 0) {
       const uint32_t slot = (uint32_t)__cvta_generic_to_shared(&tmem_base);
       asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 256;\n" ::"r"(slot));
@@ -286,13 +358,10 @@ __global__ void __launch_bounds__(at::THREADS, 2) k_attention(AttnArgs a) {
     asm volatile("tcgen05.fence::before_thread_sync;\n");
     __syncthreads();
     asm volatile("tcgen05.fence::after_thread_sync;\n");
-    const uint32_t tcol = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(128 * (warp >> 2));
+    tcol = tmem_base + ((uint32_t)(32 * (warp & 3)) << 16) + (uint32_t)(128 * (warp >> 2));
     score_pass8<S>(A, Qs, SP, (warp & 3) * 64 + (lane & 7) * 4, (warp >> 2) * 16 + (lane >> 3) * 4, tcol);
-    // every TMEM access waited inside the pass: free the columns
-    asm volatile("tcgen05.fence::before_thread_sync;\n");
+    // (the columns stay allocated for the value product's fold)
     __syncthreads();
-    asm volatile("tcgen05.fence::after_thread_sync;\n");
-    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\n" ::"r"(tmem_base));
   } else {
     const int km = (warp & 3) * 32 + (lane & 7) * 4;
     const int qr = (warp >> 2) * 16 + (lane >> 3) * 4;
@@ -413,9 +482,64 @@ __global__ void __launch_bounds__(at::THREADS, 2) k_attention(AttnArgs a) {
   cp_async_wait<0>();
   __syncthreads();
 
-  // 4. The value product: warps 0-3 the segments 0-7 (T(0..7)), warps 4-7 the
-  //    segments 8-15 (T(8..15)); each half's warps 2 (width) x 2 (queries).
-  {
+  // 4. The value product. S = 256: warp w the key segments 2w and 2w + 1, a
+  //    thread 8 head-width indices x 8 queries; then the subtrees' sums up
+  //    ggml's tree through shared memory (V spent): warp 2i + 1 hands its tile
+  //    to 2i, 4i + 2 to 4i, 4 to 0, each level in a region of its own, and
+  //    warp 0 stores the root.
+  if constexpr (S == 256) {
+    const int mo = (lane & 7) * 4, ro = (lane >> 3) * 4;
+    value_pair8<S>(A, SP, warp, mo, ro, tcol);
+    float2 acc[32];
+#pragma unroll
+    for (int hf = 0; hf < 2; hf++) {
+      float t[32];
+      tmem_ld32(tcol + 32u * (uint32_t)hf, t);
+#pragma unroll
+      for (int i = 0; i < 16; i++) acc[16 * hf + i] = make_float2(t[2 * i], t[2 * i + 1]);
+    }
+    asm volatile("tcgen05.fence::before_thread_sync;\n");
+    __syncthreads();  // every read of V and P and every TMEM access is done
+    asm volatile("tcgen05.fence::after_thread_sync;\n");
+    if (warp == 0) asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 256;\n" ::"r"(tmem_base));
+    float4 *xch = reinterpret_cast<float4 *>(A) + lane;
+#pragma unroll
+    for (int lvl = 1; lvl <= 3; lvl++) {
+      // level lvl: warps w with w % 2^(lvl-1) == 0 hold a subtree; the odd
+      // ones among them (w / 2^(lvl-1) odd) hand it to w - 2^(lvl-1)
+      const int base = lvl == 1 ? 0 : lvl == 2 ? 4 : 6;  // the level's first slot of 512 float4
+      const bool holds = (warp & ((1 << (lvl - 1)) - 1)) == 0;
+      const bool gives = holds && ((warp >> (lvl - 1)) & 1);
+      float4 *slot = xch + (base + (warp >> lvl)) * 512;
+      if (gives) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) slot[32 * i] = make_float4(acc[2 * i].x, acc[2 * i].y, acc[2 * i + 1].x, acc[2 * i + 1].y);
+      }
+      __syncthreads();
+      if (holds && !gives) {
+#pragma unroll
+        for (int i = 0; i < 16; i++) {
+          const float4 u = slot[32 * i];
+          acc[2 * i] = __fadd2_rn(acc[2 * i], make_float2(u.x, u.y));
+          acc[2 * i + 1] = __fadd2_rn(acc[2 * i + 1], make_float2(u.z, u.w));
+        }
+      }
+    }
+    if (warp == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; j++) {
+        const int q = ro + (j & 3) + (j >> 2) * 16;
+        float *dst = a.o + (((int64_t)b * S + i0 + q) * a.H + h) * DH + mo;
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+          const float2 lo = acc[4 * j + 2 * hf], hi = acc[4 * j + 2 * hf + 1];
+          *reinterpret_cast<float4 *>(dst + 32 * hf) = make_float4(arm_nan(lo.x), arm_nan(lo.y), arm_nan(hi.x), arm_nan(hi.y));
+        }
+      }
+    }
+  } else {
+    // S = 128: warps 0-3 the segments 0-7 (T(0..7)), warps 4-7 the segments
+    // 8-15 (T(8..15)); each half's warps 2 (width) x 2 (queries), 4 x 4 a thread.
     const int wg = warp & 3, half = warp >> 2;
     const int mo = (wg & 1) * 32 + (lane & 7) * 4;
     const int ro = (wg >> 1) * 16 + (lane >> 3) * 4;
