@@ -47,9 +47,14 @@ static_assert(Smem<256>::BYTES <= 113 * 1024, "two CTAs an SM");
 struct AttnArgs {
   const float *q, *k, *v;
   int64_t qs[3], ks[3], vs[3];  // element strides of batch, position, head (the width is contiguous)
-  float *o;                     // [B][S][H][64]
+  float *o;                     // [B][S][H][64], or (ypk_np > 0) packed, see below
   int H;
   float sc;
+  // S = 256, ypk_np > 0: o is written as the packed x of a next product whose K
+  // is H * 64 (segments of ypk_segp packed k, ypk_np rows): (row r, column k) at
+  // (leaf_of_class(k % 16) * ypk_segp + k / 16) * ypk_np + r, r = b S + s and
+  // k = h 64 + d.
+  int ypk_segp, ypk_np;
 };
 
 // Packed position of head-width index d (K = 64: segments of 4, no padding).
@@ -525,7 +530,33 @@ __global__ void __launch_bounds__(at::THREADS, 2) k_attention(AttnArgs a) {
         }
       }
     }
-    if (warp == 0) {
+    if (a.ypk_np) {
+      // The packed layout: the root's tile through shared memory ([64 d][32
+      // queries + 1] over the first level's slots, read before the second
+      // level's barrier); then warp w the columns 8w .. 8w + 7, lane l query l
+      // (128-byte stores).
+      float *tt = A;
+      if (warp == 0) {
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+          const int q = ro + (j & 3) + (j >> 2) * 16;
+#pragma unroll
+          for (int i = 0; i < 4; i++) {
+            const float2 pr = acc[4 * j + i];
+            const int d = mo + (i & 1) * 2 + (i >> 1) * 32;
+            tt[d * 33 + q] = arm_nan(pr.x);
+            tt[(d + 1) * 33 + q] = arm_nan(pr.y);
+          }
+        }
+      }
+      __syncthreads();
+#pragma unroll
+      for (int c = 0; c < 8; c++) {
+        const int d = 8 * warp + c, k = h * DH + d;
+        a.o[((int64_t)leaf_of_class(k & 15) * a.ypk_segp + (k >> 4)) * a.ypk_np + (int64_t)b * S + i0 + lane] =
+            tt[d * 33 + lane];
+      }
+    } else if (warp == 0) {
 #pragma unroll
       for (int j = 0; j < 8; j++) {
         const int q = ro + (j & 3) + (j >> 2) * 16;
@@ -568,6 +599,10 @@ __global__ void __launch_bounds__(at::THREADS, 2) k_attention(AttnArgs a) {
 // q, k, v: [B][S][H][64] views (any element strides of the first three
 // dimensions, the width contiguous); p = [B, S, H, width, scale bits].
 int k_attention(Device *dev, Arr *q, Arr *k, Arr *v, const uint32_t *p, Arr **out) {
+  return k_attention_packed(dev, q, k, v, p, nullptr, out);
+}
+
+int k_attention_packed(Device *dev, Arr *q, Arr *k, Arr *v, const uint32_t *p, const int *y_pack, Arr **out) {
   const int64_t B = p[0], S = p[1], H = p[2], W = p[3];
   const float sc = bitsf_host(p[4]);
   if (W != at::DH || (S != 128 && S != 256) || B <= 0 || H <= 0)
@@ -601,9 +636,13 @@ int k_attention(Device *dev, Arr *q, Arr *k, Arr *v, const uint32_t *p, Arr **ou
     ptrs[i] = (const float *)data_ptr(x);
   }
   Arr *o = nullptr;
+  // the packed layout in the kernel's epilogue (S = 256, no padded rows), else
+  // by the pack kernel after it
+  const bool pk_epi = y_pack && S == 256 && y_pack[1] == B * S && 16 * (int64_t)y_pack[0] == H * W;
   if (!rc) {
-    int64_t shape[1] = {B * S * H * W};
+    int64_t shape[1] = {pk_epi ? H * W * (int64_t)y_pack[1] : B * S * H * W};
     rc = new_array(dev, kF32, shape, 1, &o);
+    if (!rc) o->shape[0] = B * S * H * W;
   }
   if (!rc) {
     a.q = ptrs[0];
@@ -612,6 +651,10 @@ int k_attention(Device *dev, Arr *q, Arr *k, Arr *v, const uint32_t *p, Arr **ou
     a.o = (float *)o->buf->ptr;
     a.H = (int)H;
     a.sc = sc;
+    if (pk_epi) {
+      a.ypk_segp = y_pack[0];
+      a.ypk_np = y_pack[1];
+    }
     static bool attr_done[64] = {false};
     if (!attr_done[dev->id]) {
       rc = cuda_check(cudaFuncSetAttribute(k_attention<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
@@ -631,6 +674,12 @@ int k_attention(Device *dev, Arr *q, Arr *k, Arr *v, const uint32_t *p, Arr **ou
   }
   for (int i = 0; i < 3; i++)
     if (own[i]) shlo_release(own[i]);
+  if (!rc && y_pack && !pk_epi) {
+    Arr *pk;
+    rc = k_pack_x(dev, o, B * S, H * W, y_pack, &pk);
+    shlo_release(o);
+    o = rc ? nullptr : pk;
+  }
   if (rc) {
     if (o) shlo_release(o);
     return 1;

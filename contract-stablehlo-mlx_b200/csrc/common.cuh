@@ -252,9 +252,19 @@ int k_soft_max(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 // norm with the executor's fused affine: (y * gamma[c]) + beta[c].
 int k_norm_affine(Device *dev, Arr *x, const uint32_t *p, Arr *gamma, Arr *beta, Arr **out);
+// k_norm_affine whose result is the packed x (y_pack = {segp, Np}, as
+// mm_packed_x_layout gives it) of a product over the normalised rows.
+int k_norm_affine_packed(Device *dev, Arr *x, const uint32_t *p, Arr *gamma, Arr *beta, const int *y_pack,
+                         Arr **out);
 // The executor's fused attention (scores, soft_max, value product): q, k, v
 // [B][S][H][64] views, p = [B, S, H, 64, scale bits]; the result is [B][S][H][64].
 int k_attention(Device *dev, Arr *q, Arr *k, Arr *v, const uint32_t *p, Arr **out);
+// k_attention whose result is the packed x (y_pack = {segp, Np}, as
+// mm_packed_x_layout gives it) of a product over the merged heads.
+int k_attention_packed(Device *dev, Arr *q, Arr *k, Arr *v, const uint32_t *p, const int *y_pack, Arr **out);
+// A row-major rows x K operand copied into the packed x layout y_pack = {segp,
+// Np} (K a multiple of 64; the rows past `rows` zero).
+int k_pack_x(Device *dev, Arr *src, int64_t rows, int64_t K, const int *y_pack, Arr **out);
 int k_silu(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 int k_gelu_erf(Device *dev, Arr *x, const uint32_t *p, Arr **out);
 int k_erff_map(Device *dev, const uint32_t *p, Arr **out);

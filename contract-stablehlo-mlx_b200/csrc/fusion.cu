@@ -13,15 +13,16 @@
 //   dense      mul_mat (one weight, no batch) -> add of a broadcast 1-D bias over
 //              the last axis [-> add of a same-shape residual] [-> gelu_erf]:
 //              k_mul_mat_fused (Lower.lean:157-182's dot_general followed by
-//              the module's adds). A chain ending in gelu_erf whose result only
-//              the next chain's product reads (a feed-forward block) hands it
-//              over in that product's packed x layout, so the second product
-//              skips its pack.
+//              the module's adds)
 //   layer norm norm -> multiply by a broadcast 1-D gain -> add a broadcast 1-D
 //              bias: k_norm_affine
 //   attention  the copies of q and k into [batch*head*position, 64], the scores
 //              mul_mat, soft_max, the copy of v, the value mul_mat, and the copy
 //              of the result into [batch, position, head*64]: k_attention
+//
+// A dense chain ending in gelu_erf, an attention block or a layer norm whose
+// result only the next dense chain's product reads, as its whole x, writes it
+// in that product's packed x layout, so the product skips its pack.
 //
 // In the capture call the same entry points are matched to the log op by op.
 // An op inside a chain returns a placeholder of the logged shape (real storage
@@ -409,13 +410,25 @@ struct Tracer {
       if (group_of[i] < 0) try_norm(i);
     }
 
-    // dense -> gelu_erf -> dense: the first chain's result read by the second
-    // chain's product alone, as its whole x
+    // A chain whose result the next dense chain's product alone reads, as its
+    // whole x, hands it over packed: dense -> gelu_erf (FFN1 -> FFN2), the
+    // attention block (-> the output projection), the layer norm (-> QKV, FFN1).
     for (int a = 0; a < (int)groups.size(); a++) {
       Group &g1 = groups[a];
-      if (g1.kind != G_DENSE || !(g1.flags & EP_GELU)) continue;
+      int64_t M1, R1;  // the result's rows and row width
+      if (g1.kind == G_DENSE && (g1.flags & EP_GELU)) {
+        M1 = g1.p[1];
+        R1 = g1.p[2];
+      } else if (g1.kind == G_ATTN) {
+        M1 = (int64_t)g1.p[2] * g1.p[3];
+        R1 = (int64_t)g1.p[0] * g1.p[1];
+      } else if (g1.kind == G_NORM) {
+        M1 = g1.p[0];
+        R1 = g1.p[1];
+      } else {
+        continue;
+      }
       const uint64_t r1 = ops[g1.last].out;
-      const int64_t M1 = g1.p[1], R1 = g1.p[2];
       const int j = single(r1);
       if (j < 0 || group_of[j] < 0 || role_of[j] != R_MM) continue;
       Group &g2 = groups[group_of[j]];
@@ -486,21 +499,21 @@ struct Tracer {
     int rc = 0;
     for (int s = 0; s < 3; s++)  // every kind's first three operands (the residual is optional)
       if (!g.h[s]) return fail("fusion: a chain ended without its operands");
+    const int *yp = g.y_pack[1] ? g.y_pack : nullptr;  // the result packed for the next chain
     if (g.kind == G_DENSE) {
       // h: 0 w, 1 x, 2 bias (1-D view), 3 residual
       for (int s = 0; s < 4 && !rc; s++)
         if (g.h[s]) rc = prep(dev, g.h[s], &c[s]);
-      if (!rc)
-        rc = k_mul_mat_fused(dev, c[0], c[1], g.p, c[2], c[3], g.flags, g.x_np, g.y_pack[1] ? g.y_pack : nullptr, &o);
-      if (!rc) g.produced = o->buf->serial;
+      if (!rc) rc = k_mul_mat_fused(dev, c[0], c[1], g.p, c[2], c[3], g.flags, g.x_np, yp, &o);
     } else if (g.kind == G_NORM) {
       // h: 0 x, 1 gain (1-D view), 2 bias (1-D view)
       for (int s = 0; s < 3 && !rc; s++) rc = prep(dev, g.h[s], &c[s]);
-      if (!rc) rc = k_norm_affine(dev, c[0], g.p, c[1], c[2], &o);
+      if (!rc) rc = k_norm_affine_packed(dev, c[0], g.p, c[1], c[2], yp, &o);
     } else {
       // h: 0 q, 1 k, 2 v, as [B, S, H, 64] views
-      rc = k_attention(dev, g.h[0], g.h[1], g.h[2], g.p, &o);
+      rc = k_attention_packed(dev, g.h[0], g.h[1], g.h[2], g.p, yp, &o);
     }
+    if (!rc) g.produced = o->buf->serial;
     for (Arr *a : c)
       if (a) shlo_release(a);
     for (Arr *&a : g.h)

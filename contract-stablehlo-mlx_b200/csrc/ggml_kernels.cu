@@ -820,24 +820,32 @@ int k_mul_mat_fused(Device *dev, Arr *w, Arr *x, const uint32_t *p, Arr *bias, A
     o = g;
   }
   if (y_pack && !pack_done) {
-    // Packed for its consumer by the pack kernel (the rows padded to y_pack[1]).
-    int64_t shape[1] = {M * (int64_t)y_pack[1]};
     Arr *q;
-    if (new_array(dev, kF32, shape, 1, &q)) {
-      shlo_release(o);
-      return 1;
-    }
-    q->shape[0] = R * M;
-    launch_pack((const float *)data_ptr(o), (int)R, (int)M, R * M, 1, (int)(M / 16), y_pack[0], y_pack[1], 0.0f,
-                (float *)q->buf->ptr, dev->stream);
+    const int rc = k_pack_x(dev, o, R, M, y_pack, &q);
     shlo_release(o);
-    if (launch_check("mul_mat pack")) {
-      shlo_release(q);
-      return 1;
-    }
+    SHLO_TRY(rc);
     o = q;
   }
   *out = o;
+  return 0;
+}
+
+int k_pack_x(Device *dev, Arr *src, int64_t rows, int64_t K, const int *y_pack, Arr **out) {
+  if (K % 64 || 16 * (int64_t)y_pack[0] != K || y_pack[1] < rows || y_pack[1] % 64 || numel(src) < rows * K ||
+      ((uintptr_t)data_ptr(src) & 15))
+    return fail("pack: a %lld x %lld operand does not fit the packed layout (%d, %d)", (long long)rows, (long long)K,
+                y_pack[0], y_pack[1]);
+  int64_t shape[1] = {K * (int64_t)y_pack[1]};
+  Arr *q;
+  SHLO_TRY(new_array(dev, kF32, shape, 1, &q));
+  q->shape[0] = rows * K;  // (the storage holds the padded rows too)
+  launch_pack((const float *)data_ptr(src), (int)rows, (int)K, rows * K, 1, (int)(K / 16), y_pack[0], y_pack[1], 0.0f,
+              (float *)q->buf->ptr, dev->stream);
+  if (launch_check("pack")) {
+    shlo_release(q);
+    return 1;
+  }
+  *out = q;
   return 0;
 }
 
@@ -1084,14 +1092,15 @@ __global__ void k_affine_rows(float *y, int64_t n, int ncols, const float *gamma
 // gives the spec's sum. Otherwise (or with an infinity or NaN) the row goes to
 // the warp's shared-memory buffer and lane 0 runs the spec's serial chain.
 // Every warp collective sits outside the per-row branches.
-template <int C>  // float4 groups a lane: ncols = 128 C
-__global__ void __launch_bounds__(128) g_norm_warp(const float *__restrict__ x, float *__restrict__ y, int64_t rows,
-                                                   float eps, const float *__restrict__ gamma,
-                                                   const float *__restrict__ beta) {
+//
+// norm_row: one row (a warp), the norm (and the fused affine) of row `row` into
+// res, lane l holding the float4 groups l, l + 32, ...; rowbuf: the warp's N
+// floats for the serial chains.
+template <int C>
+__device__ __forceinline__ void norm_row(const float *__restrict__ x, int64_t row, float eps,
+                                         const float *__restrict__ gamma, const float *__restrict__ beta,
+                                         float *rowbuf, int lane, float4 (&res)[C]) {
   constexpr int N = 128 * C;
-  __shared__ float buf[4][N];
-  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-  float *rowbuf = buf[w];
   const int lg_n = 32 - __clz(N - 1), lg_g = 32 - __clz(N / 4 - 1);
   auto span = [&](float v, int &lo, int &hi, bool &sp) {
     const uint32_t b = fbits(v) & 0x7FFFFFFFu;
@@ -1110,100 +1119,146 @@ __global__ void __launch_bounds__(128) g_norm_warp(const float *__restrict__ x, 
     }
     return !__any_sync(0xffffffffu, sp) && (lo > hi || hi - lo + 24 + lg <= 53);
   };
+  const float4 *xr = reinterpret_cast<const float4 *>(x + row * N);
+  float4 v[C];
+#pragma unroll
+  for (int c = 0; c < C; c++) v[c] = __ldg(xr + lane + 32 * c);
+  // the row sum
+  int lo = 255, hi = 0;
+  bool sp = false;
+  double sum = 0.0;
+#pragma unroll
+  for (int c = 0; c < C; c++) {
+    span(v[c].x, lo, hi, sp); span(v[c].y, lo, hi, sp); span(v[c].z, lo, hi, sp); span(v[c].w, lo, hi, sp);
+    sum = __dadd_rn(__dadd_rn(__dadd_rn(__dadd_rn(sum, (double)v[c].x), (double)v[c].y), (double)v[c].z),
+                    (double)v[c].w);
+  }
+  const bool ex1 = exact(lo, hi, sp, lg_n);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) sum = __dadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
+  if (!ex1) {  // warp-uniform
+#pragma unroll
+    for (int c = 0; c < C; c++) reinterpret_cast<float4 *>(rowbuf)[lane + 32 * c] = v[c];
+    __syncwarp();
+    if (lane == 0) {
+      double s0 = 0.0;
+      for (int k = 0; k < N; k += 8) {  // eight values loaded ahead of their serial adds
+        double t[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) t[i] = (double)rowbuf[k + i];
+#pragma unroll
+        for (int i = 0; i < 8; i++) s0 = __dadd_rn(s0, t[i]);
+      }
+      sum = s0;
+    }
+    sum = __shfl_sync(0xffffffffu, sum, 0);
+    __syncwarp();
+  }
+  const float mean = __fdiv_rn(__double2float_rn(sum), (float)N);
+  // the group sums of squared deviations
+  float q[C];
+  lo = 255; hi = 0; sp = false;
+  double s2 = 0.0;
+#pragma unroll
+  for (int c = 0; c < C; c++) {
+    const float d0 = __fsub_rn(v[c].x, mean), d1 = __fsub_rn(v[c].y, mean);
+    const float d2 = __fsub_rn(v[c].z, mean), d3 = __fsub_rn(v[c].w, mean);
+    q[c] = __fadd_rn(__fadd_rn(__fmul_rn(d0, d0), __fmul_rn(d1, d1)), __fadd_rn(__fmul_rn(d2, d2), __fmul_rn(d3, d3)));
+    span(q[c], lo, hi, sp);
+    s2 = __dadd_rn(s2, (double)q[c]);
+  }
+  const bool ex2 = exact(lo, hi, sp, lg_g);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) s2 = __dadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, o));
+  if (!ex2) {  // warp-uniform: the group sums in group order
+#pragma unroll
+    for (int c = 0; c < C; c++) rowbuf[lane + 32 * c] = q[c];
+    __syncwarp();
+    if (lane == 0) {
+      double t2 = 0.0;
+      for (int k = 0; k < N / 4; k += 8) {
+        double t[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) t[i] = (double)rowbuf[k + i];
+#pragma unroll
+        for (int i = 0; i < 8; i++) t2 = __dadd_rn(t2, t[i]);
+      }
+      s2 = t2;
+    }
+    s2 = __shfl_sync(0xffffffffu, s2, 0);
+    __syncwarp();
+  }
+  const float var = __double2float_rn(__ddiv_rn(s2, (double)N));
+  const float scl = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+#pragma unroll
+  for (int c = 0; c < C; c++) {
+    res[c].x = arm_nan(__fmul_rn(__fsub_rn(v[c].x, mean), scl));
+    res[c].y = arm_nan(__fmul_rn(__fsub_rn(v[c].y, mean), scl));
+    res[c].z = arm_nan(__fmul_rn(__fsub_rn(v[c].z, mean), scl));
+    res[c].w = arm_nan(__fmul_rn(__fsub_rn(v[c].w, mean), scl));
+    if (gamma) {  // the executor's fused affine: (y * gamma) + beta, each rounded alone
+      const float4 g = __ldg(reinterpret_cast<const float4 *>(gamma) + lane + 32 * c);
+      const float4 b = __ldg(reinterpret_cast<const float4 *>(beta) + lane + 32 * c);
+      res[c] = make_float4(__fadd_rn(__fmul_rn(res[c].x, g.x), b.x), __fadd_rn(__fmul_rn(res[c].y, g.y), b.y),
+                         __fadd_rn(__fmul_rn(res[c].z, g.z), b.z), __fadd_rn(__fmul_rn(res[c].w, g.w), b.w));
+    }
+  }
+}
+
+template <int C>  // float4 groups a lane: ncols = 128 C
+__global__ void __launch_bounds__(128) g_norm_warp(const float *__restrict__ x, float *__restrict__ y, int64_t rows,
+                                                   float eps, const float *__restrict__ gamma,
+                                                   const float *__restrict__ beta) {
+  constexpr int N = 128 * C;
+  __shared__ float buf[4][N];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   for (int64_t row = (int64_t)blockIdx.x * 4 + w; row < rows; row += (int64_t)gridDim.x * 4) {
-    const float4 *xr = reinterpret_cast<const float4 *>(x + row * N);
-    float4 v[C];
-#pragma unroll
-    for (int c = 0; c < C; c++) v[c] = __ldg(xr + lane + 32 * c);
-    // the row sum
-    int lo = 255, hi = 0;
-    bool sp = false;
-    double sum = 0.0;
-#pragma unroll
-    for (int c = 0; c < C; c++) {
-      span(v[c].x, lo, hi, sp); span(v[c].y, lo, hi, sp); span(v[c].z, lo, hi, sp); span(v[c].w, lo, hi, sp);
-      sum = __dadd_rn(__dadd_rn(__dadd_rn(__dadd_rn(sum, (double)v[c].x), (double)v[c].y), (double)v[c].z),
-                      (double)v[c].w);
-    }
-    const bool ex1 = exact(lo, hi, sp, lg_n);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) sum = __dadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, o));
-    if (!ex1) {  // warp-uniform
-#pragma unroll
-      for (int c = 0; c < C; c++) reinterpret_cast<float4 *>(rowbuf)[lane + 32 * c] = v[c];
-      __syncwarp();
-      if (lane == 0) {
-        double s0 = 0.0;
-        for (int k = 0; k < N; k += 8) {  // eight values loaded ahead of their serial adds
-          double t[8];
-#pragma unroll
-          for (int i = 0; i < 8; i++) t[i] = (double)rowbuf[k + i];
-#pragma unroll
-          for (int i = 0; i < 8; i++) s0 = __dadd_rn(s0, t[i]);
-        }
-        sum = s0;
-      }
-      sum = __shfl_sync(0xffffffffu, sum, 0);
-      __syncwarp();
-    }
-    const float mean = __fdiv_rn(__double2float_rn(sum), (float)N);
-    // the group sums of squared deviations
-    float q[C];
-    lo = 255; hi = 0; sp = false;
-    double s2 = 0.0;
-#pragma unroll
-    for (int c = 0; c < C; c++) {
-      const float d0 = __fsub_rn(v[c].x, mean), d1 = __fsub_rn(v[c].y, mean);
-      const float d2 = __fsub_rn(v[c].z, mean), d3 = __fsub_rn(v[c].w, mean);
-      q[c] = __fadd_rn(__fadd_rn(__fmul_rn(d0, d0), __fmul_rn(d1, d1)), __fadd_rn(__fmul_rn(d2, d2), __fmul_rn(d3, d3)));
-      span(q[c], lo, hi, sp);
-      s2 = __dadd_rn(s2, (double)q[c]);
-    }
-    const bool ex2 = exact(lo, hi, sp, lg_g);
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s2 = __dadd_rn(s2, __shfl_xor_sync(0xffffffffu, s2, o));
-    if (!ex2) {  // warp-uniform: the group sums in group order
-#pragma unroll
-      for (int c = 0; c < C; c++) rowbuf[lane + 32 * c] = q[c];
-      __syncwarp();
-      if (lane == 0) {
-        double t2 = 0.0;
-        for (int k = 0; k < N / 4; k += 8) {
-          double t[8];
-#pragma unroll
-          for (int i = 0; i < 8; i++) t[i] = (double)rowbuf[k + i];
-#pragma unroll
-          for (int i = 0; i < 8; i++) t2 = __dadd_rn(t2, t[i]);
-        }
-        s2 = t2;
-      }
-      s2 = __shfl_sync(0xffffffffu, s2, 0);
-      __syncwarp();
-    }
-    const float var = __double2float_rn(__ddiv_rn(s2, (double)N));
-    const float scl = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, eps)));
+    float4 o[C];
+    norm_row<C>(x, row, eps, gamma, beta, buf[w], lane, o);
     float4 *yr = reinterpret_cast<float4 *>(y + row * N);
 #pragma unroll
-    for (int c = 0; c < C; c++) {
-      float4 o;
-      o.x = arm_nan(__fmul_rn(__fsub_rn(v[c].x, mean), scl));
-      o.y = arm_nan(__fmul_rn(__fsub_rn(v[c].y, mean), scl));
-      o.z = arm_nan(__fmul_rn(__fsub_rn(v[c].z, mean), scl));
-      o.w = arm_nan(__fmul_rn(__fsub_rn(v[c].w, mean), scl));
-      if (gamma) {  // the executor's fused affine: (y * gamma) + beta, each rounded alone
-        const float4 g = __ldg(reinterpret_cast<const float4 *>(gamma) + lane + 32 * c);
-        const float4 b = __ldg(reinterpret_cast<const float4 *>(beta) + lane + 32 * c);
-        o = make_float4(__fadd_rn(__fmul_rn(o.x, g.x), b.x), __fadd_rn(__fmul_rn(o.y, g.y), b.y),
-                        __fadd_rn(__fmul_rn(o.z, g.z), b.z), __fadd_rn(__fmul_rn(o.w, g.w), b.w));
-      }
-      yr[lane + 32 * c] = o;
+    for (int c = 0; c < C; c++) yr[lane + 32 * c] = o[c];
+  }
+}
+
+// g_norm_warp writing its result as the packed x of a next product whose K is
+// N (segments of segp = N / 16 packed k, rows_p rows: (row r, column k) at
+// (leaf_of_class(k % 16) * segp + k / 16) * rows_p + r; the rows past `rows`
+// zero). 8 rows at a time, one a warp, through shared memory ([8][N + 4]);
+// then thread t the row t % 8 of the columns t / 8, t / 8 + 32, ... (32-byte
+// stores, a warp four columns; the tile's reads spread over all 32 banks).
+template <int C>
+__global__ void __launch_bounds__(256) g_norm_warp_pk(const float *__restrict__ x, float *__restrict__ y, int64_t rows,
+                                                      int64_t rows_p, float eps, const float *__restrict__ gamma,
+                                                      const float *__restrict__ beta) {
+  constexpr int N = 128 * C, TS = N + 4, segp = N / 16;
+  extern __shared__ __align__(16) float sm[];  // the tile [8][TS], then the warps' row buffers [8][N]
+  float *tile = sm, *buf = sm + 8 * TS;
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, i = threadIdx.x & 7;
+  for (int64_t r0 = (int64_t)blockIdx.x * 8; r0 < rows_p; r0 += (int64_t)gridDim.x * 8) {
+    if (r0 + w < rows) {
+      float4 o[C];
+      norm_row<C>(x, r0 + w, eps, gamma, beta, buf + w * N, lane, o);
+#pragma unroll
+      for (int c = 0; c < C; c++) reinterpret_cast<float4 *>(tile + w * TS)[lane + 32 * c] = o[c];
     }
+    __syncthreads();
+    const bool live = r0 + i < rows;
+#pragma unroll 4
+    for (int k = threadIdx.x >> 3; k < N; k += 32)
+      y[((int64_t)leaf_of_class(k & 15) * segp + (k >> 4)) * rows_p + r0 + i] = live ? tile[i * TS + k] : 0.0f;
+    __syncthreads();
   }
 }
 
 int k_norm(Device *dev, Arr *x, const uint32_t *p, Arr **out) { return k_norm_affine(dev, x, p, nullptr, nullptr, out); }
 
 int k_norm_affine(Device *dev, Arr *x, const uint32_t *p, Arr *gamma, Arr *beta, Arr **out) {
+  return k_norm_affine_packed(dev, x, p, gamma, beta, nullptr, out);
+}
+
+int k_norm_affine_packed(Device *dev, Arr *x, const uint32_t *p, Arr *gamma, Arr *beta, const int *y_pack,
+                         Arr **out) {
   const int64_t ncols = p[0], rows = p[1];
   const float eps = bitsf_host(p[2]);
   SHLO_TRY(require_dtype(x, kF32, "norm"));
@@ -1215,13 +1270,73 @@ int k_norm_affine(Device *dev, Arr *x, const uint32_t *p, Arr *gamma, Arr *beta,
   }
   const float *gp = affine ? (const float *)data_ptr(gamma) : nullptr;
   const float *bp = affine ? (const float *)data_ptr(beta) : nullptr;
-  int64_t shape[1] = {ncols * rows};
-  Arr *o;
-  SHLO_TRY(new_array(dev, kF32, shape, 1, &o));
   const size_t smem = (size_t)NORM_ROWS * (ncols + 1) * sizeof(float);
   const bool aligned = (((uintptr_t)data_ptr(x)) & 15) == 0 &&
                        (!affine || ((((uintptr_t)gp) | ((uintptr_t)bp)) & 15) == 0);
-  if (ncols * rows > 0 && p[3] == 0 && ncols % 128 == 0 && ncols <= 1024 && aligned) {
+  const bool warp_rows = ncols * rows > 0 && p[3] == 0 && ncols % 128 == 0 && ncols <= 1024 && aligned;
+  // y_pack: the packed x of a next product (K = ncols), written by
+  // g_norm_warp_pk, or by the pack kernel after the norm
+  if (y_pack && (ncols % 64 || 16 * (int64_t)y_pack[0] != ncols || y_pack[1] < rows || y_pack[1] % 64))
+    return fail("norm: a %lld x %lld result does not fit the packed layout (%d, %d)", (long long)rows,
+                (long long)ncols, y_pack[0], y_pack[1]);
+  if (y_pack && warp_rows) {
+    int64_t shape[1] = {ncols * (int64_t)y_pack[1]};
+    Arr *o;
+    SHLO_TRY(new_array(dev, kF32, shape, 1, &o));
+    o->shape[0] = ncols * rows;
+    const size_t tbytes = (size_t)8 * (2 * ncols + 4) * sizeof(float);
+    static bool attr_pk[64] = {false};
+    if (!attr_pk[dev->id]) {
+      int rc = 0;
+      rc |= cuda_check(cudaFuncSetAttribute(g_norm_warp_pk<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 260 * 4), "norm attribute");
+      rc |= cuda_check(cudaFuncSetAttribute(g_norm_warp_pk<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 516 * 4), "norm attribute");
+      rc |= cuda_check(cudaFuncSetAttribute(g_norm_warp_pk<3>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 772 * 4), "norm attribute");
+      rc |= cuda_check(cudaFuncSetAttribute(g_norm_warp_pk<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 1028 * 4), "norm attribute");
+      rc |= cuda_check(cudaFuncSetAttribute(g_norm_warp_pk<5>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 1284 * 4), "norm attribute");
+      rc |= cuda_check(cudaFuncSetAttribute(g_norm_warp_pk<6>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 1540 * 4), "norm attribute");
+      rc |= cuda_check(cudaFuncSetAttribute(g_norm_warp_pk<7>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 1796 * 4), "norm attribute");
+      rc |= cuda_check(cudaFuncSetAttribute(g_norm_warp_pk<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 2052 * 4), "norm attribute");
+      if (rc) {
+        shlo_release(o);
+        return 1;
+      }
+      attr_pk[dev->id] = true;
+    }
+    int64_t blocks = y_pack[1] / 8;
+    if (blocks > (int64_t)dev->sm_count * 8) blocks = (int64_t)dev->sm_count * 8;
+    const float *xp = (const float *)data_ptr(x);
+    float *yp = (float *)o->buf->ptr;
+    const int64_t rp = y_pack[1];
+    switch (ncols / 128) {
+      case 1: g_norm_warp_pk<1><<<(unsigned)blocks, 256, tbytes, dev->stream>>>(xp, yp, rows, rp, eps, gp, bp); break;
+      case 2: g_norm_warp_pk<2><<<(unsigned)blocks, 256, tbytes, dev->stream>>>(xp, yp, rows, rp, eps, gp, bp); break;
+      case 3: g_norm_warp_pk<3><<<(unsigned)blocks, 256, tbytes, dev->stream>>>(xp, yp, rows, rp, eps, gp, bp); break;
+      case 4: g_norm_warp_pk<4><<<(unsigned)blocks, 256, tbytes, dev->stream>>>(xp, yp, rows, rp, eps, gp, bp); break;
+      case 5: g_norm_warp_pk<5><<<(unsigned)blocks, 256, tbytes, dev->stream>>>(xp, yp, rows, rp, eps, gp, bp); break;
+      case 6: g_norm_warp_pk<6><<<(unsigned)blocks, 256, tbytes, dev->stream>>>(xp, yp, rows, rp, eps, gp, bp); break;
+      case 7: g_norm_warp_pk<7><<<(unsigned)blocks, 256, tbytes, dev->stream>>>(xp, yp, rows, rp, eps, gp, bp); break;
+      default: g_norm_warp_pk<8><<<(unsigned)blocks, 256, tbytes, dev->stream>>>(xp, yp, rows, rp, eps, gp, bp); break;
+    }
+    if (launch_check("norm")) {
+      shlo_release(o);
+      return 1;
+    }
+    *out = o;
+    return 0;
+  }
+  if (y_pack) {
+    Arr *n, *q;
+    SHLO_TRY(k_norm_affine_packed(dev, x, p, gamma, beta, nullptr, &n));
+    const int rc = k_pack_x(dev, n, rows, ncols, y_pack, &q);
+    shlo_release(n);
+    SHLO_TRY(rc);
+    *out = q;
+    return 0;
+  }
+  int64_t shape[1] = {ncols * rows};
+  Arr *o;
+  SHLO_TRY(new_array(dev, kF32, shape, 1, &o));
+  if (warp_rows) {
     // one warp a row, the row in registers
     int64_t blocks = (rows + 3) / 4;
     if (blocks > (int64_t)dev->sm_count * 32) blocks = (int64_t)dev->sm_count * 32;

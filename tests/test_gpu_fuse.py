@@ -147,6 +147,10 @@ def test_modules_fused_equal_unfused(cfg, B, capfd, monkeypatch):
     # positions (128 or 256: not the encoder's 196); two timestep dense chains
     per_layer = 6 + (1 if cfg.seq in (128, 256) else 0)
     assert chains == per_layer * cfg.layers + (2 if cfg.timestep else 0), err
+    # packed handoffs a layer: norm -> QKV, norm -> FFN1, FFN1 -> FFN2, and
+    # attention -> output projection where the attention is fused
+    m = re.search(r"handing a packed operand on: (\d+)", err)
+    assert m and int(m.group(1)) == (3 + (1 if cfg.seq in (128, 256) else 0)) * cfg.layers, err
     assert np.array_equal(bits(got), bits(want))
     again = M.to_numpy(E.call(fn, X + W)[0])  # the replay
     assert np.array_equal(bits(again), bits(want))
@@ -323,3 +327,89 @@ def test_attention_matches_unfused(B, S, H, scale, special, amp, capfd, monkeypa
         # with one head, where the value product already is the [B, S, H*64] layout
         assert chains == (1 if merged or H == 1 else 0), err
         assert np.array_equal(bits(got), bits(want))
+
+
+def then_dense(text, R, K, M2, last, last_ty):
+    """A module returning `last` ([..., K] of type last_ty) made to return
+    dense(last) = last [R, K] @ w [M2, K]^T + b [M2] instead (new arguments %w, %b)."""
+    T = lambda *d: "tensor<" + "".join("%dx" % x for x in d) + "f32>"
+    dn = ('{dot_dimension_numbers = #stablehlo.dot<lhs_contracting_dimensions = [1], '
+          'rhs_contracting_dimensions = [1]>}')
+    head, _, _ = text.partition("    func.return %s : %s\n" % (last, last_ty))
+    head = head.replace(") -> (%s) {" % last_ty, ", %%w: %s, %%b: %s) -> (%s) {" % (T(M2, K), T(M2), T(R, M2)), 1)
+    head = head.replace(") -> %s {" % last_ty, ", %%w: %s, %%b: %s) -> %s {" % (T(M2, K), T(M2), T(R, M2)), 1)
+    return head + f"""    %rr = "stablehlo.reshape"({last}) : ({last_ty}) -> {T(R, K)}
+    %y9 = "stablehlo.dot_general"(%rr, %w) {dn} : ({T(R, K)}, {T(M2, K)}) -> {T(R, M2)}
+    %c9 = "stablehlo.broadcast_in_dim"(%b) {{broadcast_dimensions = array<i64: 1>}} : ({T(M2)}) -> {T(R, M2)}
+    %z9 = "stablehlo.add"(%y9, %c9) : ({T(R, M2)}, {T(R, M2)}) -> {T(R, M2)}
+    func.return %z9 : {T(R, M2)}
+  }}
+}}
+"""
+
+
+def norm_text(R, C):
+    """x [R, C] -> ggml.norm -> * gain -> + bias, the layer norm as the encoder writes it."""
+    T = lambda *d: "tensor<" + "".join("%dx" % x for x in d) + "f32>"
+    return f"""module {{
+  func.func public @main(%x: {T(R, C)}, %g: {T(C)}, %be: {T(C)}) -> {T(R, C)} {{
+    %n = "stablehlo.custom_call"(%x) {{call_target_name = "ggml.norm", backend_config = "eps = 0x{D.EPS_BITS:08X} : f32"}} : ({T(R, C)}) -> {T(R, C)}
+    %gg = "stablehlo.broadcast_in_dim"(%g) {{broadcast_dimensions = array<i64: 1>}} : ({T(C)}) -> {T(R, C)}
+    %t = "stablehlo.multiply"(%n, %gg) : ({T(R, C)}, {T(R, C)}) -> {T(R, C)}
+    %bb = "stablehlo.broadcast_in_dim"(%be) {{broadcast_dimensions = array<i64: 1>}} : ({T(C)}) -> {T(R, C)}
+    %a = "stablehlo.add"(%t, %bb) : ({T(R, C)}, {T(R, C)}) -> {T(R, C)}
+    func.return %a : {T(R, C)}
+  }}
+}}
+"""
+
+
+@pytest.mark.parametrize("R,C,M2,linked", [
+    (1100, 512, 1536, True),   # the packed norm (a partial last 32-row tile, padded rows); k_mul_mat_seg consumer
+    (4000, 512, 1536, True),   # k_mul_mat_tm consumer
+    (300, 1024, 512, True),    # eight float4 groups a lane
+    (1100, 576, 512, True),    # a row not a multiple of 128: the block norm, then the pack kernel
+    (1100, 1000, 512, False),  # K not a multiple of 64: no handoff
+])
+def test_norm_packed_handoff_matches_unfused(R, C, M2, linked, capfd, monkeypatch):
+    """The layer norm (norm, gain, bias) writing its result in the next dense
+    product's packed x layout, against the ops one at a time."""
+    rng = np.random.default_rng(R + C + M2)
+    args = [specials(rng, (R, C)), specials(rng, (C,)), specials(rng, (C,)),
+            specials(rng, (M2, C)) * np.float32(0.05), specials(rng, (M2,))]
+    args = [M.of_numpy(a) for a in args]
+    T = lambda *d: "tensor<" + "".join("%dx" % x for x in d) + "f32>"
+    l = E.load(then_dense(norm_text(R, C), R, C, M2, "%a", T(R, C)))
+    want = M.to_numpy(E.call(E.prepare(l, None, False), args)[0])
+    fn = E.prepare(l, None, True)
+    got, chains, err = run_counted(capfd, monkeypatch, fn, args)
+    assert chains == 2, err
+    assert ("handing a packed operand on: 1" in err) == linked, err
+    assert np.array_equal(bits(got), bits(want))
+    assert np.array_equal(bits(M.to_numpy(E.call(fn, args)[0])), bits(want))
+
+
+@pytest.mark.parametrize("B,S,H,M2", [
+    (2, 256, 8, 512),    # the packed epilogue; k_mul_mat_seg consumer
+    (8, 256, 8, 1536),   # k_mul_mat_tm consumer
+    (3, 256, 2, 384),    # two heads: K = 128
+    (1, 256, 1, 256),    # one head: the chain ends at the value product
+    (2, 128, 4, 512),    # 128 positions: the pack kernel after the attention
+])
+def test_attention_packed_handoff_matches_unfused(B, S, H, M2, capfd, monkeypatch):
+    """The fused attention writing the merged heads in the output projection's
+    packed x layout, against the ops one at a time."""
+    rng = np.random.default_rng(B * 7 + S + H + M2)
+    K = H * 64
+    args = [rng.standard_normal((B, S, 3, H, 64)).astype(np.float32), specials(rng, (M2, K)) * np.float32(0.05),
+            specials(rng, (M2,))]
+    args = [M.of_numpy(a) for a in args]
+    T = lambda *d: "tensor<" + "".join("%dx" % x for x in d) + "f32>"
+    l = E.load(then_dense(attn_text(B, S, H, 64, 0x3E000000, True), B * S, K, M2, "%r", T(B, S, K)))
+    want = M.to_numpy(E.call(E.prepare(l, None, False), args)[0])
+    fn = E.prepare(l, None, True)
+    got, chains, err = run_counted(capfd, monkeypatch, fn, args)
+    assert chains == 2, err
+    assert "handing a packed operand on: 1" in err, err
+    assert np.array_equal(bits(got), bits(want))
+    assert np.array_equal(bits(M.to_numpy(E.call(fn, args)[0])), bits(want))
