@@ -79,9 +79,9 @@ struct Group {
   int flags = 0;         // dense: the epilogue flags
   int direct = 0;        // attention: q (1), k (2), v (4) read directly, without a copy
   uint32_t p[8] = {0};   // the fused kernel's parameter words
-  // dense chains linked through a packed operand: y_pack (this chain's result
-  // is the next chain's x, written in its packed layout) and x_np (this
-  // chain's x is the previous chain's result, already packed; src is that chain)
+  // chains linked through a packed operand: y_pack (this chain's result is the
+  // next dense chain's x, written in its packed layout) and x_np (this dense
+  // chain's x is an earlier chain's result, already packed; src is that chain)
   int y_pack[2] = {0, 0};
   int x_np = 0, src = -1;
   uint64_t produced = 0;  // the capture call: the serial of the fused result's storage
@@ -415,7 +415,7 @@ struct Tracer {
     // attention block (-> the output projection), the layer norm (-> QKV, FFN1).
     for (int a = 0; a < (int)groups.size(); a++) {
       Group &g1 = groups[a];
-      int64_t M1, R1;  // the result's rows and row width
+      int64_t M1, R1;  // the result's row width and rows
       if (g1.kind == G_DENSE && (g1.flags & EP_GELU)) {
         M1 = g1.p[1];
         R1 = g1.p[2];
@@ -662,7 +662,7 @@ int tracer_plan(Tracer *t, Arr *const *outs, int n) {
   if (v && atoi(v) >= 1) {
     int links = 0;
     for (const Group &g : t->groups) links += g.y_pack[1] != 0;
-    if (links) fprintf(stderr, "shlo: dense chains handing a packed operand on: %d\n", links);
+    if (links) fprintf(stderr, "shlo: fused chains handing a packed operand on: %d\n", links);
   }
   t->mode = 2;
   t->next = 0;
